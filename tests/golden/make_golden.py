@@ -1,0 +1,147 @@
+#!/usr/bin/env python3
+"""Generate the committed golden vectors that pin the CPU oracle to the reference.
+
+Run in a container where the reference tree is present (it is NOT needed at test time):
+    python tests/golden/make_golden.py --ref /root/reference
+Writes tests/golden/golden.npz. Every output is produced by the reference's own code where it is Python, and by the
+exact formulas the reference's tests compute where the reference is CUDA:
+
+  quant      vllm_turing.quantfuse.quant_torch, imported from the reference tree (quantfuse.py:18-24)
+  gemm       float64 matmul of the int8 operands, "exact for int8 sums" (tests/test_w8a8_mma.py:42-45)
+  dequant    (float)acc * sa * sw rounded to the 16-bit type, in the order of vllm_turing/csrc/w8a8_gemv.cu:91
+  allreduce  (x0.float() + x1.float()).half() (tests/bench_devll.py:28-36), rank order for more ranks
+  norm+quant h = x + r; h.float() * rsqrt(mean(h^2) + eps) * w; quant_torch  (tests/test_quantfuse.py:45-48)
+  config 0   the whole chain at BASELINE config 0 (M=16, K_local=8704, N=5120, 2 ranks, seed 0): digests of the
+             exact parts plus the int8 / scales arrays
+Inputs come from seeded torch CPU generators (vllm_turing_b200.synthetic for config 0) and are stored (small cases)
+or regenerated from the seed (config 0).
+"""
+import argparse
+import hashlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+
+
+def bits(t):
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
+
+
+def sha(x):
+    return hashlib.sha256(np.ascontiguousarray(x).tobytes()).hexdigest()
+
+
+# int8 GEMM cases: the operands are regenerated from a per-case seed (tests/test_oracle.py uses the same function and
+# checks the input digests first), as in tests/test_w8a8_mma.py:84-88 (randint int8, rand * 1e-2 / 1e-3 scales)
+MM_CASES = ((1, 64, 64), (5, 136, 5136), (16, 256, 1024), (24, 40, 256), (32, 300, 5168))
+
+
+def mm_case_inputs(M, N, K):
+    g = torch.Generator().manual_seed(M * 1000003 + N * 1009 + K)
+    a = torch.randint(-128, 128, (M, K), generator=g, dtype=torch.int8)
+    w = torch.randint(-128, 128, (N, K), generator=g, dtype=torch.int8)
+    sa = torch.rand(M, generator=g) * 1e-2
+    sw = torch.rand(N, generator=g) * 1e-3
+    return a, w, sa, sw
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
+    args = ap.parse_args()
+    sys.path.insert(0, args.ref)
+    from vllm_turing.quantfuse import quant_torch  # the reference's own quantiser
+    sys.path.insert(0, REPO)
+    from vllm_turing_b200.synthetic import make_layer_inputs
+
+    g = torch.Generator().manual_seed(20240601)
+    out = {}
+
+    # ---- quant: the reference's quant_torch on bf16 and fp16 rows ------------------------------------------------
+    for dt, code in ((torch.bfloat16, 1), (torch.float16, 0)):
+        for M, N in ((1, 64), (5, 5120), (30, 136)):
+            x = (torch.randn(M, N, generator=g) * 3).to(dt)
+            if M > 1:
+                x[1, 7] = 200.0                      # an outlier channel
+            if M == 30:
+                x[0] = 0.0                           # an all-zero row (tests/test_silu_quant.py:30 covers the same)
+            q, s = quant_torch(x)
+            key = f"quant_{code}_{M}x{N}"
+            out[key + "_x"] = bits(x)
+            out[key + "_q"] = q.numpy()
+            out[key + "_s"] = s.reshape(-1).numpy()
+
+    # ---- gemm + dequant -------------------------------------------------------------------------------------------
+    for M, N, K in MM_CASES:
+        a, w, sa, sw = mm_case_inputs(M, N, K)
+        acc = (a.double() @ w.double().t())                 # exact (tests/test_w8a8_mma.py:42-43)
+        acc32 = acc.to(torch.int32)
+        for dt, code in ((torch.bfloat16, 1), (torch.float16, 0)):
+            deq = ((acc32.float() * sa.view(-1, 1)) * sw.view(1, -1)).to(dt)   # w8a8_gemv.cu:91 order
+            out[f"mm_{M}x{N}x{K}_out{code}"] = bits(deq)
+        key = f"mm_{M}x{N}x{K}"
+        out[key + "_acc"] = acc32.numpy()
+        out[key + "_in_sha"] = np.array(sha(a.numpy()) + sha(w.numpy()) + sha(sa.numpy()) + sha(sw.numpy()))
+
+    # ---- all-reduce -------------------------------------------------------------------------------------------------
+    for nr in (2, 4, 8):
+        parts = [(torch.randn(5 * 64, generator=g) * 4).to(torch.bfloat16) for _ in range(nr)]
+        s = parts[0].float()
+        for p in parts[1:]:
+            s = s + p.float()
+        out[f"ar_{nr}_parts"] = np.stack([bits(p) for p in parts])
+        out[f"ar_{nr}_out"] = bits(s.to(torch.bfloat16))
+
+    # ---- residual add + RMSNorm + quant -----------------------------------------------------------------------------
+    for M, N in ((1, 512), (5, 5120), (24, 1024)):
+        x = (torch.randn(M, N, generator=g) * 3).to(torch.bfloat16)
+        r = torch.randn(M, N, generator=g).to(torch.bfloat16)
+        w = (1.0 + torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+        h = x + r                                             # in bf16, as tests/test_quantfuse.py:46
+        v = h.float().pow(2).mean(-1, keepdim=True)
+        y = (h.float() * torch.rsqrt(v + 1e-6) * w.float()).to(torch.bfloat16)
+        q, s = quant_torch(y)
+        key = f"norm_{M}x{N}"
+        out[key + "_x"], out[key + "_r"], out[key + "_w"] = bits(x), bits(r), bits(w)
+        out[key + "_h"], out[key + "_y"] = bits(h), bits(y)
+        out[key + "_q"], out[key + "_s"] = q.numpy(), s.reshape(-1).numpy()
+
+    # ---- M=16, K_local=8704, N=5120, 2 ranks, seed 0 ---------------------------------------------
+    M, N, K = 16, 5120, 8704
+    parts = []
+    for rank in range(2):
+        li = make_layer_inputs(M, N, K, seed=0, rank=rank)
+        # the activation quantiser must agree with the reference's own quant_torch on these inputs
+        gx = torch.Generator().manual_seed(0 * 1000 + rank)
+        x = torch.randn(M, K, generator=gx).to(torch.bfloat16)
+        qr, sr = quant_torch(x)
+        assert torch.equal(qr, li.a) and torch.equal(sr.reshape(-1), li.sa), "synthetic quantiser != quant_torch"
+        acc = (li.a.double() @ li.w.double().t()).to(torch.int32)
+        part = ((acc.float() * li.sa.view(-1, 1)) * li.sw.view(1, -1)).to(torch.bfloat16)
+        out[f"cfg0_r{rank}_acc_sha"] = np.array(sha(acc.numpy()))
+        out[f"cfg0_r{rank}_part_sha"] = np.array(sha(bits(part)))
+        out[f"cfg0_r{rank}_acc_head"] = acc[:2, :16].numpy()
+        parts.append(part)
+        res0, nw = li.residual, li.norm_w
+    red = (parts[0].float() + parts[1].float()).to(torch.bfloat16)
+    h = red + res0
+    v = h.float().pow(2).mean(-1, keepdim=True)
+    y = (h.float() * torch.rsqrt(v + 1e-6) * nw.float()).to(torch.bfloat16)
+    q, s = quant_torch(y)
+    out["cfg0_reduced_sha"] = np.array(sha(bits(red)))
+    out["cfg0_residual_sha"] = np.array(sha(bits(h)))
+    out["cfg0_q"] = q.numpy()
+    out["cfg0_s"] = s.reshape(-1).numpy()
+
+    np.savez_compressed(args.out, **out)
+    print(f"wrote {args.out}: {len(out)} arrays, {os.path.getsize(args.out) / 1024:.0f} KiB")
+
+
+if __name__ == "__main__":
+    main()

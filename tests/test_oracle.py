@@ -1,0 +1,126 @@
+"""The CPU oracle pinned against the golden vectors made by the reference's own code and its tests' formulas
+(tests/golden/make_golden.py). CPU only."""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests.golden.make_golden import MM_CASES, mm_case_inputs
+
+
+def sha(x):
+    return hashlib.sha256(np.ascontiguousarray(x).tobytes()).hexdigest()
+
+
+@pytest.mark.parametrize("code", [1, 0])
+@pytest.mark.parametrize("shape", [(1, 64), (5, 5120), (30, 136)])
+def test_quant_matches_reference_quant_torch(golden, code, shape):
+    key = f"quant_{code}_{shape[0]}x{shape[1]}"
+    q, s = O.quant_rows(golden[key + "_x"], code)
+    assert np.array_equal(s, golden[key + "_s"])           # vllm_turing/quantfuse.py:18-24, bit-exact
+    assert np.array_equal(q, golden[key + "_q"])
+
+
+@pytest.mark.parametrize("case", MM_CASES)
+def test_gemm_and_dequant(golden, case):
+    M, N, K = case
+    a, w, sa, sw = mm_case_inputs(M, N, K)
+    key = f"mm_{M}x{N}x{K}"
+    assert str(golden[key + "_in_sha"]) == sha(a.numpy()) + sha(w.numpy()) + sha(sa.numpy()) + sha(sw.numpy())
+    acc = O.gemm_s32(a.numpy(), w.numpy())
+    assert np.array_equal(acc, golden[key + "_acc"])         # exact int32
+    for code in (1, 0):
+        out = O.dequant(acc, sa.numpy(), sw.numpy(), None, code)
+        assert np.array_equal(out, golden[f"{key}_out{code}"])
+        out2 = O.scaled_mm(a.numpy(), w.numpy(), sa.numpy(), sw.numpy(), None, code)
+        assert np.array_equal(out2, out)
+
+
+def test_dequant_bias_and_per_tensor_scale():
+    """bias and per-tensor scales (tests/test_w8a8_mma.py:111-112) against a float64 restatement."""
+    g = torch.Generator().manual_seed(5)
+    a = torch.randint(-128, 128, (3, 96), generator=g, dtype=torch.int8)
+    w = torch.randint(-128, 128, (40, 96), generator=g, dtype=torch.int8)
+    sa = torch.rand(1, generator=g) * 1e-2
+    sw = torch.rand(40, generator=g) * 1e-3
+    bias = torch.randn(40, generator=g).to(torch.bfloat16)
+    out = O.scaled_mm(a.numpy(), w.numpy(), sa.numpy(), sw.numpy(), O.to_bits(bias), 1)
+    ref = (a.double() @ w.double().t()) * sa.double() * sw.double().view(1, -1) + bias.double()
+    got = O.from_bits(out, torch.bfloat16).double()
+    assert ((got - ref).abs() / (ref.abs() + 1e-3)).max().item() < 2e-2     # tests/test_w8a8_mma.py:97-99
+
+
+@pytest.mark.parametrize("nr", [2, 4, 8])
+def test_all_reduce(golden, nr):
+    parts = list(golden[f"ar_{nr}_parts"])
+    assert np.array_equal(O.all_reduce(parts, 1), golden[f"ar_{nr}_out"])
+
+
+@pytest.mark.parametrize("shape", [(1, 512), (5, 5120), (24, 1024)])
+def test_add_rms_norm_quant(golden, shape):
+    key = f"norm_{shape[0]}x{shape[1]}"
+    res, q, s, y = O.add_rms_norm_quant(golden[key + "_x"], golden[key + "_r"], golden[key + "_w"], 1e-6, 1,
+                                        want_normed=True)
+    assert np.array_equal(res, golden[key + "_h"])            # bf16 residual add, exact
+    yf = O.bits_to_float(y, 1)
+    yr = O.bits_to_float(golden[key + "_y"], 1)
+    assert np.max(np.abs(yf - yr) / (np.abs(yr) + 1e-3)) < 1e-2   # mean-of-squares order differs in the last bit
+    assert np.max(np.abs(s - golden[key + "_s"]) / golden[key + "_s"]) < 1e-2
+    assert np.abs(q.astype(np.int32) - golden[key + "_q"].astype(np.int32)).max() <= 1
+
+
+def test_config0_chain(golden):
+    """BASELINE config 0 (M=16, K_local=8704, N=5120, 2 ranks, seed 0): every exact stage bit-exact, the requantised
+    activations within one LSB."""
+    from vllm_turing_b200.synthetic import make_layer_inputs
+    M, N, K = 16, 5120, 8704
+    lis = [make_layer_inputs(M, N, K, seed=0, rank=r) for r in range(2)]
+    parts = []
+    for r, li in enumerate(lis):
+        acc = O.gemm_s32(li.a.numpy(), li.w.numpy())
+        assert sha(acc) == str(golden[f"cfg0_r{r}_acc_sha"])
+        part = O.dequant(acc, li.sa.numpy(), li.sw.numpy(), None, 1)
+        assert sha(part) == str(golden[f"cfg0_r{r}_part_sha"])
+        parts.append(part)
+    red = O.all_reduce(parts, 1)
+    assert sha(red) == str(golden["cfg0_reduced_sha"])
+    res, q, s, _ = O.add_rms_norm_quant(red, O.to_bits(lis[0].residual), O.to_bits(lis[0].norm_w), 1e-6, 1)
+    assert sha(res) == str(golden["cfg0_residual_sha"])
+    assert np.abs(q.astype(np.int32) - golden["cfg0_q"].astype(np.int32)).max() <= 1
+    assert np.max(np.abs(s - golden["cfg0_s"]) / golden["cfg0_s"]) < 1e-3
+    # the one-call chain gives the same
+    res2, q2, s2, red2 = O.row_linear_tp([li.a.numpy() for li in lis], [li.w.numpy() for li in lis],
+                                         [li.sa.numpy() for li in lis], [li.sw.numpy() for li in lis],
+                                         O.to_bits(lis[0].residual), O.to_bits(lis[0].norm_w), 1e-6, 1)
+    assert np.array_equal(red2, red) and np.array_equal(res2, res) and np.array_equal(q2, q)
+
+
+def test_weight_quant_formula():
+    """scripts/w8a8_convert.py:165-166 restated, against the synthetic generator's torch version of it."""
+    from vllm_turing_b200.synthetic import quant_per_channel
+    w = torch.randn(33, 200, generator=torch.Generator().manual_seed(3)) * 0.02
+    w[4] = 0.0
+    q, s = O.weight_quant(w.numpy())
+    qt, st = quant_per_channel(w)
+    assert np.array_equal(q, qt.numpy()) and np.array_equal(s, st.numpy())
+
+
+def test_silu_mul_quant_zero_row():
+    """silu_quant.cu semantics incl. an all-zero activation row (tests/test_silu_quant.py:30)."""
+    g = torch.Generator().manual_seed(9)
+    M, I = 4, 136
+    gu = (torch.randn(M, 2 * I, generator=g) * 3).half()
+    gu[0, :I] = 0
+    q, s = O.silu_mul_quant(O.to_bits(gu), 0)
+    assert s[0] == 0.0 and not q[0].any()
+    act = (torch.nn.functional.silu(gu[:, :I].float()).half() * gu[:, I:]).float()
+    am = act.abs().amax(-1)
+    assert np.allclose(s[1:], (am / 127.0).numpy()[1:], rtol=1e-6)
+
+
+def test_all_gather():
+    ps = [np.full(37, r + 1, np.uint8) for r in range(4)]
+    g = O.all_gather(ps)
+    assert g.size == 4 * 37 and all((g[r * 37:(r + 1) * 37] == r + 1).all() for r in range(4))
