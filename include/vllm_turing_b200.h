@@ -1,0 +1,121 @@
+/*
+ * vllm_turing_b200.h -- C ABI of libvllm_turing_b200.so, the B200 (sm_100a) tensor-parallel W8A8 linear hot path.
+ *
+ * Plain pointers and sizes only (no torch types), loaded with ctypes by the Python package exactly as the reference
+ * loads its csrc/ libraries (vllm_turing/_build.py:33-55). Every entry returns 0 on success, a negative VT_E* code on
+ * rejected arguments, or a positive cudaError_t of the launch, unless stated otherwise. Every launch goes on `stream`
+ * (a cudaStream_t; NULL = legacy default stream). Pointers are device pointers unless stated otherwise.
+ *
+ * dtype: 0 = float16, 1 = bfloat16 (the reference's code, vllm_turing/csrc/w8a8_gemv.cu:346).
+ * Matrices are row-major: activations a [M, K] int8, weights w [N, K] int8 (vLLM hands the GEMM the transposed [K, N]
+ * view of this tensor, stride (1, K); vllm_turing/csrc/w8a8_gemv.cu:5), outputs [M, N].
+ */
+#ifndef VLLM_TURING_B200_H
+#define VLLM_TURING_B200_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VT_EARG (-1)     /* unsupported shape, alignment or argument */
+#define VT_ECAPTURE (-2) /* a library workspace would have to grow while the stream is capturing */
+#define VT_ENOMEM (-3)   /* workspace allocation failed */
+
+/* ---- W8A8 GEMM: out = (a . w^T) * sa[m] * sw[n] (+ bias[n]), int32 accumulation -------------------------------- */
+
+/* Decode GEMV, M 1..16, K % 16 == 0, a / w 16-byte aligned; sa_rows / sw_rows = 0 for per-tensor scales.
+ * Replaces vllm_turing/csrc/w8a8_gemv.cu:347-361 (same signature and return convention). */
+int w8a8_gemv(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out, int M, int N,
+              int K, int sa_rows, int sw_rows, int dtype, void *stream);
+
+/* w8a8_gemv with a caller-owned workspace of w8a8_gemv_ws_bytes(M, N) bytes, zeroed before first use (kernels leave
+ * it zeroed; calls sharing it must be stream-ordered). No counterpart in the reference (its GEMV needs no scratch). */
+size_t w8a8_gemv_ws_bytes(int M, int N);
+int w8a8_gemv_ws(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out, int M,
+                 int N, int K, int sa_rows, int sw_rows, int dtype, void *workspace, size_t ws_bytes, void *stream);
+
+/* int32 accumulators acc[M, N] = a . w^T (bit-exact parity checks), M 1..16. New entry. */
+int vt_gemv_s32(const void *a, const void *w, void *acc, int M, int N, int K, void *stream);
+
+/* Status word of the library workspace of the current device: 0, or the first device-side timeout code
+ * (0x01xxxxxx pipeline, 0x02xxxxxx peer, 0x03xxxxxx cooperating CTA). Synchronises the device. */
+unsigned vt_status(int clear);
+
+/* ---- row-wise epilogues --------------------------------------------------------------------------------------- */
+
+/* Per-token dynamic symmetric int8 quantisation x [M, N] -> q [M, N], scales [M] (float32).
+ * Replaces vLLM's scaled_int8_quant as the reference patches it (vllm_turing/quantfuse.py:18-39). */
+int vt_scaled_int8_quant(const void *x, void *q, void *scales, int M, int N, int dtype, void *stream);
+
+/* residual := x + residual; q, scales := quant(RMSNorm(residual) * weight); normed (optional) := RMSNorm(...) * w.
+ * Replaces vLLM's rms_norm_dynamic_per_token_quant(h, w1, eps, int8, None, res) as called at
+ * vllm_turing/tailoverlap.py:200-201. N % 4 == 0, N <= 49152. */
+int vt_rms_norm_quant(const void *x, void *residual, const void *weight, float eps, void *q, void *scales,
+                      void *normed, int M, int N, int dtype, void *stream);
+
+/* SiLU(gate) * up + per-token int8 quantisation, gate_up (M, 2I) fp16 -> q (M, I), scales (M).
+ * Replaces vllm_turing/csrc/silu_quant.cu:71-77 (same signature; returns 1 bad args, 2 launch error). */
+int silu_mul_quant(const void *gu, void *q, void *scales, int M, int I, void *stream);
+/* The same for fp16 (dtype 0) or bf16 (dtype 1). New entry. */
+int vt_silu_mul_quant(const void *gu, void *q, void *scales, int M, int I, int dtype, void *stream);
+
+/* ---- IPC helpers (replace vllm_turing/csrc/ce_ar.cu:77-101, same names and semantics) ------------------------ */
+
+/* A zeroed device buffer of `bytes` and its 64-byte CUDA IPC handle (written to host memory `handle64`).
+ * 0 ok; 1 cudaMalloc, 2 memset, 3 sync, 4 handle failed. (ce_ar.cu:79-86) */
+int ce_alloc(size_t bytes, void **ptr, void *handle64);
+/* Maps a peer's buffer from its 64-byte handle. 0 ok, 1 failed. (ce_ar.cu:88-92) */
+int ce_open(const void *handle64, void **ptr);
+/* Unmaps a buffer opened with ce_open / frees one from ce_alloc. 0 ok, 1 failed. New entries. */
+int ce_close(void *ptr);
+int ce_free(void *ptr);
+/* Single-process use: peer access from the current device to `peer`. 0 ok, 1 failed. (ce_ar.cu:95-99) */
+int ce_enable_peer(int peer);
+
+/* ---- tensor-parallel communicator (N = 1..8 ranks, one process per GPU, NVLink P2P) ---------------------------
+ * Replaces the reference's two-rank transports (DevLLAllReduce over har_all_reduce, vllm_turing/hostar.py:152-188 /
+ * host_ar.cu:114-131; CeAllReduce over ce_all_reduce, cear.py:52-87 / ce_ar.cu:103-146; DmaAllGather over
+ * dag_all_gather, dmaag.py:107-119 / dma_ag.cu:45-74). All ranks must make the same calls in the same order; calls
+ * on one communicator must be stream-ordered on each rank. Call counting is device-resident (CUDA-graph safe). */
+
+/* Bytes of the per-rank region: ll_data = largest one-shot / fused message (bytes), big_data = largest two-shot
+ * message per launch (bytes; larger ones run in pieces), scratch_ints = int32 scratch of the fused GEMV (>= M*N). */
+size_t vt_comm_region_bytes(int world, size_t ll_data, size_t big_data, size_t scratch_ints);
+/* bases[world]: each rank's region (own from ce_alloc, peers' from ce_open), same sizes. NULL on bad arguments. */
+void *vt_comm_create(int rank, int world, void *const *bases, size_t ll_data, size_t big_data, size_t scratch_ints);
+int vt_comm_destroy(void *comm);
+long long vt_comm_ll_bytes(void *comm);
+long long vt_comm_big_bytes(void *comm);
+/* 0 or the first timeout code a collective reported on this rank; synchronises the device. */
+unsigned vt_comm_status(void *comm, int clear);
+/* Number of completed calls on this communicator (device counter); synchronises the device. */
+unsigned vt_comm_seq(void *comm);
+
+/* out[n] = sum over ranks of in[n], float32 accumulation in rank order, one rounding (the arithmetic of
+ * host_ar.cu:90-101). algo 0 auto, 1 one-shot LL (n % 4 == 0, up to ll_data), 2 two-shot (n % 8 == 0).
+ * in may equal out; 16-byte aligned. Replaces har_all_reduce (host_ar.cu:114-131) and ce_all_reduce
+ * (ce_ar.cu:103-146) for any rank count. */
+int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype, int algo, void *stream);
+
+/* gathered [world * m bytes] with this rank's payload pre-written at [rank * m, (rank + 1) * m); fills the peers'
+ * slots. m % 8 == 0 (LL) or m % 16 == 0 (bulk). Replaces dag_all_gather (dma_ag.cu:45-74) for N ranks over P2P. */
+int vt_all_gather(void *comm, void *gathered, long long m, void *stream);
+
+/* The fused row-parallel layer tail, one kernel: this rank's W8A8 GEMV partial -> all-reduce over the communicator
+ * -> residual add (in place) -> RMSNorm * norm_w -> per-token int8 q / scales. residual = NULL: plain row-linear +
+ * all-reduce into `reduced`. 1 <= M <= 16, N % 4 == 0, K % 16 == 0, M * N * 2 <= ll_data. Replaces the reference's
+ * decode tail: scaled_mm_ (w8a8.py:235-244) -> tensor_model_parallel_all_reduce (hostar.py:260-278) ->
+ * rms_norm_dynamic_per_token_quant (tailoverlap.py:200). */
+int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,
+                     const void *norm_w, float eps, void *q, void *scales, void *reduced, int M, int N, int K,
+                     int dtype, void *stream);
+/* Loads the fused kernels now (a lazily loaded module may synchronise behind a kernel spinning on a peer). */
+int vt_tp_preload(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VLLM_TURING_B200_H */

@@ -1,0 +1,390 @@
+// Tensor-parallel collectives over NVLink 5 / NVSwitch peer memory for B200 (sm_100a), N = 1..8 ranks, one process
+// per GPU. No NCCL on the path: kernels load and store peers' IPC-mapped regions directly.
+//
+//   one-shot (decode messages): every rank pushes its message as 16-byte LL words {4 data bytes, seq, 4 data bytes,
+//     seq} into every rank's receive slot, then polls its own slot and sums the ranks in rank order (float32, one
+//     rounding). The reference's two-rank LL kernel (vllm_turing/csrc/host_ar.cu:31-82) generalised to N ranks with
+//     16-byte stores and bounded waits.
+//   two-shot (prefill messages): reduce-scatter by chunk ownership (rank c owns chunk c; peers push their slice of it
+//     into c's receive buffers, then a release flag), the owner sums in rank order and publishes the reduced chunk,
+//     every rank pulls the other chunks (all-gather). The N-rank SM version of the reference's copy-engine all-reduce
+//     (vllm_turing/csrc/ce_ar.cu:103-146: push half, flag, wait, add, push, flag, wait).
+//   all-gather: each rank's slot of `gathered` is pre-written by the caller and the kernel fills the peers' slots
+//     (the ABI idea of vllm_turing/csrc/dma_ag.cu:41-47, over P2P for N ranks instead of host staging for two).
+//
+// Exports (include/vllm_turing_b200.h): ce_alloc, ce_open, ce_close, ce_free, ce_enable_peer (the reference's IPC
+// helpers, vllm_turing/csrc/ce_ar.cu:75-101), vt_comm_* (communicator objects), vt_all_reduce, vt_all_gather.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "comm.cuh"
+#include "common.cuh"
+#include "host_util.h"
+
+namespace vt {
+
+constexpr int AR_THREADS = 512;
+
+// ---- one-shot LL all-reduce -------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(AR_THREADS) ar_oneshot_kernel(CommView c, const uint2 *in, uint2 *out,
+                                                                long long nwords,
+                                                                uint64_t timeout) {
+    __shared__ unsigned s_seq;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t deadline = globaltimer() + timeout;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    for (long long i = i0; i < nwords; i += stride) {
+        const uint2 d = in[i];
+        for (int k = 0; k < c.world; ++k) {
+            const int dst = (c.rank + k) % c.world;   // staggered: ranks do not all hit the same peer first
+            ll_store(c.ll_slot(dst, p, c.rank) + i * 16, d.x, d.y, seq);
+        }
+    }
+    bool dead = false;
+    for (long long i = i0; i < nwords; i += stride) {
+        float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+        for (int r = 0; r < c.world; ++r) {
+            uint2 d = make_uint2(0u, 0u);
+            if (!dead && !ll_wait(c.ll_slot(c.rank, p, r) + i * 16, seq, deadline, d)) {
+                report(c.status(), ST_PEER_TIMEOUT | (unsigned)r);
+                dead = true;
+            }
+            const float2 a = unpack2<T>(d.x), b = unpack2<T>(d.y);
+            if (r == 0) {
+                s0 = a.x; s1 = a.y; s2 = b.x; s3 = b.y;
+            } else {
+                s0 += a.x; s1 += a.y; s2 += b.x; s3 += b.y;
+            }
+        }
+        out[i] = make_uint2(pack2<T>(s0, s1), pack2<T>(s2, s3));
+    }
+    comm_end(c, seq);
+}
+
+// ---- two-shot all-reduce (reduce-scatter + all-gather) -------------------------------------------------------------
+// n elements in 16-byte units (8 elements); chunk k = units [k U / N, (k + 1) U / N); CTA j handles slice j of
+// every chunk, so flags are per (source rank, CTA).
+__device__ __forceinline__ void slice_of(long long U, int world, int k, int G, int j, long long &cs, long long &b,
+                                         long long &e) {
+    cs = U * k / world;
+    const long long ce = U * (k + 1) / world, len = ce - cs;
+    b = cs + len * j / G;
+    e = cs + len * (j + 1) / G;
+}
+
+template <typename T>
+__device__ __forceinline__ void acc8(float (&s)[8], const uint4 &v, bool first) {
+    const float2 a = unpack2<T>(v.x), b = unpack2<T>(v.y), cc = unpack2<T>(v.z), d = unpack2<T>(v.w);
+    const float f[8] = {a.x, a.y, b.x, b.y, cc.x, cc.y, d.x, d.y};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s[k] = first ? f[k] : s[k] + f[k];
+}
+
+template <typename T>
+__global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, const uint4 *in, uint4 *out,
+                                                                long long U,
+                                                                uint64_t timeout) {
+    __shared__ unsigned s_seq;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t deadline = globaltimer() + timeout;
+    const int j = blockIdx.x, G = gridDim.x, tid = threadIdx.x, W = c.world, R = c.rank;
+    long long cs, b, e;
+    // 1. push my slice j of every peer's chunk into that peer's receive buffer for me
+    for (int k = 1; k < W; ++k) {
+        const int dst = (R + k) % W;
+        slice_of(U, W, dst, G, j, cs, b, e);
+        uint4 *rb = reinterpret_cast<uint4 *>(c.rs_buf(dst, p, R));
+        for (long long u = b + tid; u < e; u += blockDim.x) rb[u - cs] = in[u];
+    }
+    __syncthreads();
+    if (tid < W && tid != R) st_release_sys(c.flag(tid, p, 0, R, j), seq);
+    // 2. wait for every peer's slice j of my chunk, reduce in rank order, publish
+    bool ok = true;
+    if (tid < W && tid != R && !flag_wait(c.flag(R, p, 0, tid, j), seq, deadline)) {
+        report(c.status(), ST_PEER_TIMEOUT | 0x100u | (unsigned)tid);
+        ok = false;
+    }
+    __syncthreads();
+    (void)ok;
+    slice_of(U, W, R, G, j, cs, b, e);
+    uint4 *ag = reinterpret_cast<uint4 *>(c.ag_buf(R, p));
+    for (long long u = b + tid; u < e; u += blockDim.x) {
+        float s[8];
+        for (int r = 0; r < W; ++r) {
+            const uint4 v = (r == R) ? in[u] : reinterpret_cast<const uint4 *>(c.rs_buf(R, p, r))[u - cs];
+            acc8<T>(s, v, r == 0);
+        }
+        const uint4 o = make_uint4(pack2<T>(s[0], s[1]), pack2<T>(s[2], s[3]), pack2<T>(s[4], s[5]),
+                                   pack2<T>(s[6], s[7]));
+        out[u] = o;
+        ag[u - cs] = o;
+    }
+    __syncthreads();
+    if (tid < W && tid != R) st_release_sys(c.flag(tid, p, 1, R, j), seq);
+    // 3. pull every peer's reduced slice j
+    if (tid < W && tid != R && !flag_wait(c.flag(R, p, 1, tid, j), seq, deadline))
+        report(c.status(), ST_PEER_TIMEOUT | 0x200u | (unsigned)tid);
+    __syncthreads();
+    for (int k = 1; k < W; ++k) {
+        const int src = (R + k) % W;
+        slice_of(U, W, src, G, j, cs, b, e);
+        const uint4 *sb = reinterpret_cast<const uint4 *>(c.ag_buf(src, p));
+        for (long long u = b + tid; u < e; u += blockDim.x) out[u] = sb[u - cs];
+    }
+    comm_end(c, seq);
+}
+
+// ---- all-gather ------------------------------------------------------------------------------------------------------
+// LL variant (small payloads): m bytes per rank, m % 8 == 0.
+__global__ void __launch_bounds__(AR_THREADS) ag_ll_kernel(CommView c, char *__restrict__ gathered, long long m,
+                                                           uint64_t timeout) {
+    __shared__ unsigned s_seq;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t deadline = globaltimer() + timeout;
+    const long long nw = m >> 3, stride = (long long)gridDim.x * blockDim.x;
+    const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint2 *mine = reinterpret_cast<const uint2 *>(gathered + (long long)c.rank * m);
+    for (long long i = i0; i < nw; i += stride) {
+        const uint2 d = mine[i];
+        for (int k = 1; k < c.world; ++k) {
+            const int dst = (c.rank + k) % c.world;
+            ll_store(c.ll_slot(dst, p, c.rank) + i * 16, d.x, d.y, seq);
+        }
+    }
+    bool dead = false;
+    for (long long i = i0; i < nw; i += stride) {
+        for (int k = 1; k < c.world; ++k) {
+            const int src = (c.rank + k) % c.world;
+            uint2 d = make_uint2(0u, 0u);
+            if (!dead && !ll_wait(c.ll_slot(c.rank, p, src) + i * 16, seq, deadline, d)) {
+                report(c.status(), ST_PEER_TIMEOUT | 0x300u | (unsigned)src);
+                dead = true;
+            }
+            reinterpret_cast<uint2 *>(gathered + (long long)src * m)[i] = d;
+        }
+    }
+    comm_end(c, seq);
+}
+
+// bulk variant: bytes [off, off + len) of every rank's m-byte slot (m, off, len % 16 == 0, len <= chunk_cap), pushed
+// into the peers' receive buffers and flagged per CTA.
+__global__ void __launch_bounds__(AR_THREADS) ag_bulk_kernel(CommView c, char *__restrict__ gathered, long long m,
+                                                             long long off, long long len, uint64_t timeout) {
+    __shared__ unsigned s_seq;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t deadline = globaltimer() + timeout;
+    const int j = blockIdx.x, G = gridDim.x, tid = threadIdx.x, W = c.world, R = c.rank;
+    const long long U = len >> 4, b = U * j / G, e = U * (j + 1) / G;
+    gathered += off;
+    const uint4 *mine = reinterpret_cast<const uint4 *>(gathered + (long long)R * m);
+    for (int k = 1; k < W; ++k) {
+        const int dst = (R + k) % W;
+        uint4 *rb = reinterpret_cast<uint4 *>(c.rs_buf(dst, p, R));
+        for (long long u = b + tid; u < e; u += blockDim.x) rb[u] = mine[u];
+    }
+    __syncthreads();
+    if (tid < W && tid != R) st_release_sys(c.flag(tid, p, 0, R, j), seq);
+    if (tid < W && tid != R && !flag_wait(c.flag(R, p, 0, tid, j), seq, deadline))
+        report(c.status(), ST_PEER_TIMEOUT | 0x400u | (unsigned)tid);
+    __syncthreads();
+    for (int k = 1; k < W; ++k) {
+        const int src = (R + k) % W;
+        const uint4 *sb = reinterpret_cast<const uint4 *>(c.rs_buf(R, p, src));
+        uint4 *dst = reinterpret_cast<uint4 *>(gathered + (long long)src * m);
+        for (long long u = b + tid; u < e; u += blockDim.x) dst[u] = sb[u];
+    }
+    comm_end(c, seq);
+}
+
+template <typename K>
+static void preload(K k) {
+    cudaFuncAttributes fa;
+    cudaFuncGetAttributes(&fa, k);
+}
+
+}  // namespace vt
+
+using namespace vt;
+
+extern "C" {
+
+// ---- IPC helpers (the reference's names and semantics, vllm_turing/csrc/ce_ar.cu:77-101) ----------------------------
+// A zeroed device buffer and its 64-byte CUDA IPC handle. 0 ok; 1 cudaMalloc, 2 memset, 3 sync, 4 handle failed.
+int ce_alloc(size_t bytes, void **ptr, void *handle) {
+    if (cudaMalloc(ptr, bytes) != cudaSuccess) return 1;
+    if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) return 2;
+    if (cudaDeviceSynchronize() != cudaSuccess) return 3;
+    return cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t *>(handle), *ptr) == cudaSuccess ? 0 : 4;
+}
+
+int ce_open(const void *handle, void **ptr) {
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? 0 : 1;
+}
+
+int ce_close(void *ptr) { return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? 0 : 1; }
+
+int ce_free(void *ptr) { return cudaFree(ptr) == cudaSuccess ? 0 : 1; }
+
+// Single-process multi-GPU use: peer access from the current device to `peer`.
+int ce_enable_peer(int peer) {
+    cudaError_t e = cudaDeviceEnablePeerAccess(peer, 0);
+    if (e == cudaErrorPeerAccessAlreadyEnabled) {
+        cudaGetLastError();
+        return 0;
+    }
+    return e == cudaSuccess ? 0 : 1;
+}
+
+// ---- communicator ------------------------------------------------------------------------------------------------------
+size_t vt_comm_region_bytes(int world, size_t ll_data, size_t big_data, size_t scratch_ints) {
+    if (world < 1 || world > COMM_MAX_RANKS) return 0;
+    return comm_layout(world, ll_data, big_data, scratch_ints).total;
+}
+
+// bases[world]: every rank's region (this rank's own at bases[rank], peers' mapped with ce_open), each
+// vt_comm_region_bytes(...) bytes and zeroed once. Returns an opaque handle or NULL.
+void *vt_comm_create(int rank, int world, void *const *bases, size_t ll_data, size_t big_data, size_t scratch_ints) {
+    if (world < 1 || world > COMM_MAX_RANKS || rank < 0 || rank >= world || !bases) return nullptr;
+    Comm *c = new Comm();
+    memset(&c->v, 0, sizeof(c->v));
+    for (int r = 0; r < world; ++r) {
+        if (!bases[r]) {
+            delete c;
+            return nullptr;
+        }
+        c->v.base[r] = reinterpret_cast<char *>(bases[r]);
+    }
+    c->v.rank = rank;
+    c->v.world = world;
+    c->v.L = comm_layout(world, ll_data, big_data, scratch_ints);
+    c->dev = cur_device();
+    // load every collective kernel now: a lazily loaded module's first launch may synchronise behind a kernel that is
+    // already spinning on a peer (vllm_turing/csrc/host_ar.cu:84-92 preloads for the same reason)
+    preload(ar_oneshot_kernel<__half>);
+    preload(ar_oneshot_kernel<__nv_bfloat16>);
+    preload(ar_twoshot_kernel<__half>);
+    preload(ar_twoshot_kernel<__nv_bfloat16>);
+    preload(ag_ll_kernel);
+    preload(ag_bulk_kernel);
+    cudaGetLastError();
+    return c;
+}
+
+int vt_comm_destroy(void *comm) {
+    delete reinterpret_cast<Comm *>(comm);
+    return 0;
+}
+
+// Largest message of each algorithm (bytes).
+long long vt_comm_ll_bytes(void *comm) { return (long long)(reinterpret_cast<Comm *>(comm)->v.L.ll_slot / 2); }
+long long vt_comm_big_bytes(void *comm) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    return (long long)(c->v.L.chunk_cap * c->v.world);
+}
+
+// The communicator's status word (0 or the first timeout code a kernel reported); synchronises the device.
+unsigned vt_comm_status(void *comm, int clear) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    unsigned v = 0;
+    cudaDeviceSynchronize();
+    cudaMemcpy(&v, c->v.base[c->v.rank] + 128, 4, cudaMemcpyDeviceToHost);
+    if (clear) cudaMemset(c->v.base[c->v.rank] + 128, 0, 4);
+    return v;
+}
+
+// The device-side call counter (number of completed collective calls on this communicator).
+unsigned vt_comm_seq(void *comm) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    unsigned v = 0;
+    cudaDeviceSynchronize();
+    cudaMemcpy(&v, c->v.base[c->v.rank], 4, cudaMemcpyDeviceToHost);
+    return v;
+}
+
+// out[n] = sum over ranks of in[n] (fp16 / bf16: dtype 0 / 1), float32 accumulation in rank order, one rounding.
+// algo 0 auto (one-shot up to the LL slot, else two-shot), 1 one-shot, 2 two-shot. in may equal out. n % 4 == 0
+// (one-shot) / n % 8 == 0 (two-shot); 16-byte aligned. Returns 0 or VT_EARG or a CUDA error.
+int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype, int algo, void *stream) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    if (!c || n < 0 || ((uintptr_t)in & 15) || ((uintptr_t)out & 15)) return VT_EARG;
+    if (n == 0) return 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    const long long bytes = n * 2;
+    const int sms = num_sms(c->dev);
+    if (algo == 0) algo = (bytes <= (long long)(c->v.L.ll_slot / 2) && (n & 3) == 0) ? 1 : 2;
+    if (algo == 1) {
+        if ((n & 3) || bytes > (long long)(c->v.L.ll_slot / 2)) return VT_EARG;
+        const long long nwords = n >> 2;
+        long long g = (nwords + AR_THREADS - 1) / AR_THREADS;
+        if (g > sms) g = sms;
+        if (dtype == 0)
+            ar_oneshot_kernel<__half><<<(int)g, AR_THREADS, 0, s>>>(c->v, (const uint2 *)in, (uint2 *)out, nwords,
+                                                                   peer_timeout_ns());
+        else
+            ar_oneshot_kernel<__nv_bfloat16><<<(int)g, AR_THREADS, 0, s>>>(c->v, (const uint2 *)in, (uint2 *)out,
+                                                                          nwords, peer_timeout_ns());
+        return (int)cudaGetLastError();
+    }
+    if (n & 7) return VT_EARG;
+    // pieces of at most world * chunk_cap bytes (chunk boundaries in 16-byte units), one launch (one seq) each
+    const long long cap_units = (long long)(c->v.L.chunk_cap / 16) * c->v.world;
+    const long long U = n >> 3;
+    for (long long u0 = 0; u0 < U; u0 += cap_units) {
+        const long long u = (U - u0 < cap_units) ? U - u0 : cap_units;
+        long long g = u / (c->v.world * 64);   // >= 64 units (1 KB) per CTA slice
+        if (g < 1) g = 1;
+        if (g > sms) g = sms;
+        if (g > COMM_MAX_CTAS) g = COMM_MAX_CTAS;
+        const uint4 *ip = reinterpret_cast<const uint4 *>(in) + u0;
+        uint4 *op = reinterpret_cast<uint4 *>(out) + u0;
+        if (dtype == 0)
+            ar_twoshot_kernel<__half><<<(int)g, AR_THREADS, 0, s>>>(c->v, ip, op, u, peer_timeout_ns());
+        else
+            ar_twoshot_kernel<__nv_bfloat16><<<(int)g, AR_THREADS, 0, s>>>(c->v, ip, op, u, peer_timeout_ns());
+        if (cudaError_t e = cudaGetLastError()) return (int)e;
+    }
+    return 0;
+}
+
+// gathered: world * m bytes, this rank's payload pre-written at [rank * m, (rank + 1) * m); the peers' slots are
+// filled. m % 8 == 0 (LL, up to the LL slot and 1 MiB) or m % 16 == 0 (bulk, in pieces of the two-shot chunk
+// capacity, one launch each).
+int vt_all_gather(void *comm, void *gathered, long long m, void *stream) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    if (!c || m < 0 || ((uintptr_t)gathered & 15)) return VT_EARG;
+    if (m == 0 || c->v.world == 1) return 0;
+    cudaStream_t s = (cudaStream_t)stream;
+    const int sms = num_sms(c->dev);
+    if ((m & 7) == 0 && m <= (long long)(c->v.L.ll_slot / 2) && m <= (1 << 20)) {
+        const long long nw = m >> 3;
+        long long g = (nw + AR_THREADS - 1) / AR_THREADS;
+        if (g > sms) g = sms;
+        ag_ll_kernel<<<(int)g, AR_THREADS, 0, s>>>(c->v, (char *)gathered, m, peer_timeout_ns());
+        return (int)cudaGetLastError();
+    }
+    if (m & 15) return VT_EARG;
+    const long long cap = (long long)c->v.L.chunk_cap;
+    for (long long off = 0; off < m; off += cap) {
+        const long long len = (m - off < cap) ? m - off : cap;
+        long long g = (len >> 4) / 64;
+        if (g < 1) g = 1;
+        if (g > sms) g = sms;
+        if (g > COMM_MAX_CTAS) g = COMM_MAX_CTAS;
+        ag_bulk_kernel<<<(int)g, AR_THREADS, 0, s>>>(c->v, (char *)gathered, m, off, len, peer_timeout_ns());
+        if (cudaError_t e = cudaGetLastError()) return (int)e;
+    }
+    return 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,313 @@
+// Fused tensor-parallel row-linear layer tail for B200 (sm_100a), decode shapes (M <= 16 token rows), ONE kernel:
+//
+//   partial_r = bf16( (a_r . w_r^T) * sa_r[m] * sw_r[n] )           this rank's K-slice   (vllm_turing/w8a8.py path)
+//   reduced   = bf16( sum_r float(partial_r) )  in rank order         the TP all-reduce      (host_ar.cu:90-101)
+//   residual  = bf16( reduced + residual )                            written in place
+//   y         = bf16( residual * rsqrt(mean(residual^2) + eps) * norm_w )
+//   q, scales = per-token int8 quantisation of y                     (the vLLM op the reference calls at
+//                                                                     vllm_turing/tailoverlap.py:200; arithmetic of
+//                                                                     tests/test_quantfuse.py:45-48, quantfuse.py:18-24)
+//
+// The reference runs these as three or more kernels (GEMV, LL all-reduce, compiled norm + quant); here:
+//  1. GEMV phase (gemv_core.cuh): all CTAs stream this rank's weight slice; the CTA that finishes a 32-column
+//     row-block dequantises it to bf16 and pushes it as LL words straight into every rank's receive slot (NVLink
+//     stores, no staging buffer, no flag round trip).
+//  2. Epilogue phase: token row m is owned by E CTAs (CTA index m * E + g), each for a contiguous 1/E of the row's
+//     columns. Each polls the LL words of all ranks for its columns, sums them in rank order, adds the residual and
+//     writes it back; the sum of squares and then the absmax of the normalised row are combined across the E CTAs
+//     through a seq-tagged 8-byte mailbox word per CTA (combined in CTA order: identical on every rank, no atomics).
+// With world = 1 (no tensor parallelism) the same kernel is the TP1 "fused epilogue without collective".
+// All waits are bounded; timeouts land in the communicator's status word.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "comm.cuh"
+#include "common.cuh"
+#include "gemv_core.cuh"
+#include "host_util.h"
+
+namespace vt {
+
+template <typename T>
+struct FusedArgs {
+    CommView c;
+    const int8_t *a, *w;
+    const float *sa, *sw;
+    int M, N, K, stages, E;
+    T *residual;
+    const T *norm_w;
+    float eps;
+    int8_t *q;
+    float *scales;
+    T *reduced;
+    uint64_t pipe_timeout, peer_timeout;
+};
+
+template <typename T>
+struct LLPushEpi {
+    const CommView *c;
+    const float *sa, *sw;
+    int M, N;
+    unsigned seq, p;
+    __device__ __forceinline__ void operator()(int rb, const int *tile, int tid) const {
+        const int W4 = N >> 2, nwords = M * 8, world = c->world, rank = c->rank;
+        for (int idx = tid; idx < nwords * world; idx += GV_CTHREADS) {
+            const int k = idx / nwords, wi = idx - k * nwords, m = wi >> 3, j = wi & 7;
+            const int col = rb * GV_RB + 4 * j;
+            if (col >= N) continue;
+            const float sam = sa[m];
+            const int *t = tile + m * 32 + 4 * j;
+            const float v0 = dequant1(t[0], sam, sw[col]), v1 = dequant1(t[1], sam, sw[col + 1]);
+            const float v2 = dequant1(t[2], sam, sw[col + 2]), v3 = dequant1(t[3], sam, sw[col + 3]);
+            const int dst = (rank + k) % world;
+            ll_store(c->ll_slot(dst, p, rank) + ((size_t)m * W4 + (col >> 2)) * 16, pack2<T>(v0, v1),
+                     pack2<T>(v2, v3), seq);
+        }
+    }
+};
+
+__device__ __forceinline__ float block_sum_n(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = red[0];
+    for (int i = 1; i < nw; ++i) t += red[i];
+    return t;
+}
+__device__ __forceinline__ float block_max_n(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = red[0];
+    for (int i = 1; i < nw; ++i) t = fmaxf(t, red[i]);
+    return t;
+}
+
+// Publish this CTA's value for (row m, group g, slot) and combine the E values of the row's group in group order.
+__device__ __forceinline__ float group_combine(const CommView &c, int m, int g, int E, int slot, float v, bool is_max,
+                                               unsigned seq, uint64_t deadline, float *bcast) {
+    unsigned long long *mb = c.mbox();
+    if (threadIdx.x == 0) {
+        st_volatile8(&mb[((size_t)m * COMM_MBOX_GROUPS + g) * 2 + slot],
+                     ((unsigned long long)seq << 32) | (unsigned long long)__float_as_uint(v));
+        float t = 0.0f;
+        bool dead = false;
+        for (int q = 0; q < E; ++q) {
+            const unsigned long long *p = &mb[((size_t)m * COMM_MBOX_GROUPS + q) * 2 + slot];
+            unsigned long long x = ld_volatile8(p);
+            uint32_t it = 0;
+            while (!dead && (unsigned)(x >> 32) != seq) {
+                if ((++it & 63u) == 0 && globaltimer() > deadline) {
+                    report(c.status(), ST_GROUP_TIMEOUT | (unsigned)(m * 64 + q));
+                    dead = true;
+                    break;
+                }
+                x = ld_volatile8(p);
+            }
+            const float val = __uint_as_float((unsigned)(x & 0xffffffffu));
+            t = is_max ? fmaxf(t, val) : (q == 0 ? val : t + val);
+        }
+        *bcast = t;
+    }
+    __syncthreads();
+    return *bcast;
+}
+
+template <typename T, int MT>
+__global__ void __launch_bounds__(GV_THREADS, 1) tp_row_linear_kernel(FusedArgs<T> P) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ unsigned s_seq;
+    __shared__ float red[32];
+    __shared__ float bcast;
+    const CommView &c = P.c;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t t0 = globaltimer();
+    LLPushEpi<T> push{&c, P.sa, P.sw, P.M, P.N, seq, p};
+    gemv_phase<MT>(P.a, P.w, P.M, P.N, P.K, c.scratch(), c.tickets(), smem, P.stages, t0 + P.pipe_timeout,
+                   c.status(), push);
+    __syncthreads();
+
+    const int M = P.M, N = P.N, E = P.E, W4 = N >> 2;
+    if ((int)blockIdx.x < M * E) {
+        const int m = blockIdx.x / E, g = blockIdx.x - m * E;
+        const int w0 = (int)((long long)W4 * g / E), w1 = (int)((long long)W4 * (g + 1) / E);
+        float *hbuf = reinterpret_cast<float *>(smem + GV_HDR);   // the GEMV ring is free now
+        const uint64_t deadline = globaltimer() + P.peer_timeout;
+        bool dead = false;
+        float ss = 0.0f;
+        for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
+            const int word = w0 + i;
+            const size_t off = ((size_t)m * W4 + word) * 16;
+            float s[4];
+            for (int r = 0; r < c.world; ++r) {
+                uint2 d = make_uint2(0u, 0u);
+                if (!dead && !ll_wait(c.ll_slot(c.rank, p, r) + off, seq, deadline, d)) {
+                    report(c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
+                    dead = true;
+                }
+                const float2 x0 = unpack2<T>(d.x), x1 = unpack2<T>(d.y);
+                if (r == 0) {
+                    s[0] = x0.x; s[1] = x0.y; s[2] = x1.x; s[3] = x1.y;
+                } else {
+                    s[0] += x0.x; s[1] += x0.y; s[2] += x1.x; s[3] += x1.y;
+                }
+            }
+            const size_t e0 = (size_t)m * N + (size_t)word * 4;
+            if (P.reduced)
+                *reinterpret_cast<uint2 *>(P.reduced + e0) = make_uint2(pack2<T>(s[0], s[1]), pack2<T>(s[2], s[3]));
+            if (P.residual) {
+                uint2 *rp = reinterpret_cast<uint2 *>(P.residual + e0);
+                const uint2 ru = *rp;
+                const float2 r0 = unpack2<T>(ru.x), r1 = unpack2<T>(ru.y);
+                const float h0 = rnd<T>(rnd<T>(s[0]) + r0.x), h1 = rnd<T>(rnd<T>(s[1]) + r0.y);
+                const float h2 = rnd<T>(rnd<T>(s[2]) + r1.x), h3 = rnd<T>(rnd<T>(s[3]) + r1.y);
+                *rp = make_uint2(pack2<T>(h0, h1), pack2<T>(h2, h3));
+                hbuf[4 * i] = h0;
+                hbuf[4 * i + 1] = h1;
+                hbuf[4 * i + 2] = h2;
+                hbuf[4 * i + 3] = h3;
+                ss += h0 * h0 + h1 * h1 + h2 * h2 + h3 * h3;
+            }
+        }
+        if (P.residual) {
+            ss = block_sum_n(ss, red);
+            const float tot = group_combine(c, m, g, E, 0, ss, false, seq, deadline, &bcast);
+            const float rs = __frsqrt_rn(__fdiv_rn(tot, (float)N) + P.eps);
+            float amax = 0.0f;
+            for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
+                const uint2 wu = *reinterpret_cast<const uint2 *>(P.norm_w + (size_t)(w0 + i) * 4);
+                const float2 wa = unpack2<T>(wu.x), wb = unpack2<T>(wu.y);
+                const float y0 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i], rs), wa.x));
+                const float y1 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 1], rs), wa.y));
+                const float y2 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 2], rs), wb.x));
+                const float y3 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 3], rs), wb.y));
+                hbuf[4 * i] = y0;
+                hbuf[4 * i + 1] = y1;
+                hbuf[4 * i + 2] = y2;
+                hbuf[4 * i + 3] = y3;
+                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
+            }
+            amax = block_max_n(amax, red);
+            amax = group_combine(c, m, g, E, 1, amax, true, seq, deadline, &bcast);
+            const float inv = quant_inv(amax);
+            if (g == 0 && threadIdx.x == 0) P.scales[m] = __fdiv_rn(amax, 127.0f);
+            for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
+                *reinterpret_cast<char4 *>(P.q + (size_t)m * N + (size_t)(w0 + i) * 4) =
+                    make_char4(quant1(hbuf[4 * i], inv), quant1(hbuf[4 * i + 1], inv),
+                               quant1(hbuf[4 * i + 2], inv), quant1(hbuf[4 * i + 3], inv));
+            }
+        }
+    }
+    comm_end(c, seq);
+}
+
+template <typename T, int MT>
+static int launch_fused(FusedArgs<T> P, cudaStream_t s) {
+    const int dev = cur_device();
+    const int avail = gv_smem_budget(dev);
+    int stages = (avail - GV_HDR - gv_align128((long long)MT * P.K)) / GV_STAGE;
+    if (stages > GV_MAXSTAGES) stages = GV_MAXSTAGES;
+    if (stages < 2) return VT_EARG;
+    P.stages = stages;
+    const int smem = gv_smem_bytes(MT, P.K, stages);
+    static bool attr_set[VT_MAX_DEV] = {false};
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(tp_row_linear_kernel<T, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, avail) !=
+            cudaSuccess)
+            return (int)cudaGetLastError();
+        attr_set[dev] = true;
+    }
+    const int G = num_sms(dev);
+    int E = G / P.M;
+    if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
+    if (E < 1) return VT_EARG;
+    P.E = E;
+    tp_row_linear_kernel<T, MT><<<G, GV_THREADS, smem, s>>>(P);
+    return (int)cudaGetLastError();
+}
+
+template <typename T>
+static int dispatch_fused(FusedArgs<T> P, cudaStream_t s) {
+    const int M = P.M;
+    if (M <= 1) return launch_fused<T, 1>(P, s);
+    if (M <= 2) return launch_fused<T, 2>(P, s);
+    if (M <= 3) return launch_fused<T, 3>(P, s);
+    if (M <= 4) return launch_fused<T, 4>(P, s);
+    if (M <= 5) return launch_fused<T, 5>(P, s);
+    if (M <= 6) return launch_fused<T, 6>(P, s);
+    if (M <= 8) return launch_fused<T, 8>(P, s);
+    if (M <= 12) return launch_fused<T, 12>(P, s);
+    return launch_fused<T, 16>(P, s);
+}
+
+template <typename T>
+static void preload_fused() {
+    cudaFuncAttributes fa;
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 1>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 2>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 3>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 4>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 5>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 6>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 8>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 12>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 16>);
+}
+
+}  // namespace vt
+
+using namespace vt;
+
+extern "C" {
+
+// The fused row-parallel layer tail on communicator `comm` (all ranks call it in the same order with the same M, N):
+//   a [M, K] int8 (this rank's activation slice), w [N, K] int8 (this rank's weight slice), sa [M], sw [N] float32;
+//   residual [M, N] (updated in place), norm_w [N], eps, q [M, N] int8, scales [M] float32 -- or residual = NULL for
+//   a plain row-linear + all-reduce; reduced [M, N] (optional; required without residual) receives the all-reduced
+//   sum. dtype 0 fp16 / 1 bf16. 1 <= M <= 16, N % 4 == 0, K % 16 == 0, M * N * 2 <= the communicator's LL capacity.
+int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,
+                     const void *norm_w, float eps, void *q, void *scales, void *reduced, int M, int N, int K,
+                     int dtype, void *stream) {
+    Comm *ch = reinterpret_cast<Comm *>(comm);
+    if (!ch || M < 1 || M > 16 || N < 4 || (N & 3) || K < 16 || (K & 15) || ((uintptr_t)a & 15) ||
+        ((uintptr_t)w & 15))
+        return VT_EARG;
+    if (!residual && !reduced) return VT_EARG;
+    if (residual && (!norm_w || !q || !scales || ((uintptr_t)residual & 7) || ((uintptr_t)norm_w & 7) ||
+                     ((uintptr_t)q & 3)))
+        return VT_EARG;
+    if (reduced && ((uintptr_t)reduced & 7)) return VT_EARG;
+    const CommLayout &L = ch->v.L;
+    if ((size_t)M * N * 2 > L.ll_slot / 2 || (size_t)M * N * 4 > L.scratch_bytes || (N + 31) / 32 > 4096)
+        return VT_EARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (dtype == 0) {
+        FusedArgs<__half> P{ch->v, (const int8_t *)a, (const int8_t *)w, (const float *)sa, (const float *)sw,
+                            M, N, K, 0, 0, (__half *)residual, (const __half *)norm_w, eps, (int8_t *)q,
+                            (float *)scales, (__half *)reduced, pipe_timeout_ns(), peer_timeout_ns()};
+        return dispatch_fused(P, s);
+    }
+    FusedArgs<__nv_bfloat16> P{ch->v, (const int8_t *)a, (const int8_t *)w, (const float *)sa, (const float *)sw,
+                               M, N, K, 0, 0, (__nv_bfloat16 *)residual, (const __nv_bfloat16 *)norm_w, eps,
+                               (int8_t *)q, (float *)scales, (__nv_bfloat16 *)reduced, pipe_timeout_ns(),
+                               peer_timeout_ns()};
+    return dispatch_fused(P, s);
+}
+
+// Loads the fused kernels' module now (see vt_comm_create).
+int vt_tp_preload(void) {
+    preload_fused<__half>();
+    preload_fused<__nv_bfloat16>();
+    return (int)cudaGetLastError();
+}
+
+}  // extern "C"

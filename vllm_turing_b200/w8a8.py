@@ -1,0 +1,179 @@
+"""INT8 W8A8 GEMM behind vLLM's cutlass_scaled_mm on B200 (sm_100a).
+
+vLLM's W8A8 int8 linear layers call vllm._custom_ops.cutlass_scaled_mm(a, b, scale_a, scale_b, out_dtype, bias). As in
+the reference (vllm_turing/w8a8.py:125-150), the wrapper is replaced by one that runs the custom op
+vllm_turing::scaled_mm_ with the same arguments, dispatching by M at run time (also inside torch.compile / CUDA-graph
+capture, where M is concrete):
+  - M <= VLLM_TURING_GEMV_MAX_M (default 8): the streamed HBM-bound GEMV (csrc/gemv_core.cuh, bulk copies + dp4a),
+  - M <= VLLM_TURING_MMA_MAX_M (default 32): the small-M tcgen05 kernel (weights as the MMA's A operand),
+  - larger M (prefill): the tcgen05 kind::i8 GEMM with TMEM accumulators (VLLM_TURING_BIG=0 keeps vLLM's),
+  - anything else (non-16-aligned shapes, other dtypes): vLLM's own op.
+The kernels live in libvllm_turing_b200.so, loaded with ctypes (no torch C++ ABI involved), as the reference does.
+"""
+import os
+
+import torch
+
+from . import _build
+
+MAX_M = int(os.environ.get("VLLM_TURING_GEMV_MAX_M", "8"))
+MMA_MAX_M = min(int(os.environ.get("VLLM_TURING_MMA_MAX_M", "32")), 32)
+BIG = os.environ.get("VLLM_TURING_BIG", "1") != "0"
+_ws = {}   # device -> persistent zeroed GEMV workspace (graph capture keeps its address)
+
+
+def lib():
+    return _build.load()
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _dtype_code(dt):
+    return 0 if dt == torch.float16 else 1
+
+
+def gemv_ok(out, a, b, sa, sb, bias, max_m=None):
+    """The GEMV path's layout requirements (vllm_turing/w8a8.py:165-173, same checks)."""
+    M, K = a.shape
+    return (1 <= M <= (MAX_M if max_m is None else max_m) and K % 16 == 0 and a.dtype == torch.int8
+            and a.is_contiguous() and b.dtype == torch.int8 and b.stride(0) == 1 and b.stride(1) == K
+            and out.is_contiguous() and out.dtype in (torch.float16, torch.bfloat16)
+            and sa.dtype == torch.float32 and sb.dtype == torch.float32
+            and sa.numel() in (1, M) and sb.numel() in (1, b.shape[1])
+            and a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0
+            and (bias is None or (bias.dtype == out.dtype and bias.is_contiguous())))
+
+
+def workspace(device, M, N):
+    """Persistent zeroed GEMV workspace for this device, grown outside stream capture only."""
+    need = lib().w8a8_gemv_ws_bytes(M, N)
+    ws = _ws.get(device)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("vllm_turing_b200: GEMV workspace must be sized before CUDA graph capture")
+        ws = _ws[device] = torch.zeros(max(need, 8 << 20), dtype=torch.uint8, device=device)
+    return ws
+
+
+def gemv(out, a, b, sa, sb, bias):
+    """out[M, N] = (a . w^T) * sa * sb (+ bias), w = b.t() the row-major [N, K] weight."""
+    M, K = a.shape
+    N = b.shape[1]
+    ws = workspace(a.device, M, N)
+    rc = lib().w8a8_gemv_ws(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+                            bias.data_ptr() if bias is not None else None, out.data_ptr(), M, N, K,
+                            int(sa.numel() > 1), int(sb.numel() > 1), _dtype_code(out.dtype), ws.data_ptr(),
+                            ws.numel(), _stream())
+    if rc != 0:
+        raise RuntimeError(f"w8a8_gemv launch failed: {rc}")
+
+
+def gemm_s32(a, w):
+    """int32 accumulators a [M, K] . w [N, K]^T (parity checks): the GEMV for small M, the tcgen05 GEMM above."""
+    M, K = a.shape
+    N = w.shape[0]
+    acc = torch.empty(M, N, dtype=torch.int32, device=a.device)
+    L = lib()
+    if M <= 16:
+        rc = L.vt_gemv_s32(a.data_ptr(), w.data_ptr(), acc.data_ptr(), M, N, K, _stream())
+    else:
+        if not hasattr(L, "vt_gemm_s32"):
+            raise RuntimeError("vllm_turing_b200: tensor-core GEMM not built")
+        rc = L.vt_gemm_s32(a.data_ptr(), w.data_ptr(), acc.data_ptr(), M, N, K, _stream())
+    if rc != 0:
+        raise RuntimeError(f"int32 GEMM failed: {rc}")
+    return acc
+
+
+def _has(name):
+    return hasattr(lib(), name)
+
+
+def mma_ok(out, a, b, sa, sb, bias):
+    return a.shape[0] > MAX_M and _has("w8a8_mma") and gemv_ok(out, a, b, sa, sb, bias, MMA_MAX_M)
+
+
+def mma(out, a, b, sa, sb, bias):
+    M, K = a.shape
+    N = b.shape[1]
+    rc = lib().w8a8_mma(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+                        bias.data_ptr() if bias is not None else None, out.data_ptr(), M, N, K,
+                        int(sa.numel() > 1), int(sb.numel() > 1), _dtype_code(out.dtype), _stream())
+    if rc != 0:
+        raise RuntimeError(f"w8a8_mma launch failed: {rc}")
+
+
+def big_ok(out, a, b, sa, sb, bias):
+    """The prefill kernel's requirements (vllm_turing/w8a8.py:185-193, same checks)."""
+    M, K = a.shape
+    N = b.shape[1]
+    return (BIG and _has("w8a8_big") and M > MMA_MAX_M and bias is None and K % 16 == 0 and N % 16 == 0
+            and a.dtype == torch.int8 and a.is_contiguous() and b.dtype == torch.int8 and b.stride(0) == 1
+            and b.stride(1) == K and out.is_contiguous() and out.dtype in (torch.float16, torch.bfloat16)
+            and sa.dtype == torch.float32 and sb.dtype == torch.float32 and sa.numel() == M and sb.numel() == N
+            and sa.is_contiguous() and sb.is_contiguous() and a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0)
+
+
+def big(out, a, b, sa, sb):
+    M, K = a.shape
+    N = b.shape[1]
+    rc = lib().w8a8_big(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), out.data_ptr(), M, N, K,
+                        _dtype_code(out.dtype), _stream())
+    if rc != 0:
+        raise RuntimeError(f"w8a8_big failed: {rc}")
+
+
+_lib_def = torch.library.Library("vllm_turing", "DEF")
+_lib_def.define("scaled_mm_(Tensor(a!) out, Tensor a, Tensor b, Tensor a_scales, Tensor b_scales, Tensor? bias) -> ()")
+
+
+@torch.library.impl(_lib_def, "scaled_mm_", "CUDA")
+def _scaled_mm_cuda(out, a, b, a_scales, b_scales, bias):
+    if gemv_ok(out, a, b, a_scales, b_scales, bias):
+        gemv(out, a, b, a_scales, b_scales, bias)
+    elif mma_ok(out, a, b, a_scales, b_scales, bias):
+        mma(out, a, b, a_scales, b_scales, bias)
+    elif big_ok(out, a, b, a_scales, b_scales, bias):
+        big(out, a, b, a_scales, b_scales)
+    else:
+        torch.ops._C.cutlass_scaled_mm(out, a, b, a_scales, b_scales, bias)
+
+
+@torch.library.register_fake("vllm_turing::scaled_mm_")
+def _scaled_mm_fake(out, a, b, a_scales, b_scales, bias):
+    return None
+
+
+def scaled_mm(a, b, scale_a, scale_b, out_dtype, bias=None):
+    """vLLM's cutlass_scaled_mm contract (vllm_turing/w8a8.py:263-274): a [..., K] int8, b [K, N] view."""
+    assert out_dtype is torch.bfloat16 or out_dtype is torch.float16
+    assert bias is None or bias.numel() == b.shape[1] and bias.dtype == out_dtype
+    target_shape = (*a.shape[:-1], b.shape[1])
+    a = a.view(-1, a.shape[-1])
+    out = torch.empty((a.shape[0], b.shape[1]), dtype=out_dtype, device=a.device)
+    torch.ops.vllm_turing.scaled_mm_(out, a, b, scale_a, scale_b, bias)
+    return out.view(*target_shape)
+
+
+def install():
+    """Replace vllm._custom_ops.cutlass_scaled_mm on B200 (compute capability 10.0)."""
+    from vllm import _custom_ops as ops
+    from vllm.platforms import current_platform
+
+    if getattr(ops.cutlass_scaled_mm, "_vllm_turing", False):
+        return
+    cap = current_platform.get_device_capability()
+    if cap is None or cap.to_int() != 100:
+        return
+    orig = ops.cutlass_scaled_mm
+
+    def cutlass_scaled_mm(a, b, scale_a, scale_b, out_dtype, bias=None):
+        if not (b.shape[0] % 16 == 0 and b.shape[1] % 16 == 0):
+            return orig(a, b, scale_a, scale_b, out_dtype, bias)
+        return scaled_mm(a, b, scale_a, scale_b, out_dtype, bias)
+
+    cutlass_scaled_mm._vllm_turing = True
+    cutlass_scaled_mm._orig = orig
+    ops.cutlass_scaled_mm = cutlass_scaled_mm
