@@ -5,9 +5,10 @@ Workload (BASELINE.json config 1 at N = 1, the same layer tensor-parallel at N >
   gate_up : column-parallel W8A8 GEMV, M tokens, [5120 -> 34816 / N]  (w8a8_gemv_ws)
   down    : row-parallel W8A8 GEMV, [17408 / N -> 5120] fused with the TP all-reduce, residual add, RMSNorm and per-token
             int8 re-quantisation (vt_tp_row_linear; at N = 1 the "fused epilogue without collective")
-M = 5 tokens (1 + 4 MTP drafts) by default. Strong scaling: the layer's total work is fixed, N ranks split it.
-Inputs: seeded synthetic tensors of the config's shapes and distributions (no checkpoint offline); several weight sets
-are rotated so every timed step streams more than 2 x L2 (126 MB) of weights from HBM.
+One step = a 64-layer decode stack of such layers (the depth of config 4), every layer with its own weight buffers, so
+each step streams 64 x 267 MB / N of weights from HBM (inputs far larger than L2). M = 5 tokens (1 + 4 MTP drafts) by
+default. Strong scaling: the layer's total work is fixed, N ranks split it. Inputs: seeded synthetic tensors of the
+config's shapes and distributions (no checkpoint offline; the per-layer buffers are copies of a few generated sets).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
@@ -19,6 +20,7 @@ host cores instead (the reference's own path is CUDA for sm_75 only; there is no
 import argparse
 import json
 import os
+import shutil
 import statistics
 import subprocess
 import sys
@@ -32,12 +34,14 @@ METRIC = "W8A8 linear+TP all-reduce µs/layer, TOPS & bus GB/s at 1/2/4/8 B200"
 HIDDEN, INTER = 5120, 17408
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
+LAYERS = 64
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=5)
@@ -57,7 +61,7 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms from warm-up through the timed region."""
 
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -70,9 +74,11 @@ class ClockSampler:
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
+            cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-i", str(self.index),
+                   "-lms", "100"]
+            if shutil.which("stdbuf"):
+                cmd = ["stdbuf", "-oL"] + cmd   # line-buffered: a terminated sampler loses nothing
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:   # noqa: BLE001
@@ -205,19 +211,24 @@ def main():
         gloo = dist.group.WORLD
     L = _build.load()
     M = args.tokens
+    NL = args.layers
     assert INTER % world == 0 and (2 * INTER) % world == 0
     K_dn, N_gu = INTER // world, 2 * INTER // world
     bytes_gu_w = N_gu * HIDDEN
     bytes_dn_w = HIDDEN * K_dn
-    R = max(2, -(-3 * L2_BYTES // (bytes_gu_w + bytes_dn_w)))     # weight sets streamed per rotation
-    sets = []
-    for i in range(R):
+    base = []   # a few generated weight sets; every layer gets its own device copy of one of them
+    for i in range(min(NL, 2)):
         gu = make_layer_inputs(M, N_gu, HIDDEN, seed=100 + i, rank=rank, with_norm=False)
         dn = make_layer_inputs(M, HIDDEN, K_dn, seed=i, rank=rank)
-        sets.append(dict(gu_a=gu.a.to(dev), gu_w=gu.w.to(dev), gu_sa=gu.sa.to(dev), gu_sw=gu.sw.to(dev),
+        base.append(dict(gu_a=gu.a.to(dev), gu_w=gu.w.to(dev), gu_sa=gu.sa.to(dev), gu_sw=gu.sw.to(dev),
                          dn_a=dn.a.to(dev), dn_w=dn.w.to(dev), dn_sa=dn.sa.to(dev), dn_sw=dn.sw.to(dev)))
         if i == 0:
             residual0, norm_w = dn.residual.to(dev), dn.norm_w.to(dev)
+    sets = []
+    for i in range(NL):
+        b = base[i % len(base)]
+        sets.append({k: (v.clone() if k in ("gu_w", "dn_w") else v) for k, v in b.items()})
+    R = NL
     comm = TPComm(gloo, dev)
     out_gu = torch.empty(M, N_gu, dtype=torch.bfloat16, device=dev)
     residual = residual0.clone()
@@ -234,9 +245,9 @@ def main():
                         q=q, scales=scales)
 
     def step(i):
-        s = sets[i % R]
-        gate_up(s)
-        down(s)
+        for s in sets:
+            gate_up(s)
+            down(s)
 
     def barrier():
         torch.cuda.synchronize()
@@ -250,12 +261,9 @@ def main():
         return t.item()
 
     K, W = args.steps, max(args.warmup, 1 if args.profile else 3)
-    for i in range(W):
-        step(i)
-    barrier()
-    comm.check()
     if args.profile:
-        for i in range(K):
+        sets = sets[:2]
+        for i in range(W + K):
             step(i)
         barrier()
         comm.check()
@@ -265,31 +273,45 @@ def main():
         dist.destroy_process_group()
         return
 
-    # ---- timed region: K layers ----
+    # ---- timed region: K steps of the NL-layer stack; clocks sampled from warm-up (at least 1 s of the same load)
+    # through the end of the timed region ----
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
+        t_w = time.perf_counter()
+        i = 0
+        while i < W or time.perf_counter() - t_w < 1.0:
+            step(i)
+            i += 1
+            if i % 8 == 0:
+                torch.cuda.synchronize()
         barrier()
+        comm.check()
         e0.record(stream)
         for i in range(K):
             step(i)
         e1.record(stream)
         barrier()
-    t_step = max_over_ranks(e0.elapsed_time(e1) / K) / 1e3          # seconds per layer, max over ranks
+    W = max(W, i)
+    t_step = max_over_ranks(e0.elapsed_time(e1) / K) / 1e3          # seconds per step, max over ranks
+    t_layer = t_step / NL
     comm.check()
 
-    # ---- per-kernel durations (same stream, CUDA events per launch group) for the roofline ----
-    def time_kernel(fn, n):
+    # ---- per-kernel durations for the roofline: each kernel alone over the NL layers' buffers, K passes, CUDA events on
+    # the launching stream ----
+    def time_kernel(fn, passes):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
         a.record(stream)
-        for i in range(n):
-            fn(sets[i % R])
+        for _ in range(passes):
+            for s in sets:
+                fn(s)
         b.record(stream)
         barrier()
-        return max_over_ranks(a.elapsed_time(b) / n) / 1e3
+        return max_over_ranks(a.elapsed_time(b) / (passes * NL)) / 1e3
 
-    t_gu = time_kernel(gate_up, K)
-    t_dn = time_kernel(down, K)
+    passes = max(1, min(K, 20))
+    t_gu = time_kernel(gate_up, passes)
+    t_dn = time_kernel(down, passes)
     comm.check()
     gu_bytes = bytes_gu_w + M * HIDDEN + 2 * M * N_gu + 4 * (M + N_gu)
     dn_bytes = bytes_dn_w + M * K_dn + 4 * (M + HIDDEN) + M * HIDDEN * (2 + 2 + 1) + 4 * M + 2 * HIDDEN
@@ -298,7 +320,8 @@ def main():
                                                                            dn_bytes)
     achieved = dom[2] / dom[1] / 1e9
 
-    # ---- end to end through the public API with host buffers ----
+    # ---- end to end through the public API with host buffers: every step copies the stack's inputs (the first
+    # layer's activations and scales, the residual) from pinned host memory and reads its outputs back ----
     e2e = None
     if not args.no_e2e:
         s0 = sets[0]
@@ -310,20 +333,22 @@ def main():
         d_in = {k: torch.empty_like(v, device=dev) for k, v in h_in.items()}
         h2d = sum(v.numel() * v.element_size() for v in h_in.values()) + h_res.numel() * 2
         d2h = h_q.numel() + h_s.numel() * 4 + h_r.numel() * 2
+        first = dict(sets[0])
+        first.update(d_in)
 
         def e2e_step(i):
-            s = dict(sets[i % R])
             for k, v in h_in.items():
                 d_in[k].copy_(v, non_blocking=True)
-                s[k] = d_in[k]
             residual.copy_(h_res, non_blocking=True)
-            gate_up(s)
-            down(s)
+            for j, s in enumerate(sets):
+                s = first if j == 0 else s
+                gate_up(s)
+                down(s)
             h_q.copy_(q, non_blocking=True)
             h_s.copy_(scales, non_blocking=True)
             h_r.copy_(residual, non_blocking=True)
 
-        for i in range(W):
+        for i in range(args.warmup):
             e2e_step(i)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         barrier()
@@ -334,9 +359,9 @@ def main():
         barrier()
         t_e2e = max_over_ranks(a.elapsed_time(b) / K) / 1e3
         comm.check()
-        e2e = {"value": layer_ops(M, world) / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": int(h2d),
-               "d2h_bytes_per_step": int(d2h), "us_per_layer": t_e2e * 1e6,
-               "api": "w8a8.gemv + TPComm.row_linear, pinned host inputs / outputs copied every step"}
+        e2e = {"value": layer_ops(M, world) * NL / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "us_per_layer": t_e2e / NL * 1e6,
+               "api": "w8a8.gemv + TPComm.row_linear over the stack, pinned host inputs / outputs copied every step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -345,26 +370,25 @@ def main():
                "sample": f"{n} full TP1 layers (M={M}) through the C oracle, OpenMP"}
 
     S = 2 * M * HIDDEN
-    bus = (2.0 * (world - 1) / world * S / t_step / 1e9) if world > 1 else 0.0
+    bus = (2.0 * (world - 1) / world * S / t_layer / 1e9) if world > 1 else 0.0
     clocks = clk.summary()
-    launches = 2 * K
     line = {
-        "metric": METRIC, "value": layer_ops(M, world) / t_step / 1e12, "unit": "TOPS", "n_gpus": world,
+        "metric": METRIC, "value": layer_ops(M, world) / t_layer / 1e12, "unit": "TOPS", "n_gpus": world,
         "steps": K, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "us_per_layer": t_step * 1e6, "bus_gbs": bus,
-        "config": {"workload": f"decode W8A8 MLP layer M={M}: gate_up 5120->34816 column-parallel + down "
-                               f"17408->5120 row-parallel fused with TP all-reduce + RMSNorm + int8 quant "
-                               f"(BASELINE config 1 at N=1, config 2 split at N>1)",
-                   "tokens": M, "tp": world, "K_down_local": K_dn, "N_gate_up_local": N_gu,
-                   "l2": f"inputs larger than L2: {R} weight sets rotated, "
-                         f"{R * (bytes_gu_w + bytes_dn_w) / 2**20:.0f} MiB per rotation",
+        "us_per_layer": t_layer * 1e6, "bus_gbs": bus,
+        "config": {"workload": f"decode W8A8 MLP stack of {NL} layers, M={M}: gate_up 5120->34816 column-parallel + "
+                               f"down 17408->5120 row-parallel fused with TP all-reduce + RMSNorm + int8 quant "
+                               f"(BASELINE config 1 per layer at N=1, config 2 split at N>1)",
+                   "tokens": M, "layers": NL, "tp": world, "K_down_local": K_dn, "N_gate_up_local": N_gu,
+                   "l2": f"inputs larger than L2: {NL} layers with their own weights, "
+                         f"{NL * (bytes_gu_w + bytes_dn_w) / 2**20:.0f} MiB of weights per step",
                    "parallelism": f"tp{world}"},
         "kernel_us": {"w8a8_gemv_gate_up": t_gu * 1e6, "tp_row_linear_down": t_dn * 1e6},
         "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": None, "bytes_per_launch": dom[2],
                      "peak_kind": peak_kind},
-        "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "cpu_baseline": cpu,
+        "clocks": clocks, "gpu_launches": 2 * NL * K, "e2e": e2e, "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

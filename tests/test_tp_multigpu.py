@@ -1,0 +1,173 @@
+"""Multi-rank collectives and the fused row-linear on 2..8 GPUs, one process per GPU (the reference's test pattern:
+torch.multiprocessing.spawn, a gloo group for set-up, tests/test_hostar.py:13-20), against the CPU oracle:
+  - one-shot and two-shot all-reduce bit-exact to the rank-ordered float32 sum (tests/bench_devll.py:28-36 for 2 ranks)
+    at decode / odd / prefill sizes, fp16 and bf16, identical on every rank;
+  - all-gather (LL and bulk) exact;
+  - the fused GEMV + all-reduce + residual + RMSNorm + quant at BASELINE config 0 (M=16, K_local=8704, N=5120) and
+    config 2 (M in {1, 5}, K = 17408 / world): reduced sum bit-exact, residual bit-exact, int8 within 1 LSB;
+  - 64 back-to-back calls without host syncs, and a captured CUDA graph of mixed calls replayed with fresh inputs
+    (tests/test_hostar.py:33-54).
+Skipped with fewer than 2 GPUs."""
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _parts(n, world, seed, dtype):
+    return [(torch.randn(n, generator=torch.Generator().manual_seed(seed * 100 + r)) * 4).to(dtype)
+            for r in range(world)]
+
+
+def _worker(rank, world, port, q):
+    import numpy as np
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    from oracle import oracle as O
+    from vllm_turing_b200.comm import TPComm
+    from vllm_turing_b200.synthetic import make_layer_inputs
+
+    fails = []
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+        comm = TPComm(dist.group.WORLD, dev)
+
+        def check(cond, what):
+            if not cond:
+                fails.append(f"rank {rank}: {what}")
+
+        # ---- all-reduce ----
+        for dtype, code in ((torch.bfloat16, 1), (torch.float16, 0)):
+            for i, (n, algo) in enumerate(((5120, 1), (5 * 5120, 1), (24 * 5120, 1), (4100, 1), (5 * 5120, 2),
+                                           (1000 * 8, 2), (2048 * 5120, 2), (8192 * 5120, 0))):
+                parts = _parts(n, world, 10 + i, dtype)
+                y = comm.all_reduce(parts[rank].to(dev), algo=algo)
+                torch.cuda.synchronize()
+                want = O.all_reduce([O.to_bits(p) for p in parts], code)
+                check(np.array_equal(O.to_bits(y.cpu()), want), f"all_reduce n={n} algo={algo} {dtype}")
+        # in place
+        parts = _parts(5 * 5120, world, 99, torch.bfloat16)
+        x = parts[rank].to(dev)
+        comm.all_reduce(x, out=x, algo=2)
+        torch.cuda.synchronize()
+        check(np.array_equal(O.to_bits(x.cpu()), O.all_reduce([O.to_bits(p) for p in parts], 1)), "in-place")
+
+        # ---- all-gather ----
+        for m in (5 * 1024, 48 * 1024, 3 * 1024 * 1024 + 16):
+            g = torch.zeros(world * m, dtype=torch.uint8, device=dev)
+            g[rank * m:(rank + 1) * m] = (rank * 37 + torch.arange(m, device=dev) % 251).to(torch.uint8)
+            comm.all_gather(g, m)
+            torch.cuda.synchronize()
+            for r in range(world):
+                exp = (r * 37 + torch.arange(m) % 251).to(torch.uint8)
+                check(torch.equal(g[r * m:(r + 1) * m].cpu(), exp), f"all_gather m={m} slot {r}")
+
+        # ---- fused row-linear ----
+        for (M, N, K) in ((16, 5120, 8704), (5, 5120, 17408 // world), (1, 5120, 17408 // world)):
+            lis = [make_layer_inputs(M, N, K, seed=M, rank=r) for r in range(world)]
+            me = lis[rank]
+            res = me.residual.to(dev)
+            red = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            qd, sd = comm.row_linear(me.a.to(dev), me.w.to(dev), me.sa.to(dev), me.sw.to(dev), residual=res,
+                                     norm_w=me.norm_w.to(dev), eps=1e-6, reduced=red)
+            torch.cuda.synchronize()
+            ro, qo, so, redo = O.row_linear_tp([li.a.numpy() for li in lis], [li.w.numpy() for li in lis],
+                                               [li.sa.numpy() for li in lis], [li.sw.numpy() for li in lis],
+                                               O.to_bits(me.residual), O.to_bits(me.norm_w), 1e-6, 1)
+            check(np.array_equal(O.to_bits(red.cpu()), redo), f"fused reduced M={M} K={K}")
+            check(np.array_equal(O.to_bits(res.cpu()), ro), f"fused residual M={M} K={K}")
+            d = np.abs(qd.cpu().numpy().astype(np.int32) - qo.astype(np.int32))
+            check(d.max() <= 1, f"fused q M={M} K={K} off by {d.max()}")
+            # identical on every rank
+            q0 = qd.clone().cpu()
+            dist.broadcast(q0, src=0)
+            check(torch.equal(q0, qd.cpu()), f"fused q differs from rank 0 (M={M})")
+
+        # ---- stress: back-to-back mixed calls without host syncs ----
+        xs = [_parts(n, world, 500 + i, torch.bfloat16) for i, n in enumerate((5120, 15360, 5120, 30720) * 16)]
+        ys = [comm.all_reduce(p[rank].to(dev)) for p in xs]
+        torch.cuda.synchronize()
+        bad = sum(not np.array_equal(O.to_bits(y.cpu()), O.all_reduce([O.to_bits(t) for t in p], 1))
+                  for y, p in zip(ys, xs))
+        check(bad == 0, f"stress: {bad} of {len(xs)} wrong")
+
+        # ---- CUDA graph of mixed calls, replayed with fresh inputs ----
+        sizes = (5120, 15360, 5120, 30720, 2048 * 5120) * 3
+        ins = [torch.empty(n, dtype=torch.bfloat16, device=dev) for n in sizes]
+        outs = [torch.empty_like(t) for t in ins]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for t, o in zip(ins, outs):
+                comm.all_reduce(t, out=o)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for t, o in zip(ins, outs):
+                comm.all_reduce(t, out=o)
+        for it in range(6):
+            parts = [_parts(n, world, 1000 + 31 * it + j, torch.bfloat16) for j, n in enumerate(sizes)]
+            for t, p in zip(ins, parts):
+                t.copy_(p[rank])
+            g.replay()
+            torch.cuda.synchronize()
+            for j, (o, p) in enumerate(zip(outs, parts)):
+                if not np.array_equal(O.to_bits(o.cpu()), O.all_reduce([O.to_bits(x) for x in p], 1)):
+                    check(False, f"graph replay {it} call {j}")
+                    break
+        del g
+        st = comm.status(clear=True)
+        check(st == 0, f"device status {st:#x}")
+        comm.close()
+        dist.destroy_process_group()
+    except Exception:   # noqa: BLE001
+        fails.append(f"rank {rank}: {traceback.format_exc()}")
+    q.put((rank, fails))
+
+
+def _run(world):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(world):
+            r, f = q.get(timeout=600)
+            res[r] = f
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    fails = [x for r in sorted(res) for x in res[r]]
+    assert len(res) == world, f"only {len(res)} of {world} ranks reported"
+    assert not fails, "\n".join(fails)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_ranks(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run(world)

@@ -53,13 +53,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Waits for the phase of `parity` to complete; false once globaltimer passes `deadline` (ns).
+// Waits for the phase of `parity` to complete; false once globaltimer passes `deadline` (ns). The timer is read only
+// every 1024 polls: reading %globaltimer costs far more than a poll and would throttle the pipeline it bounds.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64_t deadline) {
-    if (mbar_try_wait(bar, parity)) return true;
-    while (true) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer() > deadline) return false;
+    uint32_t it = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if ((++it & 1023u) == 0 && globaltimer() > deadline) return false;
     }
+    return true;
 }
 
 // ---- 1-D bulk copy global -> shared (TMA engine), completion counted in bytes on an mbarrier -------------------------
