@@ -33,6 +33,7 @@ def lib():
         sig = {
             "orc_gemm_s32": [_P, _P, _P, _I, _I, _I],
             "orc_dequant": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I],
+            "orc_dequant_big": [_P, _P, _P, _P, _I, _I, _I],
             "orc_scaled_mm": [_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I],
             "orc_quant_rows": [_P, _P, _P, _I, _I, _I],
             "orc_weight_quant": [_P, _P, _P, _I, _I],
@@ -106,6 +107,16 @@ def dequant(acc, sa, sw, bias=None, dtype=1):
     return out
 
 
+def dequant_big(acc, sa, sw, dtype=1):
+    """The prefill epilogue order sa * (sw * acc) (vllm_turing/csrc/w8a8_big.cu:26-35)."""
+    acc = np.ascontiguousarray(acc, np.int32)
+    M, N = acc.shape
+    out = np.empty((M, N), np.uint16)
+    lib().orc_dequant_big(_p(acc), _p(np.ascontiguousarray(sa, np.float32).reshape(-1)),
+                          _p(np.ascontiguousarray(sw, np.float32).reshape(-1)), _p(out), M, N, dtype)
+    return out
+
+
 def scaled_mm(a, w, sa, sw, bias=None, dtype=1):
     """bits [M, N] of the W8A8 linear (GEMM + per-token x per-channel dequant)."""
     M, K = a.shape
@@ -169,9 +180,10 @@ def row_linear_tp(a_list, w_list, sa_list, sw_list, residual_bits, weight_bits, 
     q = np.empty((M, N), np.int8)
     s = np.empty((M,), np.float32)
     red = np.empty((M, N), np.uint16)
-    arrs = [(ctypes.c_void_p * n)(*[np.ascontiguousarray(x).ctypes.data for x in lst])
-            for lst in (a_list, w_list, sa_list, sw_list)]
-    lib().orc_row_linear_tp(n, arrs[0], arrs[1], arrs[2], arrs[3], _p(res), _p(np.ascontiguousarray(weight_bits)),
+    keep = [[np.ascontiguousarray(x) for x in lst] for lst in (a_list, w_list, sa_list, sw_list)]  # alive
+    arrs = [(ctypes.c_void_p * n)(*[x.ctypes.data for x in lst]) for lst in keep]
+    wb = np.ascontiguousarray(weight_bits)
+    lib().orc_row_linear_tp(n, arrs[0], arrs[1], arrs[2], arrs[3], _p(res), _p(wb),
                             float(eps), _p(q), _p(s), _p(red), M, N, K, dtype)
     return res, q, s, red
 

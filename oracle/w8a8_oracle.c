@@ -110,6 +110,20 @@ void orc_dequant(const int32_t *acc, const float *sa, const float *sw, const uin
     }
 }
 
+/* The prefill GEMM's epilogue order: out[m, n] = round_dtype(sa[m] * (sw[n] * (float)acc)).
+ * Reference: the CUTLASS visitor tree of vllm_turing/csrc/w8a8_big.cu:26-35 (Compute0 = ScaleB * Acc, then
+ * Compute1 = ScaleA * that, each a float32 multiply), which its test pins bitwise to vLLM's cutlass_scaled_mm
+ * (tests/test_w8a8_big.py:49-54). */
+void orc_dequant_big(const int32_t *acc, const float *sa, const float *sw, uint16_t *out, int M, int N, int dtype) {
+#pragma omp parallel for schedule(static)
+    for (int m = 0; m < M; ++m) {
+        for (int n = 0; n < N; ++n) {
+            const float t = sw[n] * (float)acc[(long)m * N + n];
+            out[(long)m * N + n] = rnd16(sa[m] * t, dtype);
+        }
+    }
+}
+
 /* cutlass_scaled_mm semantics as the reference plugin serves them (vllm_turing/w8a8.py:235-244 -> gemv / mma). */
 void orc_scaled_mm(const int8_t *a, const int8_t *w, const float *sa, const float *sw, const uint16_t *bias,
                    uint16_t *out, int M, int N, int K, int sa_rows, int sw_rows, int dtype) {

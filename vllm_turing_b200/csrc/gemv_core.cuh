@@ -10,10 +10,12 @@
 //    (no wave quantisation on 148 SMs). A CTA's range cuts at most two row-blocks; their partial int32 sums meet in
 //    a zero-initialised global scratch through atomicAdd (exact: integer addition commutes), and the CTA that brings a
 //    row-block's ticket to K / 16 chunks finishes it (then zeroes the scratch and the ticket for the next call).
-//  * The producer warp streams the owned weight rows segment by segment (32 rows x up to 512 bytes = 16 KB) into a
-//    ring of shared-memory stages with 1-D bulk copies (TMA engine, L2 evict-first), one mbarrier per stage for "full"
-//    (bytes landed) and one for "empty" (the 8 consumer warps are done). Up to 128 KB per SM are in flight, decoupled
-//    from registers.
+//  * The producer warp streams the owned weight rows segment by segment (32 rows x 512 bytes = 16 KB) into a ring of
+//    shared-memory stages with two 2-D TMA tensor loads per stage (box 256 bytes x 32 rows; L2 evict-first), one
+//    mbarrier per stage for "full" (bytes landed) and one for "empty" (the 8 consumer warps are done). Up to 128 KB per
+//    SM are in flight, decoupled from registers; few large TMA operations per stage, because the number of TMA
+//    operations a SM keeps in flight (not their bytes) bounded a first design with one 512-byte copy per row.
+//    Boxes reaching past K or N read zeros (OOB fill) and still count their full bytes.
 //  * Consumer warp w owns rows 4w .. 4w+3 of the row-block; lane l the 16-byte chunk l of the segment: 4 weight
 //    vectors and M activation vectors from shared memory (conflict-free, consecutive lanes read consecutive 16 bytes)
 //    feed 16 M dp4a. At the end of a piece the 32 lanes reduce with xor shuffles.
@@ -88,7 +90,7 @@ __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c
 // (tid 0..255) for every row-block this CTA finishes, with the row-block's int32 accumulators in tile[m * 32 + j]
 // (column n = rb * 32 + j); named barrier 1 spans the consumer threads. Returns false if any wait of this CTA timed out.
 template <int MT, class Fin>
-__device__ __forceinline__ bool gemv_phase(const int8_t *__restrict__ a, const int8_t *__restrict__ w, int M, int N,
+__device__ __forceinline__ bool gemv_phase(const int8_t *__restrict__ a, const CUtensorMap *wmap, int M, int N,
                                            int K, int *__restrict__ scratch, int *__restrict__ tickets,
                                            unsigned char *smem, int stages, uint64_t deadline, unsigned *status,
                                            Fin &fin) {
@@ -115,6 +117,7 @@ __device__ __forceinline__ bool gemv_phase(const int8_t *__restrict__ a, const i
     if (warp == GV_CWARPS) {
         // ---------------- producer warp ----------------
         if (lane == 0) {
+            tma_prefetch_desc(wmap);
             mbar_arrive_expect_tx(sm.act_bar, (uint32_t)(M * K));
             bulk_g2s(sm.act, a, (uint32_t)(M * K), sm.act_bar);
         }
@@ -132,14 +135,11 @@ __device__ __forceinline__ bool gemv_phase(const int8_t *__restrict__ a, const i
                 }
             }
             __syncwarp();
-            const int rows = min(GV_RB, N - sg.rb * GV_RB);
-            const uint32_t bytes = (uint32_t)(sg.c1 - sg.c0) * 16u;
-            if (lane == 0) mbar_arrive_expect_tx(&sm.full[s], (uint32_t)rows * bytes);
-            __syncwarp();
-            if (lane < rows) {
-                bulk_g2s_hint(sm.ring + (size_t)s * GV_STAGE + lane * GV_SEGB,
-                              w + (long long)(sg.rb * GV_RB + lane) * K + (long long)sg.c0 * 16, bytes, &sm.full[s],
-                              pol);
+            if (lane == 0) {
+                mbar_arrive_expect_tx(&sm.full[s], (uint32_t)GV_STAGE);
+                unsigned char *st = sm.ring + (size_t)s * GV_STAGE;
+                tma_load_2d_hint(st, wmap, sg.c0 * 16, sg.rb * GV_RB, &sm.full[s], pol);
+                tma_load_2d_hint(st + GV_STAGE / 2, wmap, sg.c0 * 16 + GV_SEGB / 2, sg.rb * GV_RB, &sm.full[s], pol);
             }
             ++i;
         }
@@ -172,10 +172,12 @@ __device__ __forceinline__ bool gemv_phase(const int8_t *__restrict__ a, const i
         if (pc0 < 0) pc0 = sg.c0;
         const int nch = sg.c1 - sg.c0;
         if (lane < nch) {
-            const unsigned char *st = sm.ring + (size_t)s * GV_STAGE + (warp * 4) * GV_SEGB + lane * 16;
+            // stage layout: [box (lane / 16)][row 0..31][256 bytes]
+            const unsigned char *st = sm.ring + (size_t)s * GV_STAGE + (lane >> 4) * (GV_STAGE / 2) +
+                                      (warp * 4) * (GV_SEGB / 2) + (lane & 15) * 16;
             int4 wv[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const int4 *>(st + j * GV_SEGB);
+            for (int j = 0; j < 4; ++j) wv[j] = *reinterpret_cast<const int4 *>(st + j * (GV_SEGB / 2));
             const unsigned char *ap = act + (size_t)(sg.c0 + lane) * 16;
 #pragma unroll
             for (int m = 0; m < MT; ++m) {

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "host_util.h"
+#include "tma_host.h"
 
 namespace vt {
 
@@ -122,7 +123,8 @@ __device__ __forceinline__ float group_combine(const CommView &c, int m, int g, 
 }
 
 template <typename T, int MT>
-__global__ void __launch_bounds__(GV_THREADS, 1) tp_row_linear_kernel(FusedArgs<T> P) {
+__global__ void __launch_bounds__(GV_THREADS, 1)
+    tp_row_linear_kernel(const __grid_constant__ CUtensorMap wmap, FusedArgs<T> P) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ unsigned s_seq;
     __shared__ float red[32];
@@ -132,7 +134,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) tp_row_linear_kernel(FusedArgs<
     const unsigned p = seq & 1u;
     const uint64_t t0 = globaltimer();
     LLPushEpi<T> push{&c, P.sa, P.sw, P.M, P.N, seq, p};
-    gemv_phase<MT>(P.a, P.w, P.M, P.N, P.K, c.scratch(), c.tickets(), smem, P.stages, t0 + P.pipe_timeout,
+    gemv_phase<MT>(P.a, &wmap, P.M, P.N, P.K, c.scratch(), c.tickets(), smem, P.stages, t0 + P.pipe_timeout,
                    c.status(), push);
     __syncthreads();
 
@@ -231,7 +233,9 @@ static int launch_fused(FusedArgs<T> P, cudaStream_t s) {
     if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
     if (E < 1) return VT_EARG;
     P.E = E;
-    tp_row_linear_kernel<T, MT><<<G, GV_THREADS, smem, s>>>(P);
+    CUtensorMap wmap;
+    if (!make_map_i8(&wmap, P.w, P.N, P.K, GV_SEGB / 2, GV_RB, CU_TENSOR_MAP_SWIZZLE_NONE)) return VT_EARG;
+    tp_row_linear_kernel<T, MT><<<G, GV_THREADS, smem, s>>>(wmap, P);
     return (int)cudaGetLastError();
 }
 

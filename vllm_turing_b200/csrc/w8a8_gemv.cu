@@ -13,6 +13,7 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "host_util.h"
+#include "tma_host.h"
 
 namespace vt {
 
@@ -46,11 +47,16 @@ struct S32Epi {
 
 template <int MT, class Epi>
 __global__ void __launch_bounds__(GV_THREADS, 1)
-    gemv_kernel(const int8_t *__restrict__ a, const int8_t *__restrict__ w, int M, int N, int K, int *scratch,
-                int *tickets, int stages, uint64_t timeout_ns, unsigned *status, Epi epi) {
+    gemv_kernel(const int8_t *__restrict__ a, const __grid_constant__ CUtensorMap wmap, int M, int N, int K,
+                int *scratch, int *tickets, int stages, uint64_t timeout_ns, unsigned *status, Epi epi) {
     extern __shared__ __align__(128) unsigned char smem[];
     const uint64_t deadline = globaltimer() + timeout_ns;
-    gemv_phase<MT>(a, w, M, N, K, scratch, tickets, smem, stages, deadline, status, epi);
+    gemv_phase<MT>(a, &wmap, M, N, K, scratch, tickets, smem, stages, deadline, status, epi);
+}
+
+// TMA map of the weight [N, K] for the GEMV stages: box 256 bytes x 32 rows, no swizzle.
+inline bool gemv_wmap(CUtensorMap *m, const void *w, int N, int K) {
+    return make_map_i8(m, w, N, K, GV_SEGB / 2, GV_RB, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 // Scratch the GEMV needs: int32 partial sums [M, N] + one ticket per 32-column row-block.
@@ -89,7 +95,9 @@ static int launch_mt(const int8_t *a, const int8_t *w, int M, int N, int K, void
     if (g > num_sms(dev)) g = num_sms(dev);
     int *sc = reinterpret_cast<int *>(scratch);
     int *tickets = sc + (size_t)M * N;
-    gemv_kernel<MT, Epi><<<(int)g, GV_THREADS, smem, s>>>(a, w, M, N, K, sc, tickets, stages, pipe_timeout_ns(),
+    CUtensorMap wmap;
+    if (!gemv_wmap(&wmap, w, N, K)) return VT_EARG;
+    gemv_kernel<MT, Epi><<<(int)g, GV_THREADS, smem, s>>>(a, wmap, M, N, K, sc, tickets, stages, pipe_timeout_ns(),
                                                           status, epi);
     return (int)cudaGetLastError();
 }
