@@ -306,8 +306,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const bool nok = n < P.N;
                 if (P.ksplit == 1) {
                     if (nok) {
-                        const float swn = P.sw[P.sw_rows ? n : 0];
-                        const float bn = P.bias ? t2f<T>(reinterpret_cast<const T *>(P.bias)[n]) : 0.f;
+                        // scales and bias only in dequant mode (they are NULL for int32 output)
+                        const float swn = P.s32_out ? 0.f : P.sw[P.sw_rows ? n : 0];
+                        const float bn = (!P.s32_out && P.bias) ? t2f<T>(reinterpret_cast<const T *>(P.bias)[n]) : 0.f;
                         #pragma unroll
                         for (int m = 0; m < BN; ++m) {
                             if (m >= P.M) continue;
@@ -338,8 +339,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     if (last) {
                         __threadfence();
                         if (nok) {
-                            const float swn = P.sw[P.sw_rows ? n : 0];
-                            const float bn = P.bias ? t2f<T>(reinterpret_cast<const T *>(P.bias)[n]) : 0.f;
+                            const float swn = P.s32_out ? 0.f : P.sw[P.sw_rows ? n : 0];
+                            const float bn =
+                                (!P.s32_out && P.bias) ? t2f<T>(reinterpret_cast<const T *>(P.bias)[n]) : 0.f;
                             #pragma unroll
                         for (int m = 0; m < BN; ++m) {
                             if (m >= P.M) continue;
