@@ -36,8 +36,21 @@ size_t w8a8_gemv_ws_bytes(int M, int N);
 int w8a8_gemv_ws(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out, int M,
                  int N, int K, int sa_rows, int sw_rows, int dtype, void *workspace, size_t ws_bytes, void *stream);
 
+/* w8a8_gemv for callers that cannot allocate device memory when they run it (inside a memory profiler or a custom
+ * allocator, or after handing all device memory to a pool): same arguments and results, but the split-K scratch is a
+ * fixed array compiled into the library (about 1 MiB per GPU that loads it, held until exit), so the call allocates
+ * nothing. Limits: M * N <= 262144 and N <= 262144, else VT_EARG. The first call on a device resolves the array's
+ * address and must come before any stream capture; calls sharing a device must not overlap on the GPU (they share
+ * the array). No counterpart in the reference (its GEMV needs no scratch). */
+int w8a8_gemv_noalloc(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out,
+                      int M, int N, int K, int sa_rows, int sw_rows, int dtype, void *stream);
+
 /* int32 accumulators acc[M, N] = a . w^T (bit-exact parity checks), M 1..16. New entry. */
 int vt_gemv_s32(const void *a, const void *w, void *acc, int M, int N, int K, void *stream);
+
+/* Non-zero 32-bit words in the first `bytes` of the current device's library workspace scratch (kernels leave it
+ * zeroed; a test hook). Synchronises the device; -1 on error. New entry. */
+long long vt_workspace_nonzero(long long bytes);
 
 /* Status word of the library workspace of the current device: 0, or the first device-side timeout code
  * (0x01xxxxxx pipeline, 0x02xxxxxx peer, 0x03xxxxxx cooperating CTA). Synchronises the device. */

@@ -25,13 +25,22 @@ def _s():
                                    (24, 5120, 2176), (32, 5120, 8704), (25, 7168, 5120), (32, 136, 128)])
 def test_small_s32(M, N, K):
     """decode orientation (weights as the A operand, split-K): M 9..32"""
+    L = _lib()
     a, w = rand_int8((M, K), M + K), rand_int8((N, K), N + 3 * K)
-    acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+    acc = torch.full((M, N), -7, dtype=torch.int32, device="cuda")
     ac, wc = a.cuda(), w.cuda()
-    assert _lib().vt_gemm_s32(ac.data_ptr(), wc.data_ptr(), acc.data_ptr(), M, N, K, _s()) == 0
+    nz0 = L.vt_workspace_nonzero(8 << 20)
+    assert L.vt_gemm_s32(ac.data_ptr(), wc.data_ptr(), acc.data_ptr(), M, N, K, _s()) == 0
     torch.cuda.synchronize()
-    assert np.array_equal(acc.cpu().numpy(), O.gemm_s32(a.numpy(), w.numpy()))
-    assert _lib().vt_status(1) == 0
+    got, ref = acc.cpu().numpy(), O.gemm_s32(a.numpy(), w.numpy())
+    if not np.array_equal(got, ref):
+        bad = np.argwhere(got != ref)
+        d = (got - ref)[got != ref]
+        raise AssertionError(
+            f"{len(bad)} mismatches; workspace non-zero before {nz0}, after {L.vt_workspace_nonzero(8 << 20)}; "
+            f"first {bad[:6].tolist()}; rows {np.unique(bad[:, 0]).tolist()[:12]}; n in [{bad[:, 1].min()}, "
+            f"{bad[:, 1].max()}]; unwritten (-7) {(got == -7).sum()}; diffs {d[:8].tolist()}; status {L.vt_status(0):#x}")
+    assert L.vt_status(1) == 0
 
 
 @pytest.mark.parametrize("M,N,K", [(33, 256, 128), (128, 5120, 3072), (200, 1000, 5136), (2048, 5120, 8704),

@@ -182,6 +182,94 @@ int vt_gemv_s32(const void *a, const void *w, void *acc, int M, int N, int K, vo
     return launch((const int8_t *)a, (const int8_t *)w, M, N, K, scratch, status, epi, s);
 }
 
+}  // extern "C"
+
+// ---- allocation-free GEMV ------------------------------------------------------------------------------------------
+// Some callers cannot allocate device memory at the moment they run a GEMV: code inside a custom allocator or memory
+// profiler (vLLM's memory profiling measures every allocation, so the kernel must not add any), processes that hand
+// all device memory to a pool before the first call, and code paths that run while another thread holds the
+// allocator. For them w8a8_gemv_noalloc takes its split-K scratch from a fixed array compiled into the library
+// instead of cudaMalloc: NOALLOC_INTS int32 words (1 MiB + 33 KiB), which every GPU that loads the library keeps
+// until the process exits. Its first call on a device resolves the array's device address (cudaGetSymbolAddress, with
+// that device current); make that first call before any stream capture. All calls on a device share the one array,
+// so calls that overlap on the GPU (different streams, or different host threads without ordering) race and produce
+// wrong results; order them on one stream.
+namespace vt {
+
+constexpr int NOALLOC_PARTIAL_INTS = 1 << 18;                     // int32 partial sums: M * N <= 262144
+constexpr int NOALLOC_TICKET_INTS = 8192;                         // one per 32-column row-block: N <= 262144
+constexpr int NOALLOC_INTS = 64 + NOALLOC_PARTIAL_INTS + NOALLOC_TICKET_INTS;   // 256-byte status header first
+static __device__ __align__(256) int g_noalloc_scratch[NOALLOC_INTS];
+
+static int *noalloc_scratch_ptr(int dev) {
+    static int *ptrs[VT_MAX_DEV] = {nullptr};
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        ptrs[dev] = reinterpret_cast<int *>(p);
+    }
+    return ptrs[dev];
+}
+
+}  // namespace vt
+
+extern "C" {
+
+// The w8a8_gemv contract (same arguments, same results) without any device allocation: scratch comes from the
+// library's fixed array. Rejects, with VT_EARG and before launching anything, M * N > 262144 or N > 262144 (the
+// array's capacity) as well as every shape w8a8_gemv rejects. The partial-sum region and tickets it uses are cleared
+// on the stream before the kernel runs (cudaMemsetAsync, no allocation), so a call never depends on the contents a
+// previous call left. The first call on each device must come before any stream capture (see above).
+int w8a8_gemv_noalloc(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out,
+                      int M, int N, int K, int sa_rows, int sw_rows, int dtype, void *stream) {
+    if (!gemv_args_ok(a, w, M, N, K)) return VT_EARG;
+    const long long nrb = (N + GV_RB - 1) / GV_RB;
+    if ((long long)M * N > NOALLOC_PARTIAL_INTS || nrb > NOALLOC_TICKET_INTS) return VT_EARG;
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    int *base = noalloc_scratch_ptr(dev);
+    if (!base) return (int)cudaErrorInvalidSymbol;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned *status = reinterpret_cast<unsigned *>(base);
+    int *partials = base + 64;
+    int *tickets = partials + (size_t)M * N;   // the layout the GEMV launcher expects: partials, then tickets
+    cudaError_t e = cudaMemsetAsync(partials, 0, ((size_t)M * N + (size_t)nrb) * sizeof(int), s);
+    if (e != cudaSuccess) return (int)e;
+    (void)tickets;
+    if (dtype == 0)
+        return gemv_dequant<__half>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, partials, status, s);
+    return gemv_dequant<__nv_bfloat16>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, partials, status, s);
+}
+
+// Number of non-zero 32-bit words in the first `bytes` of the current device's library workspace scratch (every
+// kernel that uses it leaves it zeroed; tests check that invariant). Synchronises the device; -1 on error.
+long long vt_workspace_nonzero(long long bytes) {
+    void *scratch;
+    unsigned *status;
+    if (bytes <= 0 || ws_acquire(0, 0, &scratch, &status) != 0) return -1;
+    const int dev = cur_device();
+    const size_t have = ws_table()[dev].bytes - 256;
+    if ((size_t)bytes > have) bytes = (long long)have;
+    const size_t n = (size_t)bytes / 4;
+    int *h = (int *)malloc(n * 4);
+    if (!h) return -1;
+    cudaDeviceSynchronize();
+    if (cudaMemcpy(h, scratch, n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        free(h);
+        cudaGetLastError();
+        return -1;
+    }
+    long long c = 0;
+    for (size_t i = 0; i < n; ++i) c += h[i] != 0;
+    free(h);
+    return c;
+}
+
 // Reads (and with clear != 0 resets) the library workspace status word of the current device: 0, or the first
 // timeout code a kernel reported (see common.cuh). Synchronises the device.
 unsigned vt_status(int clear) {
