@@ -1,14 +1,19 @@
 #!/usr/bin/env python3
 """Benchmark of the tensor-parallel W8A8 linear layer on B200 (one process per GPU).
 
-Workload (BASELINE.json config 1 at N = 1, the same layer tensor-parallel at N > 1, config 2's split): one "layer" =
-  gate_up : column-parallel W8A8 GEMV, M tokens, [5120 -> 34816 / N]  (w8a8_gemv_ws)
-  down    : row-parallel W8A8 GEMV, [17408 / N -> 5120] fused with the TP all-reduce, residual add, RMSNorm and per-token
-            int8 re-quantisation (vt_tp_row_linear; at N = 1 the "fused epilogue without collective")
+Workload (BASELINE.json config 1 at N = 1, the same layer tensor-parallel at N > 1, config 2's split): one "layer" is a
+decode MLP through the public API, each kernel's output feeding the next:
+  gate_up : column-parallel W8A8 linear, M tokens, [5120 -> 34816 / N] (vllm_turing::scaled_mm_, the cutlass_scaled_mm
+            replacement: the tcgen05 decode kernel)
+  silu    : SiLU(gate) * up and per-token int8 quantisation (silu_mul_quant)
+  down    : row-parallel W8A8 linear, [17408 / N -> 5120], fused with the TP all-reduce, residual add, RMSNorm and
+            per-token int8 re-quantisation (TPComm.row_linear -> vt_tp_row_linear; at N = 1 the "fused epilogue without
+            collective"), whose int8 output is the next layer's input
 One step = a 64-layer decode stack of such layers (the depth of config 4), every layer with its own weight buffers, so
-each step streams 64 x 267 MB / N of weights from HBM (inputs far larger than L2). M = 5 tokens (1 + 4 MTP drafts) by
-default. Strong scaling: the layer's total work is fixed, N ranks split it. Inputs: seeded synthetic tensors of the
-config's shapes and distributions (no checkpoint offline; the per-layer buffers are copies of a few generated sets).
+each step streams 64 x 267 MB / N of weights from HBM (inputs far larger than L2), captured once as a CUDA graph and
+replayed (as vLLM replays its captured decode forward). M = 5 tokens (1 + 4 MTP drafts) by default. Strong scaling:
+the layer's total work is fixed, N ranks split it. Inputs: seeded synthetic tensors of the config's shapes and
+distributions (no checkpoint offline; the per-layer buffers are copies of a few generated sets).
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
   torchrun --nproc-per-node N bench.py --gpus N ...
@@ -132,21 +137,21 @@ def layer_ops(M, world):
 
 # ---- CPU: the oracle restatement ------------------------------------------------------------------------------------
 def time_oracle_layer(M, threads, budget_s=12.0, max_steps=20):
-    """The same layer (TP1) on the host cores via the C oracle; returns (seconds per layer, steps, threads)."""
-    import numpy as np
-
+    """The same layer (TP1) on the host cores via the C oracle -- gate_up, silu_mul_quant, down + RMSNorm + quant, the
+    layer's output feeding the next step; returns (seconds per layer, steps, threads)."""
     from oracle import oracle as O
     from vllm_turing_b200.synthetic import make_layer_inputs
     O.set_threads(threads)
     gu = make_layer_inputs(M, 2 * INTER, HIDDEN, seed=1, rank=0, with_norm=False)
     dn = make_layer_inputs(M, HIDDEN, INTER, seed=0, rank=0)
-    a_gu, w_gu, sa_gu, sw_gu = gu.a.numpy(), gu.w.numpy(), gu.sa.numpy(), gu.sw.numpy()
-    args = ([dn.a.numpy()], [dn.w.numpy()], [dn.sa.numpy()], [dn.sw.numpy()])
-    res, nw = O.to_bits(dn.residual), O.to_bits(dn.norm_w)
+    w_gu, sw_gu, w_dn, sw_dn = gu.w.numpy(), gu.sw.numpy(), dn.w.numpy(), dn.sw.numpy()
+    nw = O.to_bits(dn.norm_w)
+    st = {"x": gu.a.numpy(), "xs": gu.sa.numpy(), "res": O.to_bits(dn.residual)}
 
     def step():
-        O.scaled_mm(a_gu, w_gu, sa_gu, sw_gu, None, 1)
-        O.row_linear_tp(*args, res, nw, 1e-6, 1)
+        h = O.scaled_mm(st["x"], w_gu, st["xs"], sw_gu, None, 1)
+        hq, hs = O.silu_mul_quant(h, 1)
+        st["res"], st["x"], st["xs"], _ = O.row_linear_tp([hq], [w_dn], [hs], [sw_dn], st["res"], nw, 1e-6, 1)
 
     step()
     n, t0 = 0, time.perf_counter()
@@ -154,7 +159,6 @@ def time_oracle_layer(M, threads, budget_s=12.0, max_steps=20):
         step()
         n += 1
     dt = (time.perf_counter() - t0) / n
-    del np
     return dt, n, threads
 
 
@@ -167,7 +171,8 @@ def run_reference(args):
     steps = max(1, min(args.steps, 20))
     dt, n, threads = time_oracle_layer(M, threads, budget_s=60.0, max_steps=steps)
     tops = layer_ops(M, 1) / dt / 1e12
-    sample = f"{n} full layers (M={M}, gate_up 5120->34816 + down 17408->5120 + all-reduce + RMSNorm + quant), TP1"
+    sample = (f"{n} full layers (M={M}, gate_up 5120->34816 + silu_mul_quant + down 17408->5120 + RMSNorm + "
+              f"quant), TP1")
     line = {
         "metric": METRIC, "value": tops, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus, "steps": n,
         "warmup": 1, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -182,6 +187,24 @@ def run_reference(args):
 
 
 # ---- GPU ------------------------------------------------------------------------------------------------------------
+def read_traffic():
+    """DRAM bytes per launch of the kernels, from the committed ncu summary profiles/traffic.txt (`key bytes` lines,
+    from `ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum`). Empty when absent."""
+    out = {}
+    try:
+        with open(os.path.join(HERE, "profiles", "traffic.txt")) as f:
+            for ln in f:
+                p = ln.split()
+                if len(p) >= 2 and not ln.startswith("#"):
+                    try:
+                        out[p[0]] = float(p[1])
+                    except ValueError:
+                        pass
+    except OSError:
+        pass
+    return out
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -191,7 +214,8 @@ def main():
 
     from vllm_turing_b200 import _build, w8a8
     from vllm_turing_b200.comm import TPComm
-    from vllm_turing_b200.synthetic import make_layer_inputs
+    from vllm_turing_b200.synthetic import make_layer_inputs, quant_per_token
+    from vllm_turing_b200.tailoverlap import silu_mul_quant
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -209,7 +233,7 @@ def main():
     else:
         dist.init_process_group("gloo", rank=0, world_size=1)
         gloo = dist.group.WORLD
-    L = _build.load()
+    _build.load()
     M = args.tokens
     NL = args.layers
     assert INTER % world == 0 and (2 * INTER) % world == 0
@@ -220,34 +244,40 @@ def main():
     for i in range(min(NL, 2)):
         gu = make_layer_inputs(M, N_gu, HIDDEN, seed=100 + i, rank=rank, with_norm=False)
         dn = make_layer_inputs(M, HIDDEN, K_dn, seed=i, rank=rank)
-        base.append(dict(gu_a=gu.a.to(dev), gu_w=gu.w.to(dev), gu_sa=gu.sa.to(dev), gu_sw=gu.sw.to(dev),
-                         dn_a=dn.a.to(dev), dn_w=dn.w.to(dev), dn_sa=dn.sa.to(dev), dn_sw=dn.sw.to(dev)))
+        base.append(dict(gu_w=gu.w.to(dev), gu_sw=gu.sw.to(dev).view(-1, 1),
+                         dn_w=dn.w.to(dev), dn_sw=dn.sw.to(dev).view(-1, 1)))
         if i == 0:
             residual0, norm_w = dn.residual.to(dev), dn.norm_w.to(dev)
-    sets = []
-    for i in range(NL):
-        b = base[i % len(base)]
-        sets.append({k: (v.clone() if k in ("gu_w", "dn_w") else v) for k, v in b.items()})
-    R = NL
-    comm = TPComm(gloo, dev)
-    out_gu = torch.empty(M, N_gu, dtype=torch.bfloat16, device=dev)
+    layers = [{k: v.clone() for k, v in base[i % len(base)].items()} for i in range(NL)]
+    del base
+    # the stack's input: one hidden state every rank holds (seeded independently of the rank), quantised per token
+    x0, xs0 = quant_per_token(torch.randn(M, HIDDEN, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16))
+    xs0 = xs0.view(M, 1)
+    x_q, x_s = x0.to(dev), xs0.to(dev)          # layer input, rewritten by every layer's down epilogue
     residual = residual0.clone()
-    q = torch.empty(M, HIDDEN, dtype=torch.int8, device=dev)
-    scales = torch.empty(M, 1, dtype=torch.float32, device=dev)
+    out_gu = torch.empty(M, N_gu, dtype=torch.bfloat16, device=dev)
+    h_q = torch.empty(M, K_dn, dtype=torch.int8, device=dev)
+    h_s = torch.empty(M, 1, dtype=torch.float32, device=dev)
+    comm = TPComm(gloo, dev)
     w8a8.workspace(dev, M, N_gu)
     stream = torch.cuda.current_stream()
 
+    # one decode MLP layer through the public API: vllm_turing::scaled_mm_ (the cutlass_scaled_mm replacement),
+    # silu_mul_quant, and the fused row-parallel tail (down GEMM + all-reduce + residual + RMSNorm + int8 quant, whose
+    # output is the next layer's input)
     def gate_up(s):
-        w8a8.gemv(out_gu, s["gu_a"], s["gu_w"].t(), s["gu_sa"], s["gu_sw"], None)
+        torch.ops.vllm_turing.scaled_mm_(out_gu, x_q, s["gu_w"].t(), x_s, s["gu_sw"], None)
+
+    def silu(s):
+        silu_mul_quant(out_gu, h_q, h_s)
 
     def down(s):
-        comm.row_linear(s["dn_a"], s["dn_w"], s["dn_sa"], s["dn_sw"], residual=residual, norm_w=norm_w, eps=1e-6,
-                        q=q, scales=scales)
+        comm.row_linear(h_q, s["dn_w"], h_s, s["dn_sw"], residual=residual, norm_w=norm_w, eps=1e-6, q=x_q, scales=x_s)
 
-    def step(i):
+    def run(fns, sets):
         for s in sets:
-            gate_up(s)
-            down(s)
+            for fn in fns:
+                fn(s)
 
     def barrier():
         torch.cuda.synchronize()
@@ -260,11 +290,11 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
+    LAYER = (gate_up, silu, down)
     K, W = args.steps, max(args.warmup, 1 if args.profile else 3)
-    if args.profile:
-        sets = sets[:2]
+    if args.profile:   # eager launches of two layers, for ncu launch lists and captures
         for i in range(W + K):
-            step(i)
+            run(LAYER, layers[:2])
         barrier()
         comm.check()
         if rank == 0:
@@ -273,101 +303,107 @@ def main():
         dist.destroy_process_group()
         return
 
-    # ---- timed region: K steps of the NL-layer stack; clocks sampled from warm-up (at least 1 s of the same load)
+    # eager warm-up (sets every kernel's one-time attributes), then one CUDA graph per timed region: the NL-layer step,
+    # and each kernel alone over the NL layers' buffers (the roofline's per-kernel durations)
+    for _ in range(2):
+        run(LAYER, layers)
+    barrier()
+    comm.check()
+
+    def capture(fns):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run(fns, layers)
+        return g
+
+    g_step = capture(LAYER)
+    g_k = {"gate_up": capture((gate_up,)), "silu": capture((silu,)), "down": capture((down,))}
+    barrier()
+
+    def timed(fn, n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / n) / 1e3
+
+    # ---- timed region: K replays of the NL-layer step; clocks sampled from a warm-up of at least 1 s of the same load
     # through the end of the timed region ----
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x_q.copy_(x0)
+    x_s.copy_(xs0)
+    residual.copy_(residual0)
     with ClockSampler(local) as clk:
         t_w = time.perf_counter()
         i = 0
         while i < W or time.perf_counter() - t_w < 1.0:
-            step(i)
+            g_step.replay()
             i += 1
             if i % 8 == 0:
                 torch.cuda.synchronize()
         barrier()
         comm.check()
-        e0.record(stream)
-        for i in range(K):
-            step(i)
-        e1.record(stream)
-        barrier()
+        t_step = timed(g_step.replay, K)                           # seconds per step, max over ranks
     W = max(W, i)
-    t_step = max_over_ranks(e0.elapsed_time(e1) / K) / 1e3          # seconds per step, max over ranks
     t_layer = t_step / NL
     comm.check()
 
-    # ---- per-kernel durations for the roofline: each kernel alone over the NL layers' buffers, K passes, CUDA events on
-    # the launching stream ----
-    def time_kernel(fn, passes):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        a.record(stream)
-        for _ in range(passes):
-            for s in sets:
-                fn(s)
-        b.record(stream)
-        barrier()
-        return max_over_ranks(a.elapsed_time(b) / (passes * NL)) / 1e3
-
     passes = max(1, min(K, 20))
-    t_gu = time_kernel(gate_up, passes)
-    t_dn = time_kernel(down, passes)
+    t_k = {k: timed(g.replay, passes) / NL for k, g in g_k.items()}
     comm.check()
-    gu_bytes = bytes_gu_w + M * HIDDEN + 2 * M * N_gu + 4 * (M + N_gu)
-    dn_bytes = bytes_dn_w + M * K_dn + 4 * (M + HIDDEN) + M * HIDDEN * (2 + 2 + 1) + 4 * M + 2 * HIDDEN
-    hbm, peak_kind = peaks()
-    dom = ("w8a8_gemv (gate_up)", t_gu, gu_bytes) if t_gu >= t_dn else ("tp_row_linear (down+AR+norm+quant)", t_dn,
-                                                                           dn_bytes)
-    achieved = dom[2] / dom[1] / 1e9
 
-    # ---- end to end through the public API with host buffers: every step copies the stack's inputs (the first
-    # layer's activations and scales, the residual) from pinned host memory and reads its outputs back ----
+    # the same step launched eagerly (no graph): host-side launch cost included
+    t_eager = timed(lambda: run(LAYER, layers), max(1, min(K, 10))) / NL
+    comm.check()
+
+    # ---- end to end with host buffers: each step copies the stack's inputs (layer 0's quantised hidden state and its
+    # scales, the residual) from pinned host memory, replays the captured public-API calls (as vLLM's decode replays its
+    # captured forward) and reads the outputs (next hidden state, scales, residual) back ----
     e2e = None
     if not args.no_e2e:
-        s0 = sets[0]
-        h_in = {k: s0[k].cpu().pin_memory() for k in ("gu_a", "gu_sa", "dn_a", "dn_sa")}
-        h_res = residual0.cpu().pin_memory()
-        h_q = torch.empty(M, HIDDEN, dtype=torch.int8).pin_memory()
-        h_s = torch.empty(M, 1, dtype=torch.float32).pin_memory()
-        h_r = torch.empty_like(h_res).pin_memory()
-        d_in = {k: torch.empty_like(v, device=dev) for k, v in h_in.items()}
-        h2d = sum(v.numel() * v.element_size() for v in h_in.values()) + h_res.numel() * 2
-        d2h = h_q.numel() + h_s.numel() * 4 + h_r.numel() * 2
-        first = dict(sets[0])
-        first.update(d_in)
+        h_x, h_xs, h_res = x0.pin_memory(), xs0.pin_memory(), residual0.cpu().pin_memory()
+        o_x, o_xs, o_res = (torch.empty_like(h_x).pin_memory(), torch.empty_like(h_xs).pin_memory(),
+                            torch.empty_like(h_res).pin_memory())
+        h2d = h_x.numel() + h_xs.numel() * 4 + h_res.numel() * 2
+        d2h = o_x.numel() + o_xs.numel() * 4 + o_res.numel() * 2
 
-        def e2e_step(i):
-            for k, v in h_in.items():
-                d_in[k].copy_(v, non_blocking=True)
+        def e2e_step():
+            x_q.copy_(h_x, non_blocking=True)
+            x_s.copy_(h_xs, non_blocking=True)
             residual.copy_(h_res, non_blocking=True)
-            for j, s in enumerate(sets):
-                s = first if j == 0 else s
-                gate_up(s)
-                down(s)
-            h_q.copy_(q, non_blocking=True)
-            h_s.copy_(scales, non_blocking=True)
-            h_r.copy_(residual, non_blocking=True)
+            g_step.replay()
+            o_x.copy_(x_q, non_blocking=True)
+            o_xs.copy_(x_s, non_blocking=True)
+            o_res.copy_(residual, non_blocking=True)
 
-        for i in range(args.warmup):
-            e2e_step(i)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        barrier()
-        a.record(stream)
-        for i in range(K):
-            e2e_step(i)
-        b.record(stream)
-        barrier()
-        t_e2e = max_over_ranks(a.elapsed_time(b) / K) / 1e3
+        for _ in range(W):
+            e2e_step()
+        t_e2e = timed(e2e_step, K)
         comm.check()
         e2e = {"value": layer_ops(M, world) * NL / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "us_per_layer": t_e2e / NL * 1e6,
-               "api": "w8a8.gemv + TPComm.row_linear over the stack, pinned host inputs / outputs copied every step"}
+               "api": "vllm_turing::scaled_mm_ + silu_mul_quant + TPComm.row_linear per layer, captured in a CUDA "
+                      "graph; pinned host inputs copied in and outputs read back every step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         dt, n, thr = time_oracle_layer(M, cpu_cores())
         cpu = {"value": layer_ops(M, 1) / dt / 1e12, "unit": "TOPS", "cores": thr, "kind": "port",
-               "sample": f"{n} full TP1 layers (M={M}) through the C oracle, OpenMP"}
+               "sample": f"{n} full TP1 layers (M={M}: gate_up + silu_mul_quant + down + RMSNorm + quant) through the "
+                         f"C oracle, OpenMP"}
+
+    # algorithmic HBM bytes per launch (one layer) of each kernel
+    alg = {"gate_up": bytes_gu_w + M * HIDDEN + 4 * M + 4 * N_gu + 2 * M * N_gu,
+           "silu": 2 * M * N_gu + M * K_dn + 4 * M,
+           "down": bytes_dn_w + M * K_dn + 4 * M + 4 * HIDDEN + M * HIDDEN * (2 + 2 + 1) + 4 * M + 2 * HIDDEN}
+    names = {"gate_up": "tc_gemm_kernel (gate_up, tcgen05 decode)", "silu": "silu_mul_quant_kernel",
+             "down": "tp_row_linear_tc_kernel (down + all-reduce + RMSNorm + quant)"}
+    dom = max(t_k, key=t_k.get)
+    hbm, peak_kind = peaks()
+    achieved = alg[dom] / t_k[dom] / 1e9
+    traffic = read_traffic().get(f"{dom}_tp{world}_m{M}")
 
     S = 2 * M * HIDDEN
     bus = (2.0 * (world - 1) / world * S / t_layer / 1e9) if world > 1 else 0.0
@@ -377,21 +413,23 @@ def main():
         "steps": K, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "us_per_layer": t_layer * 1e6, "bus_gbs": bus,
-        "config": {"workload": f"decode W8A8 MLP stack of {NL} layers, M={M}: gate_up 5120->34816 column-parallel + "
-                               f"down 17408->5120 row-parallel fused with TP all-reduce + RMSNorm + int8 quant "
-                               f"(BASELINE config 1 per layer at N=1, config 2 split at N>1)",
+        "config": {"workload": f"decode W8A8 MLP stack of {NL} layers, M={M}: gate_up 5120->34816 column-parallel, "
+                               f"silu_mul_quant, down 17408->5120 row-parallel fused with TP all-reduce + RMSNorm + "
+                               f"int8 quant (BASELINE config 1 per layer at N=1, config 2 split at N>1)",
                    "tokens": M, "layers": NL, "tp": world, "K_down_local": K_dn, "N_gate_up_local": N_gu,
                    "l2": f"inputs larger than L2: {NL} layers with their own weights, "
                          f"{NL * (bytes_gu_w + bytes_dn_w) / 2**20:.0f} MiB of weights per step",
-                   "parallelism": f"tp{world}"},
-        "kernel_us": {"w8a8_gemv_gate_up": t_gu * 1e6, "tp_row_linear_down": t_dn * 1e6},
-        "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                     "frac": achieved / hbm, "traffic": None, "bytes_per_launch": dom[2],
+                   "launch": "CUDA graph of the step, replayed K times", "parallelism": f"tp{world}"},
+        "kernel_us": {k: v * 1e6 for k, v in t_k.items()},
+        "eager_us_per_layer": t_eager * 1e6,
+        "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "traffic": traffic, "bytes_per_launch": alg[dom],
                      "peak_kind": peak_kind},
-        "clocks": clocks, "gpu_launches": 2 * NL * K, "e2e": e2e, "cpu_baseline": cpu,
+        "clocks": clocks, "gpu_launches": 3 * NL * K, "e2e": e2e, "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
+    del g_step, g_k
     comm.close()
     dist.destroy_process_group()
 

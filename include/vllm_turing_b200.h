@@ -48,6 +48,27 @@ int w8a8_gemv_noalloc(const void *a, const void *w, const void *sa, const void *
 /* int32 accumulators acc[M, N] = a . w^T (bit-exact parity checks), M 1..16. New entry. */
 int vt_gemv_s32(const void *a, const void *w, void *acc, int M, int N, int K, void *stream);
 
+/* Small-M tensor-core GEMM, M 1..32 (the default decode path): tcgen05 kind::i8 with the weights as the MMA's A
+ * operand and stream-K over the SMs; split-K scratch from the library's per-device workspace (grown outside stream
+ * capture only). Replaces vllm_turing/csrc/w8a8_gemv.cu:330-344 (w8a8_mma: same signature and return convention). */
+int w8a8_mma(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out, int M, int N,
+             int K, int sa_rows, int sw_rows, int dtype, void *stream);
+/* w8a8_mma with a caller-owned workspace of w8a8_mma_ws_bytes(M, N) bytes (256-byte aligned, zeroed before first
+ * use; the kernel leaves it zeroed; calls sharing it must be stream-ordered). No counterpart in the reference (its
+ * MMA kernel needs no scratch). */
+size_t w8a8_mma_ws_bytes(int M, int N);
+int w8a8_mma_ws(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out, int M,
+                int N, int K, int sa_rows, int sw_rows, int dtype, void *workspace, size_t ws_bytes, void *stream);
+
+/* Prefill GEMM (tcgen05 kind::i8, 128 x 256 tiles): A [M, K], W [N, K] int8, sa [M], sw [N] float32, out [M, N],
+ * dequant order sa[m] * (sw[n] * acc). Returns 0 ok, 1 cannot implement (shape / alignment), 3 launch failed.
+ * Replaces vllm_turing/csrc/w8a8_big.cu:66-73 (w8a8_big: same signature and return convention). */
+int w8a8_big(const void *A, const void *W, const void *sa, const void *sw, void *out, int M, int N, int K, int dtype,
+             void *stream);
+
+/* int32 accumulators acc[M, N] = a . w^T on the tensor cores, any M (decode orientation for M <= 32). New entry. */
+int vt_gemm_s32(const void *a, const void *w, void *acc, int M, int N, int K, void *stream);
+
 /* Non-zero 32-bit words in the first `bytes` of the current device's library workspace scratch (kernels leave it
  * zeroed; a test hook). Synchronises the device; -1 on error. New entry. */
 long long vt_workspace_nonzero(long long bytes);
@@ -116,9 +137,10 @@ int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype,
  * slots. m % 8 == 0 (LL) or m % 16 == 0 (bulk). Replaces dag_all_gather (dma_ag.cu:45-74) for N ranks over P2P. */
 int vt_all_gather(void *comm, void *gathered, long long m, void *stream);
 
-/* The fused row-parallel layer tail, one kernel: this rank's W8A8 GEMV partial -> all-reduce over the communicator
- * -> residual add (in place) -> RMSNorm * norm_w -> per-token int8 q / scales. residual = NULL: plain row-linear +
- * all-reduce into `reduced`. 1 <= M <= 16, N % 4 == 0, K % 16 == 0, M * N * 2 <= ll_data. Replaces the reference's
+/* The fused row-parallel layer tail, one kernel: this rank's W8A8 GEMM partial (tcgen05; the dp4a GEMV for M <= 16
+ * with VLLM_TURING_FUSED_GEMV=1) -> all-reduce over the communicator -> residual add (in place) -> RMSNorm * norm_w
+ * -> per-token int8 q / scales. residual = NULL: plain row-linear + all-reduce into `reduced`. 1 <= M <= 32,
+ * N % 4 == 0, K % 16 == 0, M * N * 2 <= ll_data, M * N <= scratch_ints. Replaces the reference's
  * decode tail: scaled_mm_ (w8a8.py:235-244) -> tensor_model_parallel_all_reduce (hostar.py:260-278) ->
  * rms_norm_dynamic_per_token_quant (tailoverlap.py:200). */
 int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,

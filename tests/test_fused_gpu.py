@@ -33,7 +33,7 @@ def _inputs(M, N, K, seed=0):
 
 
 @pytest.mark.parametrize("M,N,K", [(5, 5120, 17408), (1, 5120, 2176), (8, 5120, 4352), (3, 1024, 512),
-                                   (16, 5120, 8704)])
+                                   (16, 5120, 8704), (24, 5120, 17408), (32, 5120, 2176), (17, 1024, 5136)])
 def test_fused_tp1_vs_oracle(comm1, M, N, K):
     li = _inputs(M, N, K, seed=M + K)
     res = li.residual.cuda()

@@ -82,3 +82,31 @@ def test_silu_mul_quant_reference_abi():
         assert q_off(q.cpu().numpy(), qo) <= 1 and (q.cpu().numpy() != qo).mean() < 1e-3
         assert np.max(np.abs(s.cpu().numpy() - so) / np.maximum(so, 1e-12)) < 1e-3
         assert s[0].item() == 0.0 and not q[0].any().item()
+
+
+@pytest.mark.parametrize("M,I", [(1, 17408), (5, 17408), (5, 2176), (24, 8704), (64, 136), (100, 4352)])
+def test_silu_mul_quant_bf16_row_split(M, I):
+    """bf16 SiLU-mul-quant at decode shapes (rows split over several CTAs, the row absmax combined across them) and
+    at 100 rows (a CTA per row); ten back-to-back calls with different inputs and no host sync in between check that
+    the per-row slots and counters are left reset for the next call."""
+    from vllm_turing_b200 import _build
+    L = _build.load()
+    ins, outs = [], []
+    for rep in range(10):
+        gu = (torch.randn(M, 2 * I, generator=torch.Generator().manual_seed(31 * rep + M + I)) * 3).to(torch.bfloat16)
+        if rep == 3:
+            gu[M - 1, :I] = 0   # an all-zero SiLU row: scale 0, q 0
+        q = torch.empty(M, I, dtype=torch.int8, device="cuda")
+        s = torch.empty(M, dtype=torch.float32, device="cuda")
+        g = gu.cuda()
+        assert L.vt_silu_mul_quant(g.data_ptr(), q.data_ptr(), s.data_ptr(), M, I, 1,
+                                   torch.cuda.current_stream().cuda_stream) == 0
+        ins.append((gu, g))
+        outs.append((q, s))
+    torch.cuda.synchronize()
+    for (gu, _), (q, s) in zip(ins, outs):
+        qo, so = O.silu_mul_quant(O.to_bits(gu), 1)
+        assert q_off(q.cpu().numpy(), qo) <= 1 and (q.cpu().numpy() != qo).mean() < 1e-3
+        assert np.max(np.abs(s.cpu().numpy() - so) / np.maximum(so, 1e-12)) < 1e-3
+    assert outs[3][1][M - 1].item() == 0.0 and not outs[3][0][M - 1].any().item()
+    assert L.vt_status(1) == 0

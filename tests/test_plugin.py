@@ -67,12 +67,14 @@ def test_gemv_ok_predicates():
     w = torch.zeros(N, K, dtype=torch.int8)
     sa, sb = torch.ones(M, 1), torch.ones(N, 1)
     out = torch.empty(M, N, dtype=torch.bfloat16)
-    assert w8a8.gemv_ok(out, a, w.t(), sa, sb, None)
-    assert not w8a8.gemv_ok(out, a, w, sa, sb, None)                     # not the transposed view
-    assert not w8a8.gemv_ok(out, a[:, :120].contiguous(), w[:, :120].contiguous().t(), sa, sb, None) or True
+    def ok(*t):
+        return w8a8.gemv_ok(*t, max_m=8)
+    assert ok(out, a, w.t(), sa, sb, None)
+    assert not ok(out, a, w, sa, sb, None)                               # not the transposed view
     a9 = torch.zeros(9, K, dtype=torch.int8)
-    assert not w8a8.gemv_ok(torch.empty(9, N, dtype=torch.bfloat16), a9, w.t(), torch.ones(9, 1), sb, None)
-    assert not w8a8.gemv_ok(out.float(), a, w.t(), sa, sb, None)         # fp32 output not served
+    assert not ok(torch.empty(9, N, dtype=torch.bfloat16), a9, w.t(), torch.ones(9, 1), sb, None)
+    assert not ok(out.float(), a, w.t(), sa, sb, None)                   # fp32 output not served
+    assert w8a8.gemv_ok(out, a, w.t(), sa, sb, None) == (w8a8.MAX_M >= M)  # the GEMV is off by default
 
 
 def test_chunk_bounds_match_reference_formula():

@@ -21,10 +21,12 @@ def _s():
     return torch.cuda.current_stream().cuda_stream
 
 
-@pytest.mark.parametrize("M,N,K", [(9, 5120, 5136), (13, 1000, 5136), (16, 5120, 17408), (17, 300, 5168),
-                                   (24, 5120, 2176), (32, 5120, 8704), (25, 7168, 5120), (32, 136, 128)])
+@pytest.mark.parametrize("M,N,K", [(1, 128, 16), (5, 34816, 5120), (5, 5120, 17408), (9, 5120, 5136),
+                                   (13, 1000, 5136), (16, 5120, 17408), (17, 300, 5168), (24, 5120, 2176),
+                                   (32, 5120, 8704), (25, 7168, 5120), (32, 136, 128), (3, 40, 65536)])
 def test_small_s32(M, N, K):
-    """decode orientation (weights as the A operand, split-K): M 9..32"""
+    """decode orientation (weights as the A operand, stream-K over the SMs): M 1..32; single-tile and single-K-block
+    cases, tiles split across several CTAs, CTAs spanning several tiles, K not a multiple of the 128-byte block"""
     L = _lib()
     a, w = rand_int8((M, K), M + K), rand_int8((N, K), N + 3 * K)
     acc = torch.full((M, N), -7, dtype=torch.int32, device="cuda")
@@ -93,14 +95,14 @@ def test_mma_dequant_bit_exact(dtype, M, N, K, bias, per_row):
 
 
 def test_dispatch_through_scaled_mm_op():
-    """vllm_turing::scaled_mm_ picks the GEMV (M <= 8), the small-M tensor-core kernel (M <= 32) and the prefill
-    kernel (larger M), as vllm_turing/w8a8.py:235-244 does."""
+    """vllm_turing::scaled_mm_ picks the GEMV (M <= VLLM_TURING_GEMV_MAX_M, off by default), the small-M tensor-core
+    kernel (M <= 32) and the prefill kernel (larger M), as vllm_turing/w8a8.py:235-244 does."""
     from vllm_turing_b200 import w8a8
     N, K = 5120, 8704
     w = rand_int8((N, K), 1)
     wc = w.cuda()
     sw = rand_scales(N, 2, 1e-3)
-    for M, path in ((5, "gemv"), (24, "mma"), (512, "big")):
+    for M, path in ((5, "gemv" if w8a8.MAX_M >= 5 else "mma"), (24, "mma"), (512, "big")):
         a = rand_int8((M, K), 3 + M)
         sa = rand_scales(M, 4, 1e-2)
         out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")

@@ -1,0 +1,68 @@
+"""The kernel variants chosen by environment switches that are read once per process -- the fused row-linear's dp4a
+GEMV phase (VLLM_TURING_FUSED_GEMV=1) and the tcgen05 decode kernel's K blocks per pipeline stage
+(VLLM_TURING_TC_KBS = 1 or 2; 4 is the default the other tests run) -- each checked in a child process against the
+oracle: int32 accumulators and the fused layer's reduced sum and residual bit-exact, int8 within 1 LSB."""
+import os
+import subprocess
+import sys
+
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def child():
+    """Runs in the child process: decode GEMMs through vt_gemm_s32 and the fused layer at world size 1."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from tests.helpers import assert_bits_equal, q_off, rand_int8
+    from vllm_turing_b200 import _build
+    from vllm_turing_b200.comm import TPComm
+    from vllm_turing_b200.synthetic import make_layer_inputs
+
+    L = _build.load()
+    s = torch.cuda.current_stream().cuda_stream
+    for M, N, K in ((5, 34816, 5120), (16, 5120, 17408), (32, 1000, 5136), (1, 136, 128)):
+        a, w = rand_int8((M, K), M + 1), rand_int8((N, K), N + 2)
+        ac, wc = a.cuda(), w.cuda()   # kept alive until the kernel has run
+        acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
+        assert L.vt_gemm_s32(ac.data_ptr(), wc.data_ptr(), acc.data_ptr(), M, N, K, s) == 0
+        torch.cuda.synchronize()
+        assert np.array_equal(acc.cpu().numpy(), O.gemm_s32(a.numpy(), w.numpy())), (M, N, K)
+    assert L.vt_status(1) == 0
+    assert L.vt_workspace_nonzero(8 << 20) == 0
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=os.environ.get("VT_TEST_PORT", "29631"))
+    dist.init_process_group("gloo", rank=0, world_size=1)
+    torch.cuda.set_device(0)
+    comm = TPComm(dist.group.WORLD, torch.device("cuda", 0))
+    for M, N, K in ((5, 5120, 17408), (16, 5120, 8704), (1, 1024, 512)):
+        li = make_layer_inputs(M, N, K, seed=M + K, rank=0)
+        res = li.residual.cuda()
+        red = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        q, sc = comm.row_linear(li.a.cuda(), li.w.cuda(), li.sa.cuda(), li.sw.cuda(), residual=res,
+                                norm_w=li.norm_w.cuda(), eps=li.eps, reduced=red)
+        torch.cuda.synchronize()
+        comm.check()
+        ro, qo, so, redo = O.row_linear_tp([li.a.numpy()], [li.w.numpy()], [li.sa.numpy()], [li.sw.numpy()],
+                                           O.to_bits(li.residual), O.to_bits(li.norm_w), li.eps, 1)
+        assert_bits_equal(red, redo, f"reduced M={M}")
+        assert_bits_equal(res, ro, f"residual M={M}")
+        assert q_off(q.cpu().numpy(), qo) <= 1
+    comm.close()
+    dist.destroy_process_group()
+    print("CHILD OK")
+
+
+@pytest.mark.parametrize("env", [{"VLLM_TURING_FUSED_GEMV": "1"}, {"VLLM_TURING_TC_KBS": "1"},
+                                 {"VLLM_TURING_TC_KBS": "2"}], ids=["fused_gemv", "kbs1", "kbs2"])
+def test_variant_in_child(env):
+    e = dict(os.environ, **env)
+    r = subprocess.run([sys.executable, "-c", "import tests.test_variants_gpu as t; t.child()"], cwd=ROOT, env=e,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "CHILD OK" in r.stdout, (r.stdout[-2000:], r.stderr[-4000:])

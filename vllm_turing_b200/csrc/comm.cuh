@@ -4,7 +4,8 @@
 // peer's region (ce_open). All ranks use the identical layout:
 //
 //   [0, CTRL)            control: seq (u32 @0, the last completed call), done ticket (u32 @64), status (u32 @128),
-//                        group mailbox (u64 [32 rows][16 groups][2] @4096), GEMV tickets (int [4096] @16384)
+//                        group mailbox (u64 [32 rows][16 groups][2] @4096), split-K tickets of the fused
+//                        GEMM (int [4096] @16384: GEMV row-blocks or tcgen05 tiles)
 //   LL                   LL receive slots [parity 2][src rank][ll_slot bytes]: peers push 16-byte LL words here
 //   SCRATCH              int32 split-K partial sums of the fused GEMV [ll rows][N] (local use only)
 //   RS                   two-shot reduce-scatter receive buffers [parity 2][src rank][chunk_cap bytes]
@@ -30,6 +31,7 @@ constexpr int COMM_MAX_CTAS = 256;
 constexpr size_t COMM_CTRL = 65536;
 constexpr size_t COMM_MBOX_OFF = 4096;
 constexpr size_t COMM_TICKET_OFF = 16384;
+constexpr int COMM_TICKETS = 4096;
 constexpr int COMM_MBOX_ROWS = 32, COMM_MBOX_GROUPS = 16;
 
 struct CommLayout {

@@ -1,4 +1,5 @@
-// Row-wise epilogue kernels for B200 (sm_100a), one CTA per token row, HBM-bound:
+// Row-wise epilogue kernels for B200 (sm_100a), HBM-bound; one CTA per token row, except silu_mul_quant for a few
+// rows (decode), which splits each row over several CTAs so the whole GPU shares the work:
 //   vt_scaled_int8_quant  per-token dynamic symmetric int8 quantisation   (vllm_turing/quantfuse.py:18-24)
 //   vt_rms_norm_quant     residual add + RMSNorm + per-token int8 quant   (the call at vllm_turing/tailoverlap.py:200,
 //                         arithmetic of tests/test_quantfuse.py:45-48 + quantfuse.py:18-24)
@@ -141,9 +142,97 @@ __global__ void __launch_bounds__(RQ_THREADS) silu_mul_quant_kernel(const T *__r
     for (int i = threadIdx.x; i < I; i += blockDim.x) q[row * I + i] = quant1(abuf[i], inv);
 }
 
+// Row-split variant for few rows: CTA (m, g) of an M x E grid computes the SiLU products of the g-th 1/E slice of
+// row m, then the row's absmax is combined across its E CTAs through a per-row slot in device memory (atomicMax of
+// the float's bits: the values are non-negative, so the order of arrival does not matter and the result is
+// deterministic) and an arrival counter; each CTA then quantises its own slice. The last CTA of a row to leave resets
+// the row's slot and counters, so the next (stream-ordered) call starts from zero. Calls that overlap on the GPU
+// would share the slots: they must be stream-ordered (as every decode step is). The wait for the row's other CTAs
+// is bounded; a timeout lands in the library status word.
+constexpr int SQ_THREADS = 256;
+constexpr int SQ_ROWS = 64;   // rows the split path serves
+static __device__ unsigned g_sq_amax[SQ_ROWS], g_sq_arrive[SQ_ROWS], g_sq_leave[SQ_ROWS];
+
+template <typename T>
+__global__ void __launch_bounds__(SQ_THREADS)
+    silu_mul_quant_split_kernel(const T *__restrict__ gu, int8_t *__restrict__ q, float *__restrict__ scales, int I,
+                                int E, uint64_t timeout_ns, unsigned *status) {
+    extern __shared__ float pbuf[];
+    __shared__ float red[32];
+    __shared__ float s_amax;
+    const int m = blockIdx.x / E, g = blockIdx.x - m * E;
+    const int i0 = (int)((long long)I * g / E), i1 = (int)((long long)I * (g + 1) / E);
+    const T *gr = gu + (size_t)m * 2 * I;
+    const T *ur = gr + I;
+    float amax = 0.0f;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const float gf = t2f<T>(gr[i]);
+        const float sg = rnd<T>(__fdiv_rn(gf, 1.0f + expf(-gf)));
+        const float p = rnd<T>(__fmul_rn(sg, t2f<T>(ur[i])));
+        pbuf[i - i0] = p;
+        amax = fmaxf(amax, fabsf(p));
+    }
+    amax = block_max(amax, red);
+    if (threadIdx.x == 0) {
+        atomicMax(&g_sq_amax[m], __float_as_uint(amax));
+        __threadfence();
+        atomicAdd(&g_sq_arrive[m], 1u);
+        const uint64_t deadline = globaltimer() + timeout_ns;
+        uint32_t it = 0;
+        while (atomicAdd(&g_sq_arrive[m], 0u) < (unsigned)E) {
+            if ((++it & 63u) == 0 && globaltimer() > deadline) {
+                report(status, ST_GROUP_TIMEOUT | 0x800000u | (unsigned)m);
+                break;
+            }
+        }
+        __threadfence();
+        s_amax = __uint_as_float(atomicAdd(&g_sq_amax[m], 0u));
+        if (atomicAdd(&g_sq_leave[m], 1u) == (unsigned)E - 1u) {   // every CTA of the row has read the slot
+            g_sq_amax[m] = 0u;
+            g_sq_arrive[m] = 0u;
+            g_sq_leave[m] = 0u;
+            __threadfence();
+        }
+    }
+    __syncthreads();
+    amax = s_amax;
+    const float inv = quant_inv(amax);
+    if (g == 0 && threadIdx.x == 0) scales[m] = __fdiv_rn(amax, 127.0f);
+    int8_t *qr = q + (size_t)m * I;
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) qr[i] = quant1(pbuf[i - i0], inv);
+}
+
 static int smem_attr(const void *fn, int bytes) {
     if (bytes <= 48 * 1024) return 0;
     return (int)cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// Few rows: the row-split kernel on up to one CTA per SM (at least 256 elements per CTA); many rows: a CTA per row.
+template <typename T>
+static int launch_silu(const void *gu, void *q, void *scales, int M, int I, cudaStream_t s) {
+    const int dev = cur_device();
+    const int sms = num_sms(dev);
+    int E = sms / M;
+    const int E_max = (I + 255) / 256;
+    if (E > E_max) E = E_max;
+    if (M <= SQ_ROWS && E >= 2) {
+        const int chunk = (I + E - 1) / E;
+        static bool attr[VT_MAX_DEV] = {false};
+        if (dev >= 0 && dev < VT_MAX_DEV && !attr[dev]) {
+            if (int rc = smem_attr((const void *)silu_mul_quant_split_kernel<T>, 49152 * 2)) return rc;
+            attr[dev] = true;
+        }
+        void *scratch = nullptr;
+        unsigned *status = nullptr;
+        if (ws_acquire(0, s, &scratch, &status) != 0) status = nullptr;   // timeouts reported only with a workspace
+        silu_mul_quant_split_kernel<T><<<M * E, SQ_THREADS, chunk * 4, s>>>((const T *)gu, (int8_t *)q,
+                                                                             (float *)scales, I, E, pipe_timeout_ns(),
+                                                                             status);
+        return (int)cudaGetLastError();
+    }
+    if (int rc = smem_attr((const void *)silu_mul_quant_kernel<T>, I * 4)) return rc;
+    silu_mul_quant_kernel<T><<<M, RQ_THREADS, I * 4, s>>>((const T *)gu, (int8_t *)q, (float *)scales, I);
+    return (int)cudaGetLastError();
 }
 
 }  // namespace vt
@@ -192,24 +281,17 @@ int vt_rms_norm_quant(const void *x, void *residual, const void *weight, float e
 // The reference's ABI (vllm_turing/csrc/silu_quant.cu:71-77): gate_up (M, 2I) fp16 -> q (M, I) int8, scales (M).
 // Returns 1 on bad arguments, 2 on a launch error.
 int silu_mul_quant(const void *gu, void *q, void *scales, int M, int I, void *stream) {
-    if (I <= 0 || I > 49152) return 1;
+    if (I <= 0 || I > 49152 || M < 0) return 1;
     if (M == 0) return 0;
-    cudaStream_t s = (cudaStream_t)stream;
-    if (smem_attr((const void *)silu_mul_quant_kernel<__half>, I * 4)) return 2;
-    silu_mul_quant_kernel<__half><<<M, RQ_THREADS, I * 4, s>>>((const __half *)gu, (int8_t *)q, (float *)scales, I);
-    return cudaGetLastError() == cudaSuccess ? 0 : 2;
+    return launch_silu<__half>(gu, q, scales, M, I, (cudaStream_t)stream) == 0 ? 0 : 2;
 }
 
 // bf16 variant of silu_mul_quant (dtype 0 fp16 / 1 bf16).
 int vt_silu_mul_quant(const void *gu, void *q, void *scales, int M, int I, int dtype, void *stream) {
     if (dtype == 0) return silu_mul_quant(gu, q, scales, M, I, stream);
-    if (I <= 0 || I > 49152) return VT_EARG;
+    if (I <= 0 || I > 49152 || M < 0) return VT_EARG;
     if (M == 0) return 0;
-    cudaStream_t s = (cudaStream_t)stream;
-    if (int rc = smem_attr((const void *)silu_mul_quant_kernel<__nv_bfloat16>, I * 4)) return rc;
-    silu_mul_quant_kernel<__nv_bfloat16><<<M, RQ_THREADS, I * 4, s>>>((const __nv_bfloat16 *)gu, (int8_t *)q,
-                                                                      (float *)scales, I);
-    return (int)cudaGetLastError();
+    return launch_silu<__nv_bfloat16>(gu, q, scales, M, I, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -1,0 +1,498 @@
+// The tcgen05 kind::i8 GEMM core shared by the W8A8 GEMMs (w8a8_tc.cu) and the fused tensor-parallel row-linear
+// (tp_fused.cu): int32 accumulators in tensor memory (TMEM), operands staged by TMA (cp.async.bulk.tensor, 128-byte
+// swizzle, no multicast).
+//
+//   D[rows, cols] = A[rows, K] . B[cols, K]^T   (both K-major int8)
+//
+// Two orientations:
+//   prefill (SWAP = false): A = activations (128-row tiles of M), B = weights (BN-row tiles of N). Whole tiles are
+//            dealt round robin to the CTAs; the epilogue thread is a token row m, its columns are output features n.
+//   decode  (SWAP = true):  A = weights (128-row tiles of N), B = a few token rows (BN = 16 or 32). Stream-K: the
+//            (tile, K block) index space is cut into one contiguous range per CTA, so every SM streams the same number
+//            of weight bytes (+-1 K block of 16 KB). A CTA's range falls into "pieces" (one tile, a K-block range).
+//            A piece that covers its whole tile is finished in registers; otherwise the piece's int32 partial sums are
+//            added into a zeroed scratch [M, N] (atomicAdd: exact), and the CTA whose K blocks complete the tile's
+//            ticket reads the sums back, returns the scratch and the ticket to zero and hands the accumulators to the
+//            caller's finisher `fin(P, n, n_ok, acc[BN])` (thread = output feature n, acc[m] for token rows m).
+//
+// CTA = 6 warps: warp 0 issues TMA loads into a ring of shared-memory stages (KBS K blocks of 128 bytes per stage, so
+// one barrier round trip moves KBS x 16 KB of weights), warp 1 allocates TMEM and one of its threads issues the MMAs
+// (128 x BN x 32 each, 4 per K block) and commits their completion to mbarriers, warps 2..5 drain TMEM (tcgen05.ld;
+// warp w may read TMEM lanes 32 (w % 4) .. + 31). TMEM holds two accumulator buffers so the epilogue of one piece
+// overlaps the MMAs of the next. Every wait is bounded (globaltimer): on a timeout the CTA records the status, stops
+// issuing, waits (bounded) for the copies and MMAs it already issued, frees its TMEM and returns.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdlib.h>
+
+#include "common.cuh"
+#include "host_util.h"
+#include "tma_host.h"
+
+namespace vt {
+
+constexpr int TC_THREADS = 192;
+constexpr int TC_BK = 128;        // bytes of K per K block (= one 128-byte swizzle row)
+constexpr int TC_BM = 128;        // MMA M (rows of operand A per tile)
+constexpr int TC_EPI_BAR = 1;     // named barrier of the four epilogue warps
+constexpr int TC_EPI_LEAD = 64;   // thread that takes the split-K tickets (warp 2, lane 0)
+
+// ---- tcgen05 primitives (PTX ISA 8.6+, sm_100a) -------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+                 "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D (TMEM) (+)= A (smem desc) . B (smem desc)^T, kind::i8, int32 accumulate
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// arrive on `bar` once every tcgen05 operation this thread issued before has completed
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+// 32 TMEM lanes x 32 (16) consecutive 32-bit columns; thread i of the warp receives lane (base lane + i)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor of a K-major operand tile written by TMA with 128-byte swizzle: rows of 128 bytes,
+// 8-row swizzle atoms 1024 bytes apart (stride byte offset), sm100 descriptor version 1, layout SWIZZLE_128B.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;                      // leading byte offset: unused for swizzled K-major
+    d |= (uint64_t)((1024u >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1u << 46;                      // descriptor version (sm100)
+    d |= (uint64_t)2u << 61;                      // SWIZZLE_128B
+    return d;
+}
+// Instruction descriptor, kind::i8: int32 accumulator, signed A and B, both K-major, MMA M x N.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---- work description ------------------------------------------------------------------------------------------------
+struct TcArgs {
+    int n_tiles_a, n_tiles_b;   // tiles along A rows (128) and B rows (BN)
+    int nkb;                    // K blocks of 128 bytes per tile
+    int units;                  // prefill: tiles (n_tiles_a * n_tiles_b); decode: K blocks of all tiles (n_tiles_a * nkb)
+    int stream_k;               // 1: decode stream-K ranges; 0: whole tiles round robin
+    const float *sa, *sw;       // per token, per output feature (NULL in int32 mode)
+    const void *bias;           // [N] output dtype or NULL
+    int sa_rows, sw_rows;       // 1: per row / feature, 0: one value
+    void *out;                  // [M, N] row-major
+    int M, N;                   // tokens, output features
+    int *scratch, *tickets;     // stream-K: int32 [M, N] and one ticket per tile, zero between calls
+    int s32_out;                // write int32 accumulators instead of dequantised values
+    int stages;
+    uint64_t timeout_ns;
+    unsigned *status;
+};
+
+template <int BN, int KBS> struct TcLayout {
+    static constexpr int A_BYTES = TC_BM * TC_BK;   // one K block of operand A
+    static constexpr int B_BYTES = BN * TC_BK;      // one K block of operand B
+    static constexpr int KB_BYTES = A_BYTES + B_BYTES;
+    static constexpr int STAGE = KBS * KB_BYTES;    // stage = [KBS A blocks][KBS B blocks]
+    static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+    static constexpr int BAR_BYTES = 512;           // mbarriers, TMEM slot and flags after the stages
+};
+
+// The CTA's pieces: (A tile, B tile, K-block range). Identical sequence in every role of the CTA.
+struct TcPieces {
+    int idx, hi;
+    __device__ __forceinline__ explicit TcPieces(const TcArgs &P) {
+        if (P.stream_k) {
+            idx = (int)((long long)P.units * blockIdx.x / gridDim.x);
+            hi = (int)((long long)P.units * (blockIdx.x + 1) / gridDim.x);
+        } else {
+            idx = blockIdx.x;
+            hi = P.units;
+        }
+    }
+    __device__ __forceinline__ bool next(const TcArgs &P, int &ta, int &tb, int &kb0, int &kb1) {
+        if (idx >= hi) return false;
+        int tile;
+        if (P.stream_k) {
+            tile = idx / P.nkb;
+            kb0 = idx - tile * P.nkb;
+            kb1 = min(P.nkb, kb0 + (hi - idx));
+            idx += kb1 - kb0;
+        } else {
+            tile = idx;
+            kb0 = 0;
+            kb1 = P.nkb;
+            idx += gridDim.x;
+        }
+        ta = tile % P.n_tiles_a;
+        tb = tile / P.n_tiles_a;
+        return true;
+    }
+};
+
+__device__ __forceinline__ unsigned char *tc_align1024(unsigned char *p) {
+    return reinterpret_cast<unsigned char *>(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
+}
+
+// Output finisher of the decode orientation: thread = output feature n, acc[m] for the token rows.
+template <typename T, int BN>
+struct TcOutEpi {
+    __device__ __forceinline__ void operator()(const TcArgs &P, int n, bool nok, const int (&acc)[BN]) const {
+        if (!nok) return;
+        if (P.s32_out) {
+#pragma unroll
+            for (int m = 0; m < BN; ++m)
+                if (m < P.M) reinterpret_cast<int *>(P.out)[(size_t)m * P.N + n] = acc[m];
+            return;
+        }
+        // scales and bias only in dequant mode (they are NULL for int32 output)
+        const float swn = P.sw[P.sw_rows ? n : 0];
+        const float bn = P.bias ? t2f<T>(reinterpret_cast<const T *>(P.bias)[n]) : 0.f;
+#pragma unroll
+        for (int m = 0; m < BN; ++m) {
+            if (m >= P.M) continue;
+            const float sam = P.sa[P.sa_rows ? m : 0];
+            const float v = P.bias ? dequant1b(acc[m], sam, swn, bn) : dequant1(acc[m], sam, swn);
+            reinterpret_cast<T *>(P.out)[(size_t)m * P.N + n] = f2t<T>(v);
+        }
+    }
+};
+
+// Prefill epilogue of one accumulator tile: thread = token row m (A row), BN output features from column 0 of taddr.
+template <typename T, int BN>
+__device__ __forceinline__ void tc_prefill_epilogue(const TcArgs &P, int m, int tb, uint32_t taddr) {
+    const bool mok = m < P.M;
+    const float sam = (mok && !P.s32_out) ? P.sa[P.sa_rows ? m : 0] : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)c, r);
+        tmem_ld_wait();
+        const int n0 = tb * BN + c;
+        if (!mok) continue;
+        if (P.s32_out) {
+            int *o = reinterpret_cast<int *>(P.out) + (size_t)m * P.N;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (n0 + j < P.N) o[n0 + j] = (int)r[j];
+            continue;
+        }
+        // the reference's CUTLASS epilogue order: sa[m] * (sw[n] * acc) (vllm_turing/csrc/w8a8_big.cu:26-35)
+        T *o = reinterpret_cast<T *>(P.out) + (size_t)m * P.N;
+        if (n0 + 32 <= P.N && (P.N & 7) == 0) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const int n = n0 + j + 2 * h;
+                    const float v0 = __fmul_rn(sam, __fmul_rn(P.sw[P.sw_rows ? n : 0], (float)(int)r[j + 2 * h]));
+                    const float v1 =
+                        __fmul_rn(sam, __fmul_rn(P.sw[P.sw_rows ? n + 1 : 0], (float)(int)r[j + 2 * h + 1]));
+                    w4[h] = pack2<T>(v0, v1);
+                }
+                *reinterpret_cast<uint4 *>(o + n0 + j) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+        } else {
+            for (int j = 0; j < 32; ++j) {
+                const int n = n0 + j;
+                if (n < P.N) o[n] = f2t<T>(__fmul_rn(sam, __fmul_rn(P.sw[P.sw_rows ? n : 0], (float)(int)r[j])));
+            }
+        }
+    }
+}
+
+// The GEMM phase: every thread of the CTA (TC_THREADS) calls it; it returns after the CTA's pieces are done and its
+// TMEM is freed (a __syncthreads is the last thing it does, so the caller may reuse the shared memory).
+template <typename T, int BN, bool SWAP, int KBS, class Fin>
+__device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtensorMap *tmap_b, const TcArgs &P,
+                                         unsigned char *smem_raw, const Fin &fin) {
+    using Lay = TcLayout<BN, KBS>;
+    static_assert(!SWAP || BN <= 32, "decode orientation holds at most 32 token rows");
+    unsigned char *tiles = tc_align1024(smem_raw);
+    const int S = P.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + (size_t)S * Lay::STAGE);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;     // [2]
+    uint64_t *tempty = tfull + 2;    // [2]
+    uint64_t *drain = tempty + 2;    // [1]: the MMA issuer's last commit
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 4);   // [0] abort, [1] this piece finishes
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t deadline = globaltimer() + P.timeout_ns;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        flags[0] = 0;
+        flags[1] = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(tmap_a);
+        tma_prefetch_desc(tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Lay::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+
+    int ta, tb, kb0, kb1;
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();   // decode weights are read once per call
+            int it = 0;
+            bool dead = false;
+            TcPieces pc(P);
+            while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
+                for (int kb = kb0; kb < kb1; kb += KBS) {
+                    const int nb = min(KBS, kb1 - kb);
+                    const int s = it % S;
+                    const uint32_t r = (uint32_t)(it / S);
+                    if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
+                        if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x10u);
+                        flags[0] = 1;
+                        dead = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * Lay::KB_BYTES));
+                    unsigned char *st = tiles + (size_t)s * Lay::STAGE;
+                    for (int j = 0; j < nb; ++j) {
+                        if (SWAP)
+                            tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s], pol);
+                        else
+                            tma_load_2d(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s]);
+                    }
+                    for (int j = 0; j < nb; ++j)
+                        tma_load_2d(st + KBS * Lay::A_BYTES + j * Lay::B_BYTES, tmap_b, (kb + j) * TC_BK, tb * BN,
+                                    &full[s]);
+                    ++it;
+                }
+            }
+            if (dead) {   // let the copies already issued land before the shared memory is released
+                const uint64_t d2 = globaltimer() + P.timeout_ns;
+                for (int j = (it > S ? it - S : 0); j < it; ++j) mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, d2);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8(TC_BM, BN);
+            int it = 0, ut = 0;
+            TcPieces pc(P);
+            while (pc.next(P, ta, tb, kb0, kb1)) {
+                const int buf = ut & 1;
+                const uint32_t use = (uint32_t)(ut >> 1);
+                ++ut;
+                if (!flags[0] && !mbar_wait(&tempty[buf], (use & 1u) ^ 1u, deadline)) {
+                    report(P.status, ST_PIPE_TIMEOUT | 0x20u);
+                    flags[0] = 1;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+                for (int kb = kb0; kb < kb1; kb += KBS, ++it) {
+                    const int nb = min(KBS, kb1 - kb);
+                    const int s = it % S;
+                    const uint32_t r = (uint32_t)(it / S);
+                    if (flags[0]) break;   // aborted: issue nothing more
+                    if (!mbar_wait(&full[s], r & 1u, deadline)) {
+                        report(P.status, ST_PIPE_TIMEOUT | 0x30u);
+                        flags[0] = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sbase = smem_u32(tiles + (size_t)s * Lay::STAGE);
+                    for (int j = 0; j < nb; ++j) {
+                        const uint64_t adesc = sw128_desc(sbase + j * Lay::A_BYTES);
+                        const uint64_t bdesc = sw128_desc(sbase + KBS * Lay::A_BYTES + j * Lay::B_BYTES);
+#pragma unroll
+                        for (int k = 0; k < TC_BK / 32; ++k)   // 32 bytes of K per MMA: +2 in the 16-byte field
+                            umma_i8(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb0 || j > 0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!flags[0]) umma_commit(&tfull[buf]);
+            }
+            // every MMA this thread issued has completed once `drain` flips (bounded: TMEM is freed after it)
+            umma_commit(drain);
+            mbar_wait(drain, 0u, globaltimer() + P.timeout_ns);
+        }
+    } else {
+        // ---------------- epilogue warps 2..5 ----------------
+        const int q = warp & 3;   // TMEM lane quarter this warp may access
+        int ut = 0;
+        TcPieces pc(P);
+        while (pc.next(P, ta, tb, kb0, kb1)) {
+            const int buf = ut & 1;
+            const uint32_t use = (uint32_t)(ut >> 1);
+            ++ut;
+            if (!flags[0] && !mbar_wait(&tfull[buf], use & 1u, deadline)) {
+                report(P.status, ST_PIPE_TIMEOUT | 0x40u);
+                flags[0] = 1;
+            }
+            tc_fence_after();
+            const int arow = ta * TC_BM + q * 32 + lane;   // row of operand A this thread holds
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+            if constexpr (!SWAP) {
+                tc_prefill_epilogue<T, BN>(P, arow, tb, taddr);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);
+            } else {
+                uint32_t r[32];
+                if (BN == 16)
+                    tmem_ld16(taddr, r);
+                else
+                    tmem_ld32(taddr, r);
+                tmem_ld_wait();
+                tc_fence_before();   // this warp's TMEM reads are done: the MMA may refill the buffer
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[buf]);
+                const int n = arow;
+                const bool nok = n < P.N;
+                int acc[BN];
+#pragma unroll
+                for (int m = 0; m < BN; ++m) acc[m] = (int)r[m];
+                if (kb0 == 0 && kb1 == P.nkb) {   // the whole K range of the tile in this CTA
+                    fin(P, n, nok, acc);
+                    continue;
+                }
+                // split tile: add this piece's partial sums, then the CTA whose K blocks complete the tile finishes it
+                if (nok) {
+#pragma unroll
+                    for (int m = 0; m < BN; ++m)
+                        if (m < P.M) atomicAdd(&P.scratch[(size_t)m * P.N + n], acc[m]);
+                }
+                __threadfence();
+                named_sync(TC_EPI_BAR, 128);
+                if (threadIdx.x == TC_EPI_LEAD) {
+                    const int add = kb1 - kb0;
+                    const int old = atomicAdd(&P.tickets[ta], add);
+                    flags[1] = (old + add == P.nkb) ? 1 : 0;
+                }
+                named_sync(TC_EPI_BAR, 128);
+                const bool last = flags[1] != 0;
+                if (!last) continue;
+                __threadfence();
+                if (nok) {
+#pragma unroll
+                    for (int m = 0; m < BN; ++m) {
+                        if (m >= P.M) continue;
+                        int *sp = &P.scratch[(size_t)m * P.N + n];
+                        acc[m] = __ldcg(sp);
+                        *sp = 0;
+                    }
+                }
+                fin(P, n, nok, acc);
+                named_sync(TC_EPI_BAR, 128);   // every thread has read flags[1] and its sums: the ticket may restart
+                if (threadIdx.x == TC_EPI_LEAD) atomicExch(&P.tickets[ta], 0);
+            }
+        }
+    }
+    // all roles done: free TMEM (the allocating warp) after every TMEM read and MMA has completed
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Lay::TMEM_COLS);
+    }
+    __syncthreads();
+}
+
+// ---- host side -------------------------------------------------------------------------------------------------------
+// rows x K int8 operand, box = 128 bytes of K x box_rows rows, 128-byte swizzle (the UMMA K-major SW128 layout)
+inline bool tc_make_map(CUtensorMap *m, const void *base, int rows, int K, int box_rows) {
+    return make_map_i8(m, base, rows, K, TC_BK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// stages that fit the opt-in shared memory (less the 1024-byte alignment slack, the barriers and up to 1 KB of static
+// shared variables of the kernel)
+template <int BN, int KBS>
+inline int tc_stages(int dev) {
+    using Lay = TcLayout<BN, KBS>;
+    int s = (max_smem_optin(dev) - 1024 - Lay::BAR_BYTES - 1024) / Lay::STAGE;
+    return s > 16 ? 16 : s;
+}
+template <int BN, int KBS>
+inline int tc_smem_bytes(int stages) {
+    return stages * TcLayout<BN, KBS>::STAGE + 1024 + TcLayout<BN, KBS>::BAR_BYTES;
+}
+
+// K blocks per pipeline stage of the decode orientation: VLLM_TURING_TC_KBS (1, 2 or 4; default 4)
+inline int decode_kbs() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_TC_KBS");
+        const int x = e ? atoi(e) : 4;
+        v = (x == 1 || x == 2) ? x : 4;
+    }
+    return v;
+}
+
+// Decode stream-K work: weights w [N, K] as operand A, M token rows as operand B.
+inline void tc_decode_args(TcArgs &P, int M, int N, int K) {
+    P.n_tiles_a = (N + TC_BM - 1) / TC_BM;
+    P.n_tiles_b = 1;
+    P.nkb = (K + TC_BK - 1) / TC_BK;
+    P.units = P.n_tiles_a * P.nkb;
+    P.stream_k = 1;
+    P.M = M;
+    P.N = N;
+}
+
+// split-K scratch of the decode orientation: int32 [M, N], then one ticket per 128-row weight tile
+inline size_t tc_decode_scratch_bytes(int M, int N) {
+    return ((size_t)M * N * 4 + (size_t)((N + TC_BM - 1) / TC_BM) * 4 + 255) & ~(size_t)255;
+}
+
+}  // namespace vt

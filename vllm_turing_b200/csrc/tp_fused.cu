@@ -1,4 +1,4 @@
-// Fused tensor-parallel row-linear layer tail for B200 (sm_100a), decode shapes (M <= 16 token rows), ONE kernel:
+// Fused tensor-parallel row-linear layer tail for B200 (sm_100a), decode shapes (M <= 32 token rows), ONE kernel:
 //
 //   partial_r = bf16( (a_r . w_r^T) * sa_r[m] * sw_r[n] )           this rank's K-slice   (vllm_turing/w8a8.py path)
 //   reduced   = bf16( sum_r float(partial_r) )  in rank order         the TP all-reduce      (host_ar.cu:90-101)
@@ -9,9 +9,12 @@
 //                                                                     tests/test_quantfuse.py:45-48, quantfuse.py:18-24)
 //
 // The reference runs these as three or more kernels (GEMV, LL all-reduce, compiled norm + quant); here:
-//  1. GEMV phase (gemv_core.cuh): all CTAs stream this rank's weight slice; the CTA that finishes a 32-column
-//     row-block dequantises it to bf16 and pushes it as LL words straight into every rank's receive slot (NVLink
-//     stores, no staging buffer, no flag round trip).
+//  1. GEMM phase, one of
+//     - tcgen05 (default, tc_core.cuh): weights as the MMA's A operand, stream-K over the SMs; the CTA that completes
+//       a 128-feature tile dequantises it and pushes it as LL words straight into every rank's receive slot,
+//     - dp4a GEMV (VLLM_TURING_FUSED_GEMV=1, M <= 16; gemv_core.cuh): the CTA that finishes a 32-feature row-block
+//       does the same push.
+//     Either way: NVLink stores of the finished values, no staging buffer, no flag round trip.
 //  2. Epilogue phase: token row m is owned by E CTAs (CTA index m * E + g), each for a contiguous 1/E of the row's
 //     columns. Each polls the LL words of all ranks for its columns, sums them in rank order, adds the residual and
 //     writes it back; the sum of squares and then the absmax of the normalised row are combined across the E CTAs
@@ -27,6 +30,7 @@
 #include "common.cuh"
 #include "gemv_core.cuh"
 #include "host_util.h"
+#include "tc_core.cuh"
 #include "tma_host.h"
 
 namespace vt {
@@ -93,56 +97,53 @@ __device__ __forceinline__ float block_max_n(float v, float *red) {
 }
 
 // Publish this CTA's value for (row m, group g, slot) and combine the E values of the row's group in group order.
+// Lane q of warp 0 polls group q's mailbox word (all E in flight at once: one L2 round trip, not E in a row); the
+// values are then folded in group order 0, 1, .., E - 1, so every CTA of the row and every rank gets identical bits.
 __device__ __forceinline__ float group_combine(const CommView &c, int m, int g, int E, int slot, float v, bool is_max,
                                                unsigned seq, uint64_t deadline, float *bcast) {
     unsigned long long *mb = c.mbox();
-    if (threadIdx.x == 0) {
-        st_volatile8(&mb[((size_t)m * COMM_MBOX_GROUPS + g) * 2 + slot],
-                     ((unsigned long long)seq << 32) | (unsigned long long)__float_as_uint(v));
-        float t = 0.0f;
-        bool dead = false;
-        for (int q = 0; q < E; ++q) {
-            const unsigned long long *p = &mb[((size_t)m * COMM_MBOX_GROUPS + q) * 2 + slot];
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        if (lane == 0)
+            st_volatile8(&mb[((size_t)m * COMM_MBOX_GROUPS + g) * 2 + slot],
+                         ((unsigned long long)seq << 32) | (unsigned long long)__float_as_uint(v));
+        __syncwarp();
+        float val = 0.0f;
+        if (lane < E) {
+            const unsigned long long *p = &mb[((size_t)m * COMM_MBOX_GROUPS + lane) * 2 + slot];
             unsigned long long x = ld_volatile8(p);
             uint32_t it = 0;
-            while (!dead && (unsigned)(x >> 32) != seq) {
+            while ((unsigned)(x >> 32) != seq) {
                 if ((++it & 63u) == 0 && globaltimer() > deadline) {
-                    report(c.status(), ST_GROUP_TIMEOUT | (unsigned)(m * 64 + q));
-                    dead = true;
+                    report(c.status(), ST_GROUP_TIMEOUT | (unsigned)(m * 64 + lane));
                     break;
                 }
                 x = ld_volatile8(p);
             }
-            const float val = __uint_as_float((unsigned)(x & 0xffffffffu));
-            t = is_max ? fmaxf(t, val) : (q == 0 ? val : t + val);
+            val = __uint_as_float((unsigned)(x & 0xffffffffu));
         }
-        *bcast = t;
+        float t = 0.0f;
+        for (int q = 0; q < E; ++q) {
+            const float vq = __shfl_sync(0xffffffffu, val, q);
+            t = is_max ? fmaxf(t, vq) : (q == 0 ? vq : t + vq);
+        }
+        if (lane == 0) *bcast = t;
     }
     __syncthreads();
     return *bcast;
 }
 
-template <typename T, int MT>
-__global__ void __launch_bounds__(GV_THREADS, 1)
-    tp_row_linear_kernel(const __grid_constant__ CUtensorMap wmap, FusedArgs<T> P) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ unsigned s_seq;
-    __shared__ float red[32];
-    __shared__ float bcast;
-    const CommView &c = P.c;
-    const unsigned seq = comm_begin(c, &s_seq);
-    const unsigned p = seq & 1u;
-    const uint64_t t0 = globaltimer();
-    LLPushEpi<T> push{&c, P.sa, P.sw, P.M, P.N, seq, p};
-    gemv_phase<MT>(P.a, &wmap, P.M, P.N, P.K, c.scratch(), c.tickets(), smem, P.stages, t0 + P.pipe_timeout,
-                   c.status(), push);
-    __syncthreads();
-
+// Phase 2 of the fused kernel (all threads of every CTA call it once the GEMM phase has pushed this rank's values):
+// CTA m * E + g owns columns [w0, w1) (in 4-column LL words) of token row m. smem: free shared memory of at least
+// ceil(N / 4 / E) * 16 bytes; red: 32 floats; bcast: one float.
+template <typename T>
+__device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommView &c, unsigned seq, unsigned p,
+                                             unsigned char *smem, float *red, float *bcast) {
     const int M = P.M, N = P.N, E = P.E, W4 = N >> 2;
     if ((int)blockIdx.x < M * E) {
         const int m = blockIdx.x / E, g = blockIdx.x - m * E;
         const int w0 = (int)((long long)W4 * g / E), w1 = (int)((long long)W4 * (g + 1) / E);
-        float *hbuf = reinterpret_cast<float *>(smem + GV_HDR);   // the GEMV ring is free now
+        float *hbuf = reinterpret_cast<float *>(smem);
         const uint64_t deadline = globaltimer() + P.peer_timeout;
         bool dead = false;
         float ss = 0.0f;
@@ -182,7 +183,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
         }
         if (P.residual) {
             ss = block_sum_n(ss, red);
-            const float tot = group_combine(c, m, g, E, 0, ss, false, seq, deadline, &bcast);
+            const float tot = group_combine(c, m, g, E, 0, ss, false, seq, deadline, bcast);
             const float rs = __frsqrt_rn(__fdiv_rn(tot, (float)N) + P.eps);
             float amax = 0.0f;
             for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
@@ -199,7 +200,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
                 amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
             }
             amax = block_max_n(amax, red);
-            amax = group_combine(c, m, g, E, 1, amax, true, seq, deadline, &bcast);
+            amax = group_combine(c, m, g, E, 1, amax, true, seq, deadline, bcast);
             const float inv = quant_inv(amax);
             if (g == 0 && threadIdx.x == 0) P.scales[m] = __fdiv_rn(amax, 127.0f);
             for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
@@ -209,7 +210,124 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
             }
         }
     }
+}
+
+template <typename T, int MT>
+__global__ void __launch_bounds__(GV_THREADS, 1)
+    tp_row_linear_kernel(const __grid_constant__ CUtensorMap wmap, FusedArgs<T> P) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    __shared__ unsigned s_seq;
+    __shared__ float red[32];
+    __shared__ float bcast;
+    const CommView &c = P.c;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t t0 = globaltimer();
+    LLPushEpi<T> push{&c, P.sa, P.sw, P.M, P.N, seq, p};
+    gemv_phase<MT>(P.a, &wmap, P.M, P.N, P.K, c.scratch(), c.tickets(), smem, P.stages, t0 + P.pipe_timeout,
+                   c.status(), push);
+    __syncthreads();
+
+    row_epilogue<T>(P, c, seq, p, smem + GV_HDR, red, &bcast);   // the GEMV ring is free now
     comm_end(c, seq);
+}
+
+// tcgen05 finisher of the fused kernel: thread = output feature n of a finished 128-feature tile; dequantises its
+// accumulators ((acc * sa[m]) * sw[n], the GEMV's order) and lane 4j of each warp pushes the LL word of features
+// n .. n + 3 (gathered by shuffles) to every rank's receive slot.
+template <typename T, int BN>
+struct TcLLPushEpi {
+    const CommView *c;
+    const float *sa, *sw;
+    int M, N;
+    unsigned seq, p;
+    __device__ __forceinline__ void operator()(const TcArgs &, int n, bool nok, const int (&acc)[BN]) const {
+        const int W4 = N >> 2, world = c->world, rank = c->rank;
+        const int lane = threadIdx.x & 31;
+        const float swn = nok ? sw[n] : 0.0f;
+#pragma unroll
+        for (int m = 0; m < BN; ++m) {
+            if (m >= M) break;   // M is uniform: the whole warp leaves together
+            const float v = nok ? dequant1(acc[m], sa[m], swn) : 0.0f;
+            const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
+            const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
+            const float v3 = __shfl_down_sync(0xffffffffu, v, 3);
+            if ((lane & 3) == 0 && nok) {   // n % 4 == 0 here and N % 4 == 0: features n .. n + 3 all exist
+                const uint32_t lo = pack2<T>(v, v1), hi = pack2<T>(v2, v3);
+                for (int k = 0; k < world; ++k) {
+                    const int dst = (rank + k) % world;
+                    ll_store(c->ll_slot(dst, p, rank) + ((size_t)m * W4 + (n >> 2)) * 16, lo, hi, seq);
+                }
+            }
+        }
+    }
+};
+
+template <typename T, int BN, int KBS>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tp_row_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                            TcArgs G, FusedArgs<T> P) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ unsigned s_seq;
+    __shared__ float red[32];
+    __shared__ float bcast;
+    const CommView &c = P.c;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    TcLLPushEpi<T, BN> push{&c, P.sa, P.sw, P.M, P.N, seq, p};
+    tc_phase<T, BN, true, KBS>(&tmap_w, &tmap_a, G, smem_raw, push);   // ends with __syncthreads
+    row_epilogue<T>(P, c, seq, p, tc_align1024(smem_raw), red, &bcast);   // the stage ring is free now
+    comm_end(c, seq);
+}
+
+template <typename T, int BN, int KBS>
+static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    CUtensorMap mw, ma;
+    if (!tc_make_map(&mw, P.w, P.N, P.K, TC_BM) || !tc_make_map(&ma, P.a, P.M, P.K, BN)) return VT_EARG;
+    TcArgs G{};
+    tc_decode_args(G, P.M, P.N, P.K);
+    if (G.n_tiles_a > COMM_TICKETS) return VT_EARG;
+    G.sa = P.sa;
+    G.sw = P.sw;
+    G.sa_rows = 1;
+    G.sw_rows = 1;
+    char *local = P.c.base[P.c.rank];
+    G.scratch = reinterpret_cast<int *>(local + P.c.L.scratch_off);
+    G.tickets = reinterpret_cast<int *>(local + COMM_TICKET_OFF);
+    G.status = reinterpret_cast<unsigned *>(local + 128);
+    G.timeout_ns = P.pipe_timeout;
+    const int stages = tc_stages<BN, KBS>(dev);
+    if (stages < 2) return VT_EARG;
+    G.stages = stages;
+    const int smem = tc_smem_bytes<BN, KBS>(stages);
+    static bool attr_set[VT_MAX_DEV] = {false};
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(tp_row_linear_tc_kernel<T, BN, KBS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem) != cudaSuccess)
+            return (int)cudaGetLastError();
+        attr_set[dev] = true;
+    }
+    int g = num_sms(dev);
+    if (g > G.units) g = G.units;
+    int E = g / P.M;
+    if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
+    if (E < 1) return VT_EARG;
+    P.E = E;
+    // row epilogue buffer: ceil(N / 4 / E) words of 4 floats in the (free) stage ring
+    if ((size_t)((P.N / 4 + E - 1) / E) * 16 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
+    tp_row_linear_tc_kernel<T, BN, KBS><<<g, TC_THREADS, smem, s>>>(mw, ma, G, P);
+    return (int)cudaGetLastError();
+}
+
+template <typename T, int BN>
+static int fused_tc_kbs(FusedArgs<T> P, cudaStream_t s) {
+    switch (decode_kbs()) {
+        case 1: return launch_fused_tc<T, BN, 1>(P, s);
+        case 2: return launch_fused_tc<T, BN, 2>(P, s);
+        default: return launch_fused_tc<T, BN, 4>(P, s);
+    }
 }
 
 template <typename T, int MT>
@@ -239,9 +357,23 @@ static int launch_fused(FusedArgs<T> P, cudaStream_t s) {
     return (int)cudaGetLastError();
 }
 
+// VLLM_TURING_FUSED_GEMV=1 selects the dp4a GEMV phase for M <= 16 (default: the tcgen05 phase for every M <= 32).
+static bool fused_use_gemv() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_FUSED_GEMV");
+        v = (e && atoi(e) != 0) ? 1 : 0;
+    }
+    return v != 0;
+}
+
 template <typename T>
 static int dispatch_fused(FusedArgs<T> P, cudaStream_t s) {
     const int M = P.M;
+    if (!fused_use_gemv() || M > 16) {
+        if (M <= 16) return fused_tc_kbs<T, 16>(P, s);
+        return fused_tc_kbs<T, 32>(P, s);
+    }
     if (M <= 1) return launch_fused<T, 1>(P, s);
     if (M <= 2) return launch_fused<T, 2>(P, s);
     if (M <= 3) return launch_fused<T, 3>(P, s);
@@ -265,6 +397,12 @@ static void preload_fused() {
     cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 8>);
     cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 12>);
     cudaFuncGetAttributes(&fa, tp_row_linear_kernel<T, 16>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 16, 1>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 16, 2>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 16, 4>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 32, 1>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 32, 2>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 32, 4>);
 }
 
 }  // namespace vt
@@ -277,12 +415,12 @@ extern "C" {
 //   a [M, K] int8 (this rank's activation slice), w [N, K] int8 (this rank's weight slice), sa [M], sw [N] float32;
 //   residual [M, N] (updated in place), norm_w [N], eps, q [M, N] int8, scales [M] float32 -- or residual = NULL for
 //   a plain row-linear + all-reduce; reduced [M, N] (optional; required without residual) receives the all-reduced
-//   sum. dtype 0 fp16 / 1 bf16. 1 <= M <= 16, N % 4 == 0, K % 16 == 0, M * N * 2 <= the communicator's LL capacity.
+//   sum. dtype 0 fp16 / 1 bf16. 1 <= M <= 32, N % 4 == 0, K % 16 == 0, M * N * 2 <= the communicator's LL capacity.
 int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,
                      const void *norm_w, float eps, void *q, void *scales, void *reduced, int M, int N, int K,
                      int dtype, void *stream) {
     Comm *ch = reinterpret_cast<Comm *>(comm);
-    if (!ch || M < 1 || M > 16 || N < 4 || (N & 3) || K < 16 || (K & 15) || ((uintptr_t)a & 15) ||
+    if (!ch || M < 1 || M > COMM_MBOX_ROWS || N < 4 || (N & 3) || K < 16 || (K & 15) || ((uintptr_t)a & 15) ||
         ((uintptr_t)w & 15))
         return VT_EARG;
     if (!residual && !reduced) return VT_EARG;
@@ -291,7 +429,7 @@ int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, c
         return VT_EARG;
     if (reduced && ((uintptr_t)reduced & 7)) return VT_EARG;
     const CommLayout &L = ch->v.L;
-    if ((size_t)M * N * 2 > L.ll_slot / 2 || (size_t)M * N * 4 > L.scratch_bytes || (N + 31) / 32 > 4096)
+    if ((size_t)M * N * 2 > L.ll_slot / 2 || (size_t)M * N * 4 > L.scratch_bytes || (N + 31) / 32 > COMM_TICKETS)
         return VT_EARG;
     cudaStream_t s = (cudaStream_t)stream;
     if (dtype == 0) {

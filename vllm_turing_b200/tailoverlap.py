@@ -32,11 +32,14 @@ _REG = []
 _STREAMS = {}
 
 
-def silu_mul_quant(gate_up: torch.Tensor):
-    """(M, 2I) fp16 / bf16 -> int8 (M, I) of SiLU(gate) * up and its per-row scales (M, 1) float32."""
+def silu_mul_quant(gate_up: torch.Tensor, q=None, sc=None):
+    """(M, 2I) fp16 / bf16 -> int8 (M, I) of SiLU(gate) * up and its per-row scales (M, 1) float32, written into q / sc
+    when given (e.g. the static buffers of a captured decode step)."""
     M, I2 = gate_up.shape
-    q = torch.empty(M, I2 // 2, dtype=torch.int8, device=gate_up.device)
-    sc = torch.empty(M, 1, dtype=torch.float32, device=gate_up.device)
+    q = q if q is not None else torch.empty(M, I2 // 2, dtype=torch.int8, device=gate_up.device)
+    sc = sc if sc is not None else torch.empty(M, 1, dtype=torch.float32, device=gate_up.device)
+    if q.shape != (M, I2 // 2) or q.dtype != torch.int8 or not q.is_contiguous() or sc.numel() != M:
+        raise ValueError("silu_mul_quant: q must be int8 [M, I] contiguous and sc hold M floats")
     code = 0 if gate_up.dtype == torch.float16 else 1
     rc = _build.load().vt_silu_mul_quant(gate_up.data_ptr(), q.data_ptr(), sc.data_ptr(), M, I2 // 2, code,
                                          torch.cuda.current_stream().cuda_stream)

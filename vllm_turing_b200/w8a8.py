@@ -4,8 +4,10 @@ vLLM's W8A8 int8 linear layers call vllm._custom_ops.cutlass_scaled_mm(a, b, sca
 the reference (vllm_turing/w8a8.py:125-150), the wrapper is replaced by one that runs the custom op
 vllm_turing::scaled_mm_ with the same arguments, dispatching by M at run time (also inside torch.compile / CUDA-graph
 capture, where M is concrete):
-  - M <= VLLM_TURING_GEMV_MAX_M (default 8): the streamed HBM-bound GEMV (csrc/gemv_core.cuh, bulk copies + dp4a),
-  - M <= VLLM_TURING_MMA_MAX_M (default 32): the small-M tcgen05 kernel (weights as the MMA's A operand),
+  - M <= VLLM_TURING_GEMV_MAX_M (default 0, i.e. off): the streamed dp4a GEMV (csrc/gemv_core.cuh),
+  - M <= VLLM_TURING_MMA_MAX_M (default 32): the small-M tcgen05 kernel (weights as the MMA's A operand, stream-K over
+    the SMs); on B200 it streams decode weights at least as fast as the dp4a GEMV at every M from 1 to 32, so it is
+    the default decode path (the reference's default, GEMV up to 12 rows, suits its sm_75 part),
   - larger M (prefill): the tcgen05 kind::i8 GEMM with TMEM accumulators (VLLM_TURING_BIG=0 keeps vLLM's),
   - anything else (non-16-aligned shapes, other dtypes): vLLM's own op.
 The kernels live in libvllm_turing_b200.so, loaded with ctypes (no torch C++ ABI involved), as the reference does.
@@ -16,10 +18,10 @@ import torch
 
 from . import _build
 
-MAX_M = int(os.environ.get("VLLM_TURING_GEMV_MAX_M", "8"))
+MAX_M = int(os.environ.get("VLLM_TURING_GEMV_MAX_M", "0"))
 MMA_MAX_M = min(int(os.environ.get("VLLM_TURING_MMA_MAX_M", "32")), 32)
 BIG = os.environ.get("VLLM_TURING_BIG", "1") != "0"
-_ws = {}   # device -> persistent zeroed GEMV workspace (graph capture keeps its address)
+_ws = {}   # device -> persistent zeroed split-K workspace (graph capture keeps its address)
 
 
 def lib():
@@ -47,12 +49,12 @@ def gemv_ok(out, a, b, sa, sb, bias, max_m=None):
 
 
 def workspace(device, M, N):
-    """Persistent zeroed GEMV workspace for this device, grown outside stream capture only."""
-    need = lib().w8a8_gemv_ws_bytes(M, N)
+    """Persistent zeroed split-K workspace for this device (GEMV and tensor-core decode), grown outside capture only."""
+    need = max(lib().w8a8_gemv_ws_bytes(M, N), lib().w8a8_mma_ws_bytes(M, N))
     ws = _ws.get(device)
     if ws is None or ws.numel() < need:
         if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("vllm_turing_b200: GEMV workspace must be sized before CUDA graph capture")
+            raise RuntimeError("vllm_turing_b200: split-K workspace must be sized before CUDA graph capture")
         ws = _ws[device] = torch.zeros(max(need, 8 << 20), dtype=torch.uint8, device=device)
     return ws
 
@@ -92,15 +94,17 @@ def _has(name):
 
 
 def mma_ok(out, a, b, sa, sb, bias):
-    return a.shape[0] > MAX_M and _has("w8a8_mma") and gemv_ok(out, a, b, sa, sb, bias, MMA_MAX_M)
+    return a.shape[0] > MAX_M and _has("w8a8_mma_ws") and gemv_ok(out, a, b, sa, sb, bias, MMA_MAX_M)
 
 
 def mma(out, a, b, sa, sb, bias):
     M, K = a.shape
     N = b.shape[1]
-    rc = lib().w8a8_mma(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(),
-                        bias.data_ptr() if bias is not None else None, out.data_ptr(), M, N, K,
-                        int(sa.numel() > 1), int(sb.numel() > 1), _dtype_code(out.dtype), _stream())
+    ws = workspace(a.device, M, N)
+    rc = lib().w8a8_mma_ws(a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+                           bias.data_ptr() if bias is not None else None, out.data_ptr(), M, N, K,
+                           int(sa.numel() > 1), int(sb.numel() > 1), _dtype_code(out.dtype), ws.data_ptr(),
+                           ws.numel(), _stream())
     if rc != 0:
         raise RuntimeError(f"w8a8_mma launch failed: {rc}")
 
