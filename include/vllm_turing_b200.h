@@ -115,7 +115,8 @@ int ce_enable_peer(int peer);
  * on one communicator must be stream-ordered on each rank. Call counting is device-resident (CUDA-graph safe). */
 
 /* Bytes of the per-rank region: ll_data = largest one-shot / fused message (bytes), big_data = largest two-shot
- * message per launch (bytes; larger ones run in pieces), scratch_ints = int32 scratch of the fused GEMV (>= M*N). */
+ * message per launch (bytes; larger ones run in pieces), scratch_ints = split-K scratch of the fused row-linear in
+ * int32 words (>= M * N for the GEMV phase, >= SMs * 128 * ceil(M / 2) * 4 for the tcgen05 phase). */
 size_t vt_comm_region_bytes(int world, size_t ll_data, size_t big_data, size_t scratch_ints);
 /* bases[world]: each rank's region (own from ce_alloc, peers' from ce_open), same sizes. NULL on bad arguments. */
 void *vt_comm_create(int rank, int world, void *const *bases, size_t ll_data, size_t big_data, size_t scratch_ints);

@@ -44,7 +44,9 @@ class TPComm:
         self.world = dist.get_world_size(group)
         self.device = torch.device(device)
         self.ll_bytes, self.big_bytes = int(ll_bytes), int(big_bytes)
-        self.scratch_ints = int(scratch_ints if scratch_ints is not None else max(self.ll_bytes // 2, 1 << 16))
+        # split-K scratch of the fused row-linear: the GEMV's int32 [M, N] partials, or the tcgen05 kernel's slots
+        # (SMs x 128 x ceil(M / 2) x 16 bytes: 4.9 MB at M = 32 on 148 SMs)
+        self.scratch_ints = int(scratch_ints if scratch_ints is not None else max(self.ll_bytes // 2, 2 << 20))
         self.handle = None
         self._opened = []
         self._local = None

@@ -107,6 +107,19 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// ---- programmatic dependent launch (griddepcontrol; no-ops when the grid was launched without the attribute) -------
+// pdl_wait: returns once the preceding grid in the stream has completed and its memory is visible; every global access
+// to data an earlier kernel produces or still reads comes after it. pdl_launch_dependents: lets the next grid in the
+// stream be scheduled (onto SMs as they free up) before this one ends; its own pdl_wait keeps it correct.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 // ---- named barrier among a subset of warps ---------------------------------------------------------------------------
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -7,6 +7,7 @@
 #include <stdlib.h>
 
 #include <mutex>
+#include <utility>
 
 namespace vt {
 
@@ -66,6 +67,37 @@ inline uint64_t pipe_timeout_ns() {
 inline uint64_t peer_timeout_ns() {
     static uint64_t v = env_ns("VLLM_TURING_AR_TIMEOUT_MS", 10000.0);
     return v;
+}
+
+// Programmatic dependent launch for the decode-chain kernels (tcgen05 GEMMs, fused row-linear, row-split SiLU-quant):
+// VLLM_TURING_PDL=0 turns it off.
+inline bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_PDL");
+        v = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    return v != 0;
+}
+
+// kernel<<<grid, block, smem, s>>>(args...) with the programmatic-stream-serialization attribute when pdl is set (the
+// kernel may start while its predecessor in the stream finishes; it must call pdl_wait before using that one's data).
+template <typename... KArgs, typename... Args>
+inline int launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                    Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return (int)e;
+    return (int)cudaGetLastError();
 }
 
 inline bool stream_capturing(cudaStream_t s) {

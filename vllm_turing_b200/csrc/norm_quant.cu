@@ -148,7 +148,8 @@ __global__ void __launch_bounds__(RQ_THREADS) silu_mul_quant_kernel(const T *__r
 // deterministic) and an arrival counter; each CTA then quantises its own slice. The last CTA of a row to leave resets
 // the row's slot and counters, so the next (stream-ordered) call starts from zero. Calls that overlap on the GPU
 // would share the slots: they must be stream-ordered (as every decode step is). The wait for the row's other CTAs
-// is bounded; a timeout lands in the library status word.
+// is bounded; a timeout lands in the library status word. Launched with programmatic dependent launch (it waits for
+// the kernel that wrote gate_up before reading it).
 constexpr int SQ_THREADS = 256;
 constexpr int SQ_ROWS = 64;   // rows the split path serves
 static __device__ unsigned g_sq_amax[SQ_ROWS], g_sq_arrive[SQ_ROWS], g_sq_leave[SQ_ROWS];
@@ -160,6 +161,8 @@ __global__ void __launch_bounds__(SQ_THREADS)
     extern __shared__ float pbuf[];
     __shared__ float red[32];
     __shared__ float s_amax;
+    pdl_launch_dependents();
+    pdl_wait();   // gate_up comes from the previous kernel
     const int m = blockIdx.x / E, g = blockIdx.x - m * E;
     const int i0 = (int)((long long)I * g / E), i1 = (int)((long long)I * (g + 1) / E);
     const T *gr = gu + (size_t)m * 2 * I;
@@ -225,10 +228,8 @@ static int launch_silu(const void *gu, void *q, void *scales, int M, int I, cuda
         void *scratch = nullptr;
         unsigned *status = nullptr;
         if (ws_acquire(0, s, &scratch, &status) != 0) status = nullptr;   // timeouts reported only with a workspace
-        silu_mul_quant_split_kernel<T><<<M * E, SQ_THREADS, chunk * 4, s>>>((const T *)gu, (int8_t *)q,
-                                                                             (float *)scales, I, E, pipe_timeout_ns(),
-                                                                             status);
-        return (int)cudaGetLastError();
+        return launch_k(silu_mul_quant_split_kernel<T>, dim3(M * E), dim3(SQ_THREADS), (size_t)chunk * 4, s, true,
+                        (const T *)gu, (int8_t *)q, (float *)scales, I, E, pipe_timeout_ns(), status);
     }
     if (int rc = smem_attr((const void *)silu_mul_quant_kernel<T>, I * 4)) return rc;
     silu_mul_quant_kernel<T><<<M, RQ_THREADS, I * 4, s>>>((const T *)gu, (int8_t *)q, (float *)scales, I);

@@ -10,10 +10,13 @@
 //   decode  (SWAP = true):  A = weights (128-row tiles of N), B = a few token rows (BN = 16 or 32). Stream-K: the
 //            (tile, K block) index space is cut into one contiguous range per CTA, so every SM streams the same number
 //            of weight bytes (+-1 K block of 16 KB). A CTA's range falls into "pieces" (one tile, a K-block range).
-//            A piece that covers its whole tile is finished in registers; otherwise the piece's int32 partial sums are
-//            added into a zeroed scratch [M, N] (atomicAdd: exact), and the CTA whose K blocks complete the tile's
-//            ticket reads the sums back, returns the scratch and the ticket to zero and hands the accumulators to the
-//            caller's finisher `fin(P, n, n_ok, acc[BN])` (thread = output feature n, acc[m] for token rows m).
+//            A piece that covers its whole tile is finished in registers. A split tile is finished by the CTA holding
+//            its first K blocks (the "head" piece, the last piece of that CTA's range): the other pieces add their
+//            int32 partial sums into a zeroed scratch [M, N] (atomicAdd: exact) and count their K blocks on the tile's
+//            ticket; the head CTA waits (bounded) for the count, adds the scratch to its own sums, returns scratch and
+//            ticket to zero and hands the accumulators to the caller's finisher `fin(P, n, n_ok, acc[BN])` (thread =
+//            output feature n, acc[m] for token rows m;
+//            fin.on_start() runs once in every epilogue thread before the first piece).
 //
 // CTA = 6 warps: warp 0 issues TMA loads into a ring of shared-memory stages (KBS K blocks of 128 bytes per stage, so
 // one barrier round trip moves KBS x 16 KB of weights), warp 1 allocates TMEM and one of its threads issues the MMAs
@@ -21,6 +24,11 @@
 // warp w may read TMEM lanes 32 (w % 4) .. + 31). TMEM holds two accumulator buffers so the epilogue of one piece
 // overlaps the MMAs of the next. Every wait is bounded (globaltimer): on a timeout the CTA records the status, stops
 // issuing, waits (bounded) for the copies and MMAs it already issued, frees its TMEM and returns.
+//
+// Programmatic dependent launch: the phase lets the next kernel in the stream launch as soon as all of its own CTAs
+// are resident, and only the producer thread runs before pdl_wait -- it loads the weight half of its first stages,
+// which no kernel writes, so the weight stream of a decode layer starts while the previous kernel finishes. (The
+// kernels' shared memory keeps two of them off one SM, so their TMEM allocations never wait on each other.)
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -39,7 +47,7 @@ constexpr int TC_THREADS = 192;
 constexpr int TC_BK = 128;        // bytes of K per K block (= one 128-byte swizzle row)
 constexpr int TC_BM = 128;        // MMA M (rows of operand A per tile)
 constexpr int TC_EPI_BAR = 1;     // named barrier of the four epilogue warps
-constexpr int TC_EPI_LEAD = 64;   // thread that takes the split-K tickets (warp 2, lane 0)
+constexpr int TC_EPI_LEAD = 64;   // first epilogue thread (warp 2, lane 0)
 
 // ---- tcgen05 primitives (PTX ISA 8.6+, sm_100a) -------------------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
@@ -121,7 +129,7 @@ struct TcArgs {
     int sa_rows, sw_rows;       // 1: per row / feature, 0: one value
     void *out;                  // [M, N] row-major
     int M, N;                   // tokens, output features
-    int *scratch, *tickets;     // stream-K: int32 [M, N] and one ticket per tile, zero between calls
+    uint4 *slots;               // stream-K: split-K LL slots [grid][hw][128] (16-byte words), zero between calls
     int s32_out;                // write int32 accumulators instead of dequantised values
     int stages;
     uint64_t timeout_ns;
@@ -134,7 +142,7 @@ template <int BN, int KBS> struct TcLayout {
     static constexpr int KB_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE = KBS * KB_BYTES;    // stage = [KBS A blocks][KBS B blocks]
     static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-    static constexpr int BAR_BYTES = 512;           // mbarriers, TMEM slot and flags after the stages
+    static constexpr int BAR_BYTES = 1024;          // mbarriers, TMEM slot, flags and the finisher's 64 floats
 };
 
 // The CTA's pieces: (A tile, B tile, K-block range). Identical sequence in every role of the CTA.
@@ -169,14 +177,50 @@ struct TcPieces {
     }
 };
 
+// First K-block unit of CTA c in the stream-K partition (the formula TcPieces uses), and the CTA holding unit u.
+__device__ __forceinline__ int tc_range_lo(const TcArgs &P, int c) {
+    return (int)((long long)P.units * c / gridDim.x);
+}
+__device__ __forceinline__ int tc_owner(const TcArgs &P, int u) {
+    int c = (int)((long long)u * gridDim.x / P.units);
+    if (c + 1 < (int)gridDim.x && tc_range_lo(P, c + 1) <= u) ++c;
+    return c;
+}
+// Split-K slot words: CTA c's contribution (its first piece, when that piece is not a tile's head), row r of the
+// tile, token-row pair h: {acc[2h], 1, acc[2h + 1], 1} (an LL word: each 8-byte half carries its own flag).
+__device__ __forceinline__ uint4 *tc_slot(const TcArgs &P, int c, int h, int r) {
+    return P.slots + ((size_t)c * ((P.M + 1) >> 1) + h) * TC_BM + r;
+}
+
 __device__ __forceinline__ unsigned char *tc_align1024(unsigned char *p) {
     return reinterpret_cast<unsigned char *>(((uintptr_t)p + 1023) & ~(uintptr_t)1023);
 }
 
-// Output finisher of the decode orientation: thread = output feature n, acc[m] for the token rows.
+// Output finisher of the decode orientation: thread = output feature n, acc[m] for the token rows. Finisher
+// interface: on_start(sm) once per epilogue thread after pdl_wait (sm: 64 floats of shared memory the finisher may
+// fill, then the epilogue warps synchronise); prep(P, n) before the piece's accumulators are ready (global loads whose
+// latency then hides behind the MMAs); operator()(P, n, nok, acc, prep) with the accumulators.
 template <typename T, int BN>
 struct TcOutEpi {
-    __device__ __forceinline__ void operator()(const TcArgs &P, int n, bool nok, const int (&acc)[BN]) const {
+    struct Prep {
+        float swn, bn;
+    };
+    float *sa_sm;   // the token scales, loaded once per CTA
+    __device__ __forceinline__ void on_start(const TcArgs &P, float *sm) {
+        sa_sm = sm;
+        const int t = threadIdx.x - 64;
+        if (!P.s32_out && t < P.M) sm[t] = P.sa[P.sa_rows ? t : 0];
+    }
+    __device__ __forceinline__ Prep prep(const TcArgs &P, int n) const {
+        Prep r{0.f, 0.f};
+        if (!P.s32_out && n < P.N) {   // scales and bias only in dequant mode (NULL for int32 output)
+            r.swn = P.sw[P.sw_rows ? n : 0];
+            if (P.bias) r.bn = t2f<T>(reinterpret_cast<const T *>(P.bias)[n]);
+        }
+        return r;
+    }
+    __device__ __forceinline__ void operator()(const TcArgs &P, int n, bool nok, const int (&acc)[BN],
+                                               const Prep &pr) const {
         if (!nok) return;
         if (P.s32_out) {
 #pragma unroll
@@ -184,14 +228,11 @@ struct TcOutEpi {
                 if (m < P.M) reinterpret_cast<int *>(P.out)[(size_t)m * P.N + n] = acc[m];
             return;
         }
-        // scales and bias only in dequant mode (they are NULL for int32 output)
-        const float swn = P.sw[P.sw_rows ? n : 0];
-        const float bn = P.bias ? t2f<T>(reinterpret_cast<const T *>(P.bias)[n]) : 0.f;
 #pragma unroll
         for (int m = 0; m < BN; ++m) {
             if (m >= P.M) continue;
-            const float sam = P.sa[P.sa_rows ? m : 0];
-            const float v = P.bias ? dequant1b(acc[m], sam, swn, bn) : dequant1(acc[m], sam, swn);
+            const float sam = sa_sm[m];
+            const float v = P.bias ? dequant1b(acc[m], sam, pr.swn, pr.bn) : dequant1(acc[m], sam, pr.swn);
             reinterpret_cast<T *>(P.out)[(size_t)m * P.N + n] = f2t<T>(v);
         }
     }
@@ -245,7 +286,7 @@ __device__ __forceinline__ void tc_prefill_epilogue(const TcArgs &P, int m, int 
 // TMEM is freed (a __syncthreads is the last thing it does, so the caller may reuse the shared memory).
 template <typename T, int BN, bool SWAP, int KBS, class Fin>
 __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtensorMap *tmap_b, const TcArgs &P,
-                                         unsigned char *smem_raw, const Fin &fin) {
+                                         unsigned char *smem_raw, Fin fin) {
     using Lay = TcLayout<BN, KBS>;
     static_assert(!SWAP || BN <= 32, "decode orientation holds at most 32 token rows");
     unsigned char *tiles = tc_align1024(smem_raw);
@@ -256,10 +297,11 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
     uint64_t *tempty = tfull + 2;    // [2]
     uint64_t *drain = tempty + 2;    // [1]: the MMA issuer's last commit
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
-    volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 4);   // [0] abort, [1] this piece finishes
+    volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 4);   // [0] abort
+    float *epi_sm = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(full) + 512);   // [64] for the finisher
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint64_t deadline = globaltimer() + P.timeout_ns;
+    pdl_launch_dependents();   // once every CTA of this grid got here, the next kernel may take SMs as they free up
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
@@ -285,12 +327,36 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+    // Everything but the weight stream depends on earlier kernels (activations, scales, scratch, outputs): only the
+    // producer thread runs ahead, loading the weight half of its first stages before it waits.
+    const bool producer = (warp == 0 && lane == 0);
+    if (!producer) pdl_wait();
+    uint64_t deadline = globaltimer() + P.timeout_ns;   // the bound starts once the kernel's inputs are ready
 
     int ta, tb, kb0, kb1;
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();   // decode weights are read once per call
+            // (1) before the wait: the weight (SWAP) half of the first S stages -- their ring slots are free and
+            // nothing an earlier kernel writes is read
+            int pre = 0;
+            if (SWAP) {
+                TcPieces pp(P);
+                while (pre < S && pp.next(P, ta, tb, kb0, kb1)) {
+                    for (int kb = kb0; kb < kb1 && pre < S; kb += KBS, ++pre) {
+                        const int nb = min(KBS, kb1 - kb);
+                        mbar_arrive_expect_tx(&full[pre], (uint32_t)(nb * Lay::KB_BYTES));
+                        unsigned char *st = tiles + (size_t)pre * Lay::STAGE;
+                        for (int j = 0; j < nb; ++j)
+                            tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[pre],
+                                             pol);
+                    }
+                }
+            }
+            pdl_wait();
+            deadline = globaltimer() + P.timeout_ns;
+            // (2) the stream: activations for the pre-issued stages, then whole stages
             int it = 0;
             bool dead = false;
             TcPieces pc(P);
@@ -299,19 +365,22 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                     const int nb = min(KBS, kb1 - kb);
                     const int s = it % S;
                     const uint32_t r = (uint32_t)(it / S);
-                    if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
-                        if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x10u);
-                        flags[0] = 1;
-                        dead = true;
-                        break;
-                    }
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * Lay::KB_BYTES));
                     unsigned char *st = tiles + (size_t)s * Lay::STAGE;
-                    for (int j = 0; j < nb; ++j) {
-                        if (SWAP)
-                            tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s], pol);
-                        else
-                            tma_load_2d(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s]);
+                    if (it >= pre) {
+                        if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
+                            if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x10u);
+                            flags[0] = 1;
+                            dead = true;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * Lay::KB_BYTES));
+                        for (int j = 0; j < nb; ++j) {
+                            if (SWAP)
+                                tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s],
+                                                 pol);
+                            else
+                                tma_load_2d(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s]);
+                        }
                     }
                     for (int j = 0; j < nb; ++j)
                         tma_load_2d(st + KBS * Lay::A_BYTES + j * Lay::B_BYTES, tmap_b, (kb + j) * TC_BK, tb * BN,
@@ -370,25 +439,69 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
     } else {
         // ---------------- epilogue warps 2..5 ----------------
         const int q = warp & 3;   // TMEM lane quarter this warp may access
+        const int row = q * 32 + lane;   // row of the 128-row A tile this thread holds
+        fin.on_start(P, epi_sm);  // after pdl_wait: e.g. the token scales, the communicator's call number
+        named_sync(TC_EPI_BAR, 128);
+        const int hw = (P.M + 1) >> 1;
         int ut = 0;
         TcPieces pc(P);
         while (pc.next(P, ta, tb, kb0, kb1)) {
             const int buf = ut & 1;
             const uint32_t use = (uint32_t)(ut >> 1);
             ++ut;
-            if (!flags[0] && !mbar_wait(&tfull[buf], use & 1u, deadline)) {
-                report(P.status, ST_PIPE_TIMEOUT | 0x40u);
-                flags[0] = 1;
-            }
-            tc_fence_after();
-            const int arow = ta * TC_BM + q * 32 + lane;   // row of operand A this thread holds
+            const int arow = ta * TC_BM + row;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
             if constexpr (!SWAP) {
+                if (!flags[0] && !mbar_wait(&tfull[buf], use & 1u, deadline)) {
+                    report(P.status, ST_PIPE_TIMEOUT | 0x40u);
+                    flags[0] = 1;
+                }
+                tc_fence_after();
                 tc_prefill_epilogue<T, BN>(P, arow, tb, taddr);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             } else {
+                const int n = arow;
+                const bool nok = n < P.N;
+                const bool whole = (kb0 == 0 && kb1 == P.nkb);
+                const bool head = (kb0 == 0 && !whole);
+                const auto pr = fin.prep(P, n);   // scale loads in flight while the MMAs run
+                int acc[BN];
+#pragma unroll
+                for (int m = 0; m < BN; ++m) acc[m] = 0;
+                if (head) {
+                    // This CTA finishes the tile: the CTAs holding its other K blocks (each one's first piece) left
+                    // their sums in their slots, normally long ago -- collect them while this piece's MMAs still run,
+                    // and clear the slots for the next launch.
+                    const int clast = tc_owner(P, ta * P.nkb + P.nkb - 1);
+                    for (int c = blockIdx.x + 1; c <= clast; ++c) {
+                        uint4 v[BN / 2];
+#pragma unroll
+                        for (int h = 0; h < BN / 2; ++h)   // all of the slot's words in flight at once
+                            if (h < hw) v[h] = ld_volatile16(tc_slot(P, c, h, row));
+#pragma unroll
+                        for (int h = 0; h < BN / 2; ++h) {
+                            if (h >= hw) continue;
+                            uint32_t it = 0;
+                            while (v[h].y != 1u || v[h].w != 1u) {
+                                if ((++it & 255u) == 0 && globaltimer() > deadline) {
+                                    report(P.status, ST_PIPE_TIMEOUT | 0x50u);
+                                    break;
+                                }
+                                v[h] = ld_volatile16(tc_slot(P, c, h, row));
+                            }
+                            acc[2 * h] += (int)v[h].x;
+                            acc[2 * h + 1] += (int)v[h].z;
+                            *tc_slot(P, c, h, row) = make_uint4(0u, 0u, 0u, 0u);
+                        }
+                    }
+                }
+                if (!flags[0] && !mbar_wait(&tfull[buf], use & 1u, deadline)) {
+                    report(P.status, ST_PIPE_TIMEOUT | 0x40u);
+                    flags[0] = 1;
+                }
+                tc_fence_after();
                 uint32_t r[32];
                 if (BN == 16)
                     tmem_ld16(taddr, r);
@@ -398,44 +511,17 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                 tc_fence_before();   // this warp's TMEM reads are done: the MMA may refill the buffer
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
-                const int n = arow;
-                const bool nok = n < P.N;
-                int acc[BN];
 #pragma unroll
-                for (int m = 0; m < BN; ++m) acc[m] = (int)r[m];
-                if (kb0 == 0 && kb1 == P.nkb) {   // the whole K range of the tile in this CTA
-                    fin(P, n, nok, acc);
-                    continue;
-                }
-                // split tile: add this piece's partial sums, then the CTA whose K blocks complete the tile finishes it
-                if (nok) {
+                for (int m = 0; m < BN; ++m) acc[m] += (int)r[m];
+                if (whole || head) {
+                    fin(P, n, nok, acc, pr);
+                } else {
+                    // the CTA's first piece, inside a tile another CTA finishes: leave its sums in this CTA's slot
 #pragma unroll
-                    for (int m = 0; m < BN; ++m)
-                        if (m < P.M) atomicAdd(&P.scratch[(size_t)m * P.N + n], acc[m]);
+                    for (int h = 0; h < BN / 2; ++h)
+                        if (h < hw) ll_store(tc_slot(P, blockIdx.x, h, row), (uint32_t)acc[2 * h],
+                                             (uint32_t)acc[2 * h + 1], 1u);
                 }
-                __threadfence();
-                named_sync(TC_EPI_BAR, 128);
-                if (threadIdx.x == TC_EPI_LEAD) {
-                    const int add = kb1 - kb0;
-                    const int old = atomicAdd(&P.tickets[ta], add);
-                    flags[1] = (old + add == P.nkb) ? 1 : 0;
-                }
-                named_sync(TC_EPI_BAR, 128);
-                const bool last = flags[1] != 0;
-                if (!last) continue;
-                __threadfence();
-                if (nok) {
-#pragma unroll
-                    for (int m = 0; m < BN; ++m) {
-                        if (m >= P.M) continue;
-                        int *sp = &P.scratch[(size_t)m * P.N + n];
-                        acc[m] = __ldcg(sp);
-                        *sp = 0;
-                    }
-                }
-                fin(P, n, nok, acc);
-                named_sync(TC_EPI_BAR, 128);   // every thread has read flags[1] and its sums: the ticket may restart
-                if (threadIdx.x == TC_EPI_LEAD) atomicExch(&P.tickets[ta], 0);
             }
         }
     }
@@ -480,7 +566,7 @@ inline int decode_kbs() {
 }
 
 // Decode stream-K work: weights w [N, K] as operand A, M token rows as operand B.
-inline void tc_decode_args(TcArgs &P, int M, int N, int K) {
+inline void tc_decode_args(TcArgs &P, int M, int N, int K) {  // (the launch grid is min(SMs, units))
     P.n_tiles_a = (N + TC_BM - 1) / TC_BM;
     P.n_tiles_b = 1;
     P.nkb = (K + TC_BK - 1) / TC_BK;
@@ -490,9 +576,9 @@ inline void tc_decode_args(TcArgs &P, int M, int N, int K) {
     P.N = N;
 }
 
-// split-K scratch of the decode orientation: int32 [M, N], then one ticket per 128-row weight tile
-inline size_t tc_decode_scratch_bytes(int M, int N) {
-    return ((size_t)M * N * 4 + (size_t)((N + TC_BM - 1) / TC_BM) * 4 + 255) & ~(size_t)255;
+// split-K slots of the decode orientation: one contribution of up to 128 x M int32 per CTA, as 16-byte LL words
+inline size_t tc_decode_slot_bytes(int M, int grid) {
+    return (size_t)grid * ((M + 1) / 2) * TC_BM * 16;
 }
 
 }  // namespace vt

@@ -134,46 +134,75 @@ __device__ __forceinline__ float group_combine(const CommView &c, int m, int g, 
 }
 
 // Phase 2 of the fused kernel (all threads of every CTA call it once the GEMM phase has pushed this rank's values):
-// CTA m * E + g owns columns [w0, w1) (in 4-column LL words) of token row m. smem: free shared memory of at least
-// ceil(N / 4 / E) * 16 bytes; red: 32 floats; bcast: one float.
+// CTA m * E + g owns columns [w0, w1) (in 4-column LL words) of token row m; the other CTAs return at once. Loads are
+// issued in batches (KW words per thread, all ranks' LL words of a batch at once) so a batch costs about one memory
+// round trip, not one per word. E = 1 (the usual case up to two ranks) needs no cross-CTA combine at all.
+// smem: free shared memory of at least ceil(N / 4 / E) * 16 bytes; red: 32 floats; bcast: one float.
 template <typename T>
 __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommView &c, unsigned seq, unsigned p,
                                              unsigned char *smem, float *red, float *bcast) {
-    const int M = P.M, N = P.N, E = P.E, W4 = N >> 2;
-    if ((int)blockIdx.x < M * E) {
-        const int m = blockIdx.x / E, g = blockIdx.x - m * E;
-        const int w0 = (int)((long long)W4 * g / E), w1 = (int)((long long)W4 * (g + 1) / E);
-        float *hbuf = reinterpret_cast<float *>(smem);
-        const uint64_t deadline = globaltimer() + P.peer_timeout;
-        bool dead = false;
-        float ss = 0.0f;
-        for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
-            const int word = w0 + i;
-            const size_t off = ((size_t)m * W4 + word) * 16;
-            float s[4];
-            for (int r = 0; r < c.world; ++r) {
-                uint2 d = make_uint2(0u, 0u);
-                if (!dead && !ll_wait(c.ll_slot(c.rank, p, r) + off, seq, deadline, d)) {
-                    report(c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
-                    dead = true;
+    constexpr int KW = 4;
+    const int M = P.M, N = P.N, E = P.E, W4 = N >> 2, world = c.world;
+    if ((int)blockIdx.x >= M * E) return;
+    const int m = blockIdx.x / E, g = blockIdx.x - m * E;
+    const int w0 = (int)((long long)W4 * g / E), w1 = (int)((long long)W4 * (g + 1) / E);
+    const int nw = w1 - w0, nt = blockDim.x, tid = threadIdx.x;
+    float *hbuf = reinterpret_cast<float *>(smem);
+    const uint64_t deadline = globaltimer() + P.peer_timeout;
+    bool dead = false;
+    float ss = 0.0f;
+    for (int b = 0; b < nw; b += nt * KW) {
+        uint2 ru[KW];
+        if (P.residual) {   // this batch's residual words: independent of the peers, in flight with the LL polls
+#pragma unroll
+            for (int k = 0; k < KW; ++k) {
+                const int i = b + tid + k * nt;
+                if (i < nw) ru[k] = *reinterpret_cast<const uint2 *>(P.residual + (size_t)m * N + (size_t)(w0 + i) * 4);
+            }
+        }
+        float s[KW][4];
+        for (int r = 0; r < world; ++r) {   // ranks in order: the float sums are identical on every rank
+            const char *slot = c.ll_slot(c.rank, p, r) + ((size_t)m * W4 + w0) * 16;
+            uint4 v[KW];
+#pragma unroll
+            for (int k = 0; k < KW; ++k) {
+                const int i = b + tid + k * nt;
+                if (i < nw) v[k] = ld_volatile16(slot + (size_t)i * 16);
+            }
+#pragma unroll
+            for (int k = 0; k < KW; ++k) {
+                const int i = b + tid + k * nt;
+                if (i >= nw) continue;
+                uint32_t it = 0;
+                while (!dead && (v[k].y != seq || v[k].w != seq)) {
+                    if ((++it & 255u) == 0 && globaltimer() > deadline) {
+                        report(c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
+                        dead = true;
+                        break;
+                    }
+                    v[k] = ld_volatile16(slot + (size_t)i * 16);
                 }
-                const float2 x0 = unpack2<T>(d.x), x1 = unpack2<T>(d.y);
+                const float2 x0 = unpack2<T>(v[k].x), x1 = unpack2<T>(v[k].z);
                 if (r == 0) {
-                    s[0] = x0.x; s[1] = x0.y; s[2] = x1.x; s[3] = x1.y;
+                    s[k][0] = x0.x; s[k][1] = x0.y; s[k][2] = x1.x; s[k][3] = x1.y;
                 } else {
-                    s[0] += x0.x; s[1] += x0.y; s[2] += x1.x; s[3] += x1.y;
+                    s[k][0] += x0.x; s[k][1] += x0.y; s[k][2] += x1.x; s[k][3] += x1.y;
                 }
             }
-            const size_t e0 = (size_t)m * N + (size_t)word * 4;
+        }
+#pragma unroll
+        for (int k = 0; k < KW; ++k) {
+            const int i = b + tid + k * nt;
+            if (i >= nw) continue;
+            const size_t e0 = (size_t)m * N + (size_t)(w0 + i) * 4;
             if (P.reduced)
-                *reinterpret_cast<uint2 *>(P.reduced + e0) = make_uint2(pack2<T>(s[0], s[1]), pack2<T>(s[2], s[3]));
+                *reinterpret_cast<uint2 *>(P.reduced + e0) =
+                    make_uint2(pack2<T>(s[k][0], s[k][1]), pack2<T>(s[k][2], s[k][3]));
             if (P.residual) {
-                uint2 *rp = reinterpret_cast<uint2 *>(P.residual + e0);
-                const uint2 ru = *rp;
-                const float2 r0 = unpack2<T>(ru.x), r1 = unpack2<T>(ru.y);
-                const float h0 = rnd<T>(rnd<T>(s[0]) + r0.x), h1 = rnd<T>(rnd<T>(s[1]) + r0.y);
-                const float h2 = rnd<T>(rnd<T>(s[2]) + r1.x), h3 = rnd<T>(rnd<T>(s[3]) + r1.y);
-                *rp = make_uint2(pack2<T>(h0, h1), pack2<T>(h2, h3));
+                const float2 r0 = unpack2<T>(ru[k].x), r1 = unpack2<T>(ru[k].y);
+                const float h0 = rnd<T>(rnd<T>(s[k][0]) + r0.x), h1 = rnd<T>(rnd<T>(s[k][1]) + r0.y);
+                const float h2 = rnd<T>(rnd<T>(s[k][2]) + r1.x), h3 = rnd<T>(rnd<T>(s[k][3]) + r1.y);
+                *reinterpret_cast<uint2 *>(P.residual + e0) = make_uint2(pack2<T>(h0, h1), pack2<T>(h2, h3));
                 hbuf[4 * i] = h0;
                 hbuf[4 * i + 1] = h1;
                 hbuf[4 * i + 2] = h2;
@@ -181,35 +210,54 @@ __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommVi
                 ss += h0 * h0 + h1 * h1 + h2 * h2 + h3 * h3;
             }
         }
-        if (P.residual) {
-            ss = block_sum_n(ss, red);
-            const float tot = group_combine(c, m, g, E, 0, ss, false, seq, deadline, bcast);
-            const float rs = __frsqrt_rn(__fdiv_rn(tot, (float)N) + P.eps);
-            float amax = 0.0f;
-            for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
-                const uint2 wu = *reinterpret_cast<const uint2 *>(P.norm_w + (size_t)(w0 + i) * 4);
-                const float2 wa = unpack2<T>(wu.x), wb = unpack2<T>(wu.y);
-                const float y0 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i], rs), wa.x));
-                const float y1 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 1], rs), wa.y));
-                const float y2 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 2], rs), wb.x));
-                const float y3 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 3], rs), wb.y));
-                hbuf[4 * i] = y0;
-                hbuf[4 * i + 1] = y1;
-                hbuf[4 * i + 2] = y2;
-                hbuf[4 * i + 3] = y3;
-                amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
-            }
-            amax = block_max_n(amax, red);
-            amax = group_combine(c, m, g, E, 1, amax, true, seq, deadline, bcast);
-            const float inv = quant_inv(amax);
-            if (g == 0 && threadIdx.x == 0) P.scales[m] = __fdiv_rn(amax, 127.0f);
-            for (int i = threadIdx.x; i < w1 - w0; i += blockDim.x) {
-                *reinterpret_cast<char4 *>(P.q + (size_t)m * N + (size_t)(w0 + i) * 4) =
-                    make_char4(quant1(hbuf[4 * i], inv), quant1(hbuf[4 * i + 1], inv),
-                               quant1(hbuf[4 * i + 2], inv), quant1(hbuf[4 * i + 3], inv));
-            }
+    }
+    if (!P.residual) return;
+    ss = block_sum_n(ss, red);
+    const float tot = E > 1 ? group_combine(c, m, g, E, 0, ss, false, seq, deadline, bcast) : ss;
+    const float rs = __frsqrt_rn(__fdiv_rn(tot, (float)N) + P.eps);
+    float amax = 0.0f;
+    for (int b = 0; b < nw; b += nt * KW) {
+        uint2 wu[KW];
+#pragma unroll
+        for (int k = 0; k < KW; ++k) {
+            const int i = b + tid + k * nt;
+            if (i < nw) wu[k] = *reinterpret_cast<const uint2 *>(P.norm_w + (size_t)(w0 + i) * 4);
+        }
+#pragma unroll
+        for (int k = 0; k < KW; ++k) {
+            const int i = b + tid + k * nt;
+            if (i >= nw) continue;
+            const float2 wa = unpack2<T>(wu[k].x), wb = unpack2<T>(wu[k].y);
+            const float y0 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i], rs), wa.x));
+            const float y1 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 1], rs), wa.y));
+            const float y2 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 2], rs), wb.x));
+            const float y3 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 3], rs), wb.y));
+            hbuf[4 * i] = y0;
+            hbuf[4 * i + 1] = y1;
+            hbuf[4 * i + 2] = y2;
+            hbuf[4 * i + 3] = y3;
+            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
         }
     }
+    amax = block_max_n(amax, red);
+    if (E > 1) amax = group_combine(c, m, g, E, 1, amax, true, seq, deadline, bcast);
+    const float inv = quant_inv(amax);
+    if (g == 0 && tid == 0) P.scales[m] = __fdiv_rn(amax, 127.0f);
+    for (int i = tid; i < nw; i += nt) {
+        *reinterpret_cast<char4 *>(P.q + (size_t)m * N + (size_t)(w0 + i) * 4) =
+            make_char4(quant1(hbuf[4 * i], inv), quant1(hbuf[4 * i + 1], inv), quant1(hbuf[4 * i + 2], inv),
+                       quant1(hbuf[4 * i + 3], inv));
+    }
+}
+
+// CTAs per token row in the row epilogue: one up to two ranks (no cross-CTA combine); more ranks bring world x more
+// LL words per row, shared by world / 2 CTAs (at most the mailbox's groups and one CTA per row per SM).
+inline int row_ctas(int world, int M, int grid) {
+    int E = world / 2;
+    if (E < 1) E = 1;
+    if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
+    while (E > 1 && E * M > grid) --E;
+    return E;
 }
 
 template <typename T, int MT>
@@ -237,18 +285,30 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
 // n .. n + 3 (gathered by shuffles) to every rank's receive slot.
 template <typename T, int BN>
 struct TcLLPushEpi {
+    struct Prep {
+        float swn;
+    };
     const CommView *c;
     const float *sa, *sw;
     int M, N;
-    unsigned seq, p;
-    __device__ __forceinline__ void operator()(const TcArgs &, int n, bool nok, const int (&acc)[BN]) const {
+    unsigned *s_seq;   // shared: this call's sequence number, read after pdl_wait
+    float *sa_sm;      // shared: the token scales
+    __device__ __forceinline__ void on_start(const TcArgs &, float *sm) {
+        sa_sm = sm;
+        const int t = threadIdx.x - TC_EPI_LEAD;
+        if (t < M) sm[t] = sa[t];
+        if (t == 0) *s_seq = *reinterpret_cast<volatile unsigned *>(c->seq_ptr()) + 1u;
+    }
+    __device__ __forceinline__ Prep prep(const TcArgs &, int n) const { return Prep{n < N ? sw[n] : 0.0f}; }
+    __device__ __forceinline__ void operator()(const TcArgs &, int n, bool nok, const int (&acc)[BN],
+                                               const Prep &pr) const {
         const int W4 = N >> 2, world = c->world, rank = c->rank;
         const int lane = threadIdx.x & 31;
-        const float swn = nok ? sw[n] : 0.0f;
+        const unsigned seq = *s_seq, p = seq & 1u;
 #pragma unroll
         for (int m = 0; m < BN; ++m) {
             if (m >= M) break;   // M is uniform: the whole warp leaves together
-            const float v = nok ? dequant1(acc[m], sa[m], swn) : 0.0f;
+            const float v = nok ? dequant1(acc[m], sa_sm[m], pr.swn) : 0.0f;
             const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
             const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
             const float v3 = __shfl_down_sync(0xffffffffu, v, 3);
@@ -263,6 +323,8 @@ struct TcLLPushEpi {
     }
 };
 
+// Launched with programmatic dependent launch: the call number is read after pdl_wait (by the epilogue lead in
+// fin.on_start), not at kernel entry, since the previous call on this communicator may still be finishing then.
 template <typename T, int BN, int KBS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tp_row_linear_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
@@ -272,10 +334,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ float red[32];
     __shared__ float bcast;
     const CommView &c = P.c;
-    const unsigned seq = comm_begin(c, &s_seq);
-    const unsigned p = seq & 1u;
-    TcLLPushEpi<T, BN> push{&c, P.sa, P.sw, P.M, P.N, seq, p};
+    TcLLPushEpi<T, BN> push{&c, P.sa, P.sw, P.M, P.N, &s_seq, nullptr};
     tc_phase<T, BN, true, KBS>(&tmap_w, &tmap_a, G, smem_raw, push);   // ends with __syncthreads
+    const unsigned seq = s_seq, p = seq & 1u;
     row_epilogue<T>(P, c, seq, p, tc_align1024(smem_raw), red, &bcast);   // the stage ring is free now
     comm_end(c, seq);
 }
@@ -288,14 +349,12 @@ static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     if (!tc_make_map(&mw, P.w, P.N, P.K, TC_BM) || !tc_make_map(&ma, P.a, P.M, P.K, BN)) return VT_EARG;
     TcArgs G{};
     tc_decode_args(G, P.M, P.N, P.K);
-    if (G.n_tiles_a > COMM_TICKETS) return VT_EARG;
     G.sa = P.sa;
     G.sw = P.sw;
     G.sa_rows = 1;
     G.sw_rows = 1;
     char *local = P.c.base[P.c.rank];
-    G.scratch = reinterpret_cast<int *>(local + P.c.L.scratch_off);
-    G.tickets = reinterpret_cast<int *>(local + COMM_TICKET_OFF);
+    G.slots = reinterpret_cast<uint4 *>(local + P.c.L.scratch_off);
     G.status = reinterpret_cast<unsigned *>(local + 128);
     G.timeout_ns = P.pipe_timeout;
     const int stages = tc_stages<BN, KBS>(dev);
@@ -311,14 +370,12 @@ static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     }
     int g = num_sms(dev);
     if (g > G.units) g = G.units;
-    int E = g / P.M;
-    if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
-    if (E < 1) return VT_EARG;
+    if (P.M > g || tc_decode_slot_bytes(P.M, g) > P.c.L.scratch_bytes) return VT_EARG;
+    const int E = row_ctas(P.c.world, P.M, g);
     P.E = E;
     // row epilogue buffer: ceil(N / 4 / E) words of 4 floats in the (free) stage ring
     if ((size_t)((P.N / 4 + E - 1) / E) * 16 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
-    tp_row_linear_tc_kernel<T, BN, KBS><<<g, TC_THREADS, smem, s>>>(mw, ma, G, P);
-    return (int)cudaGetLastError();
+    return launch_k(tp_row_linear_tc_kernel<T, BN, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, mw, ma, G, P);
 }
 
 template <typename T, int BN>
@@ -347,10 +404,10 @@ static int launch_fused(FusedArgs<T> P, cudaStream_t s) {
         attr_set[dev] = true;
     }
     const int G = num_sms(dev);
-    int E = G / P.M;
-    if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
-    if (E < 1) return VT_EARG;
+    if (P.M > G) return VT_EARG;
+    const int E = row_ctas(P.c.world, P.M, G);
     P.E = E;
+    if ((size_t)((P.N / 4 + E - 1) / E) * 16 + GV_HDR > (size_t)smem) return VT_EARG;   // row epilogue buffer
     CUtensorMap wmap;
     if (!make_map_i8(&wmap, P.w, P.N, P.K, GV_SEGB / 2, GV_RB, CU_TENSOR_MAP_SWIZZLE_NONE)) return VT_EARG;
     tp_row_linear_kernel<T, MT><<<G, GV_THREADS, smem, s>>>(wmap, P);

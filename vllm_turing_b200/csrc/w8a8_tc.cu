@@ -49,8 +49,7 @@ static int launch_tc(const CUtensorMap &ma, const CUtensorMap &mb, TcArgs P, cud
     }
     int g = num_sms(dev);
     if (g > P.units) g = P.units;
-    tc_gemm_kernel<T, BN, SWAP, KBS><<<g, TC_THREADS, smem, s>>>(ma, mb, P);
-    return (int)cudaGetLastError();
+    return launch_k(tc_gemm_kernel<T, BN, SWAP, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, ma, mb, P);
 }
 
 // Prefill orientation: a [M, K] activations, w [N, K] weights, whole 128 x 256 tiles per CTA.
@@ -88,7 +87,7 @@ static int small_kbs(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs 
 }
 
 // Decode orientation: weights as operand A, M <= 32 token rows as operand B, stream-K over the SMs. scratch holds
-// tc_decode_scratch_bytes(M, N) zeroed bytes (partial sums, then tickets); the kernel leaves them zeroed.
+// decode_ws(M) zeroed bytes (the split-K slots); the kernel leaves them zeroed.
 template <typename T>
 static int small_gemm(const void *a, const void *w, const float *sa, const float *sw, const void *bias, void *out,
                       int M, int N, int K, int sa_rows, int sw_rows, int s32, void *scratch, unsigned *status,
@@ -104,14 +103,16 @@ static int small_gemm(const void *a, const void *w, const float *sa, const float
     P.sa_rows = sa_rows;
     P.sw_rows = sw_rows;
     P.out = out;
-    P.scratch = (int *)scratch;
-    P.tickets = P.scratch + (size_t)M * N;
+    P.slots = (uint4 *)scratch;
     P.s32_out = s32;
     P.timeout_ns = pipe_timeout_ns();
     P.status = status;
     if (BN == 16) return small_kbs<T, 16>(ma, mb, P, s);
     return small_kbs<T, 32>(ma, mb, P, s);
 }
+
+// split-K slot bytes for M token rows on this device (the grid is at most one CTA per SM)
+static size_t decode_ws(int M) { return tc_decode_slot_bytes(M, num_sms(cur_device())); }
 
 static bool tc_args_ok(const void *a, const void *w, int M, int N, int K) {
     return M >= 1 && N >= 1 && K >= 16 && (K & 15) == 0 && ((uintptr_t)a & 15) == 0 && ((uintptr_t)w & 15) == 0;
@@ -140,14 +141,14 @@ int w8a8_mma(const void *a, const void *w, const void *sa, const void *sw, const
     cudaStream_t s = (cudaStream_t)stream;
     void *scratch;
     unsigned *status;
-    if (int rc = ws_acquire(tc_decode_scratch_bytes(M, N), s, &scratch, &status)) return rc;
+    if (int rc = ws_acquire(decode_ws(M), s, &scratch, &status)) return rc;
     if (dtype == 0)
         return mma_dequant<__half>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, scratch, status, s);
     return mma_dequant<__nv_bfloat16>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, scratch, status, s);
 }
 
 // Bytes of zeroed workspace w8a8_mma_ws needs for these shapes (256-byte status header included).
-size_t w8a8_mma_ws_bytes(int M, int N) { return 256 + tc_decode_scratch_bytes(M, N); }
+size_t w8a8_mma_ws_bytes(int M, int N) { return (void)N, 256 + decode_ws(M); }
 
 // w8a8_mma with a caller-owned workspace of w8a8_mma_ws_bytes(M, N) bytes, zeroed once before its first use (the
 // kernel leaves it zeroed); calls sharing a workspace must be stream-ordered. The first 256 bytes hold the status word.
@@ -189,7 +190,7 @@ int vt_gemm_s32(const void *a, const void *w, void *acc, int M, int N, int K, vo
     void *scratch;
     unsigned *status;
     if (M <= 32) {
-        if (int rc = ws_acquire(tc_decode_scratch_bytes(M, N), s, &scratch, &status)) return rc;
+        if (int rc = ws_acquire(decode_ws(M), s, &scratch, &status)) return rc;
         return small_gemm<__nv_bfloat16>(a, w, nullptr, nullptr, nullptr, acc, M, N, K, 1, 1, 1, scratch, status, s);
     }
     if (int rc = ws_acquire(0, s, &scratch, &status)) return rc;
