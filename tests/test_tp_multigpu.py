@@ -79,7 +79,8 @@ def _worker(rank, world, port, q):
                 check(torch.equal(g[r * m:(r + 1) * m].cpu(), exp), f"all_gather m={m} slot {r}")
 
         # ---- fused row-linear ----
-        for (M, N, K) in ((16, 5120, 8704), (5, 5120, 17408 // world), (1, 5120, 17408 // world)):
+        for (M, N, K) in ((16, 5120, 8704), (5, 5120, 17408 // world), (1, 5120, 17408 // world),
+                          (32, 5120, 17408 // world), (24, 5120, 8704)):
             lis = [make_layer_inputs(M, N, K, seed=M, rank=r) for r in range(world)]
             me = lis[rank]
             res = me.residual.to(dev)
@@ -98,6 +99,44 @@ def _worker(rank, world, port, q):
             q0 = qd.clone().cpu()
             dist.broadcast(q0, src=0)
             check(torch.equal(q0, qd.cpu()), f"fused q differs from rank 0 (M={M})")
+
+        # ---- fused row-linear captured in a CUDA graph (three chained calls), replayed with fresh inputs ----
+        M, N, K = 5, 5120, 17408 // world
+        ws = [make_layer_inputs(M, N, K, seed=70 + j, rank=rank) for j in range(3)]
+        dw = [(w.w.to(dev), w.sw.to(dev)) for w in ws]
+        a_in, sa_in = ws[0].a.to(dev), ws[0].sa.to(dev)
+        res_g = ws[0].residual.to(dev)
+        nw_g = ws[0].norm_w.to(dev)
+        qs = [torch.empty(M, N, dtype=torch.int8, device=dev) for _ in range(3)]
+        ss = [torch.empty(M, 1, dtype=torch.float32, device=dev) for _ in range(3)]
+
+        def chain():
+            for j in range(3):   # each call's int8 output feeds nothing: every call reads the same a, sa
+                comm.row_linear(a_in, dw[j][0], sa_in, dw[j][1], residual=res_g, norm_w=nw_g, eps=1e-6,
+                                q=qs[j], scales=ss[j])
+        chain()
+        torch.cuda.synchronize()
+        dist.barrier()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            chain()
+        allw = [[make_layer_inputs(M, N, K, seed=70 + j, rank=r) for r in range(world)] for j in range(3)]
+        for it in range(3):
+            lis = [make_layer_inputs(M, N, K, seed=200 + it, rank=r) for r in range(world)]
+            a_in.copy_(lis[rank].a.to(dev))
+            sa_in.copy_(lis[rank].sa.to(dev))
+            res_g.copy_(lis[rank].residual.to(dev))
+            r_host = O.to_bits(lis[rank].residual)
+            gr.replay()
+            torch.cuda.synchronize()
+            for j in range(3):
+                r_host, qo, so, _ = O.row_linear_tp([li.a.numpy() for li in lis], [x.w.numpy() for x in allw[j]],
+                                                    [li.sa.numpy() for li in lis], [x.sw.numpy() for x in allw[j]],
+                                                    r_host, O.to_bits(ws[0].norm_w), 1e-6, 1)
+                d = np.abs(qs[j].cpu().numpy().astype(np.int32) - qo.astype(np.int32))
+                check(d.max() <= 1, f"graph replay {it} fused call {j}: q off by {d.max()}")
+            check(np.array_equal(O.to_bits(res_g.cpu()), r_host), f"graph replay {it}: residual")
+        del gr
 
         # ---- stress: back-to-back mixed calls without host syncs ----
         xs = [_parts(n, world, 500 + i, torch.bfloat16) for i, n in enumerate((5120, 15360, 5120, 30720) * 16)]

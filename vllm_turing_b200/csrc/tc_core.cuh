@@ -197,9 +197,10 @@ __device__ __forceinline__ unsigned char *tc_align1024(unsigned char *p) {
 }
 
 // Output finisher of the decode orientation: thread = output feature n, acc[m] for the token rows. Finisher
-// interface: on_start(sm) once per epilogue thread after pdl_wait (sm: 64 floats of shared memory the finisher may
-// fill, then the epilogue warps synchronise); prep(P, n) before the piece's accumulators are ready (global loads whose
-// latency then hides behind the MMAs); operator()(P, n, nok, acc, prep) with the accumulators.
+// interface: on_start(P, sm) once per epilogue thread after pdl_wait (sm: 64 floats of shared memory the finisher may
+// fill), then the epilogue warps synchronise and each calls post_start() (per-thread state in registers); prep(P, n)
+// before the piece's accumulators are ready (global loads whose latency then hides behind the MMAs);
+// operator()(P, n, nok, acc, prep) with the accumulators.
 template <typename T, int BN>
 struct TcOutEpi {
     struct Prep {
@@ -211,6 +212,7 @@ struct TcOutEpi {
         const int t = threadIdx.x - 64;
         if (!P.s32_out && t < P.M) sm[t] = P.sa[P.sa_rows ? t : 0];
     }
+    __device__ __forceinline__ void post_start() {}
     __device__ __forceinline__ Prep prep(const TcArgs &P, int n) const {
         Prep r{0.f, 0.f};
         if (!P.s32_out && n < P.N) {   // scales and bias only in dequant mode (NULL for int32 output)
@@ -442,6 +444,7 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
         const int row = q * 32 + lane;   // row of the 128-row A tile this thread holds
         fin.on_start(P, epi_sm);  // after pdl_wait: e.g. the token scales, the communicator's call number
         named_sync(TC_EPI_BAR, 128);
+        fin.post_start();         // per-thread state from what on_start shared
         const int hw = (P.M + 1) >> 1;
         int ut = 0;
         TcPieces pc(P);
@@ -474,11 +477,15 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                     // This CTA finishes the tile: the CTAs holding its other K blocks (each one's first piece) left
                     // their sums in their slots, normally long ago -- collect them while this piece's MMAs still run,
                     // and clear the slots for the next launch.
+                    // One contributor at a time, its words in flight together. (Tried: all contributors' words in one
+                    // flight. It measured slower, likely because this code runs once per CTA per launch from a cold
+                    // instruction cache, where the larger unrolled body costs more in fetches than the round trips
+                    // it saves.)
                     const int clast = tc_owner(P, ta * P.nkb + P.nkb - 1);
                     for (int c = blockIdx.x + 1; c <= clast; ++c) {
                         uint4 v[BN / 2];
 #pragma unroll
-                        for (int h = 0; h < BN / 2; ++h)   // all of the slot's words in flight at once
+                        for (int h = 0; h < BN / 2; ++h)
                             if (h < hw) v[h] = ld_volatile16(tc_slot(P, c, h, row));
 #pragma unroll
                         for (int h = 0; h < BN / 2; ++h) {

@@ -136,33 +136,53 @@ __device__ __forceinline__ float group_combine(const CommView &c, int m, int g, 
 // Phase 2 of the fused kernel (all threads of every CTA call it once the GEMM phase has pushed this rank's values):
 // CTA m * E + g owns columns [w0, w1) (in 4-column LL words) of token row m; the other CTAs return at once. Loads are
 // issued in batches (KW words per thread, all ranks' LL words of a batch at once) so a batch costs about one memory
-// round trip, not one per word. E = 1 (the usual case up to two ranks) needs no cross-CTA combine at all.
-// smem: free shared memory of at least ceil(N / 4 / E) * 16 bytes; red: 32 floats; bcast: one float.
-template <typename T>
+// round trip, not one per word. (KW = 8 measured slower than 4, likely because this code runs once per launch from a
+// cold instruction cache, where the larger unrolled body costs more in fetches than the second batch.) E = 1 (the usual case up to two ranks) needs no cross-CTA combine at all.
+// smem: free shared memory of at least ceil(N / 4 / E) * 24 bytes; red: 32 floats; bcast: one float. publish_seq:
+// the kernel's CTAs read the call number before their first piece and every piece feeds row 0, so CTA 0 publishes
+// the next number once row 0 is complete (residual mode only; the caller counts CTAs out otherwise).
+template <typename T, int KW>
 __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommView &c, unsigned seq, unsigned p,
-                                             unsigned char *smem, float *red, float *bcast) {
-    constexpr int KW = 4;
+                                             unsigned char *smem, float *red, float *bcast, bool publish_seq) {
+    // every field in registers: the LL polls are asm with a memory clobber, after which values read through pointers
+    // (the kernel's parameter block included) would be read again
     const int M = P.M, N = P.N, E = P.E, W4 = N >> 2, world = c.world;
     if ((int)blockIdx.x >= M * E) return;
     const int m = blockIdx.x / E, g = blockIdx.x - m * E;
     const int w0 = (int)((long long)W4 * g / E), w1 = (int)((long long)W4 * (g + 1) / E);
     const int nw = w1 - w0, nt = blockDim.x, tid = threadIdx.x;
-    float *hbuf = reinterpret_cast<float *>(smem);
+    T *const residual = P.residual, *const reduced = P.reduced;
+    const T *const norm_w = P.norm_w;
+    int8_t *const qout = P.q;
+    float *const scales = P.scales;
+    const float eps = P.eps;
+    unsigned *const status = c.status();
+    const char *src[COMM_MAX_RANKS];   // rank r's LL words for this CTA's columns of row m
+#pragma unroll
+    for (int r = 0; r < COMM_MAX_RANKS; ++r)
+        src[r] = r < world ? c.ll_slot(c.rank, p, r) + ((size_t)m * W4 + w0) * 16 : nullptr;
+    float *hbuf = reinterpret_cast<float *>(smem);          // [nw * 4] the new residual, then the normalised row
+    uint2 *nbuf = reinterpret_cast<uint2 *>(hbuf + 4 * nw);  // [nw] norm weight words, loaded with the residual
     const uint64_t deadline = globaltimer() + P.peer_timeout;
     bool dead = false;
     float ss = 0.0f;
     for (int b = 0; b < nw; b += nt * KW) {
-        uint2 ru[KW];
-        if (P.residual) {   // this batch's residual words: independent of the peers, in flight with the LL polls
+        uint2 ru[KW], wv[KW];
+        if (residual) {   // this batch's residual and norm weight: independent of the peers, in flight with the polls
 #pragma unroll
             for (int k = 0; k < KW; ++k) {
                 const int i = b + tid + k * nt;
-                if (i < nw) ru[k] = *reinterpret_cast<const uint2 *>(P.residual + (size_t)m * N + (size_t)(w0 + i) * 4);
+                if (i < nw) {
+                    ru[k] = *reinterpret_cast<const uint2 *>(residual + (size_t)m * N + (size_t)(w0 + i) * 4);
+                    wv[k] = *reinterpret_cast<const uint2 *>(norm_w + (size_t)(w0 + i) * 4);
+                }
             }
         }
         float s[KW][4];
-        for (int r = 0; r < world; ++r) {   // ranks in order: the float sums are identical on every rank
-            const char *slot = c.ll_slot(c.rank, p, r) + ((size_t)m * W4 + w0) * 16;
+#pragma unroll
+        for (int r = 0; r < COMM_MAX_RANKS; ++r) {   // ranks in order: the float sums are identical on every rank
+            if (r >= world) break;
+            const char *slot = src[r];
             uint4 v[KW];
 #pragma unroll
             for (int k = 0; k < KW; ++k) {
@@ -176,7 +196,7 @@ __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommVi
                 uint32_t it = 0;
                 while (!dead && (v[k].y != seq || v[k].w != seq)) {
                     if ((++it & 255u) == 0 && globaltimer() > deadline) {
-                        report(c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
+                        report(status, ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
                         dead = true;
                         break;
                     }
@@ -195,14 +215,15 @@ __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommVi
             const int i = b + tid + k * nt;
             if (i >= nw) continue;
             const size_t e0 = (size_t)m * N + (size_t)(w0 + i) * 4;
-            if (P.reduced)
-                *reinterpret_cast<uint2 *>(P.reduced + e0) =
+            if (reduced)
+                *reinterpret_cast<uint2 *>(reduced + e0) =
                     make_uint2(pack2<T>(s[k][0], s[k][1]), pack2<T>(s[k][2], s[k][3]));
-            if (P.residual) {
+            if (residual) {
                 const float2 r0 = unpack2<T>(ru[k].x), r1 = unpack2<T>(ru[k].y);
                 const float h0 = rnd<T>(rnd<T>(s[k][0]) + r0.x), h1 = rnd<T>(rnd<T>(s[k][1]) + r0.y);
                 const float h2 = rnd<T>(rnd<T>(s[k][2]) + r1.x), h3 = rnd<T>(rnd<T>(s[k][3]) + r1.y);
-                *reinterpret_cast<uint2 *>(P.residual + e0) = make_uint2(pack2<T>(h0, h1), pack2<T>(h2, h3));
+                *reinterpret_cast<uint2 *>(residual + e0) = make_uint2(pack2<T>(h0, h1), pack2<T>(h2, h3));
+                nbuf[i] = wv[k];
                 hbuf[4 * i] = h0;
                 hbuf[4 * i + 1] = h1;
                 hbuf[4 * i + 2] = h2;
@@ -211,40 +232,36 @@ __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommVi
             }
         }
     }
-    if (!P.residual) return;
+    if (!residual) return;
     ss = block_sum_n(ss, red);
     const float tot = E > 1 ? group_combine(c, m, g, E, 0, ss, false, seq, deadline, bcast) : ss;
-    const float rs = __frsqrt_rn(__fdiv_rn(tot, (float)N) + P.eps);
+    if (publish_seq && blockIdx.x == 0 && tid == 0) {
+        // Row 0 is complete across all its CTAs: every tile was finished and pushed, so every CTA of the grid has
+        // read this call's number -- publish it now, for the next call on the communicator (the kernel boundary
+        // makes it visible), instead of counting CTAs out at the end.
+        *reinterpret_cast<volatile unsigned *>(c.seq_ptr()) = seq;
+    }
+    const float rs = __frsqrt_rn(__fdiv_rn(tot, (float)N) + eps);
     float amax = 0.0f;
-    for (int b = 0; b < nw; b += nt * KW) {
-        uint2 wu[KW];
-#pragma unroll
-        for (int k = 0; k < KW; ++k) {
-            const int i = b + tid + k * nt;
-            if (i < nw) wu[k] = *reinterpret_cast<const uint2 *>(P.norm_w + (size_t)(w0 + i) * 4);
-        }
-#pragma unroll
-        for (int k = 0; k < KW; ++k) {
-            const int i = b + tid + k * nt;
-            if (i >= nw) continue;
-            const float2 wa = unpack2<T>(wu[k].x), wb = unpack2<T>(wu[k].y);
-            const float y0 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i], rs), wa.x));
-            const float y1 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 1], rs), wa.y));
-            const float y2 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 2], rs), wb.x));
-            const float y3 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 3], rs), wb.y));
-            hbuf[4 * i] = y0;
-            hbuf[4 * i + 1] = y1;
-            hbuf[4 * i + 2] = y2;
-            hbuf[4 * i + 3] = y3;
-            amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
-        }
+    for (int i = tid; i < nw; i += nt) {
+        const uint2 wu = nbuf[i];
+        const float2 wa = unpack2<T>(wu.x), wb = unpack2<T>(wu.y);
+        const float y0 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i], rs), wa.x));
+        const float y1 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 1], rs), wa.y));
+        const float y2 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 2], rs), wb.x));
+        const float y3 = rnd<T>(__fmul_rn(__fmul_rn(hbuf[4 * i + 3], rs), wb.y));
+        hbuf[4 * i] = y0;
+        hbuf[4 * i + 1] = y1;
+        hbuf[4 * i + 2] = y2;
+        hbuf[4 * i + 3] = y3;
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(y0), fabsf(y1)), fmaxf(fabsf(y2), fabsf(y3))));
     }
     amax = block_max_n(amax, red);
     if (E > 1) amax = group_combine(c, m, g, E, 1, amax, true, seq, deadline, bcast);
     const float inv = quant_inv(amax);
-    if (g == 0 && tid == 0) P.scales[m] = __fdiv_rn(amax, 127.0f);
+    if (g == 0 && tid == 0) scales[m] = __fdiv_rn(amax, 127.0f);
     for (int i = tid; i < nw; i += nt) {
-        *reinterpret_cast<char4 *>(P.q + (size_t)m * N + (size_t)(w0 + i) * 4) =
+        *reinterpret_cast<char4 *>(qout + (size_t)m * N + (size_t)(w0 + i) * 4) =
             make_char4(quant1(hbuf[4 * i], inv), quant1(hbuf[4 * i + 1], inv), quant1(hbuf[4 * i + 2], inv),
                        quant1(hbuf[4 * i + 3], inv));
     }
@@ -276,7 +293,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
                    c.status(), push);
     __syncthreads();
 
-    row_epilogue<T>(P, c, seq, p, smem + GV_HDR, red, &bcast);   // the GEMV ring is free now
+    row_epilogue<T, 4>(P, c, seq, p, smem + GV_HDR, red, &bcast, false);   // the GEMV ring is free now
     comm_end(c, seq);
 }
 
@@ -293,31 +310,46 @@ struct TcLLPushEpi {
     int M, N;
     unsigned *s_seq;   // shared: this call's sequence number, read after pdl_wait
     float *sa_sm;      // shared: the token scales
+    // registers from post_start: the call's sequence number and this rank's LL slot in every rank's region, in push
+    // order (own rank first). The pushes are asm with a memory clobber; values kept in registers are not re-read.
+    unsigned seq;
+    int world;
+    char *dst[COMM_MAX_RANKS];
     __device__ __forceinline__ void on_start(const TcArgs &, float *sm) {
         sa_sm = sm;
         const int t = threadIdx.x - TC_EPI_LEAD;
         if (t < M) sm[t] = sa[t];
         if (t == 0) *s_seq = *reinterpret_cast<volatile unsigned *>(c->seq_ptr()) + 1u;
     }
+    __device__ __forceinline__ void post_start() {
+        seq = *s_seq;
+        world = c->world;
+        const int rank = c->rank;
+#pragma unroll
+        for (int k = 0; k < COMM_MAX_RANKS; ++k)
+            dst[k] = k < world ? c->ll_slot((rank + k) % world, seq & 1u, rank) : nullptr;
+    }
     __device__ __forceinline__ Prep prep(const TcArgs &, int n) const { return Prep{n < N ? sw[n] : 0.0f}; }
     __device__ __forceinline__ void operator()(const TcArgs &, int n, bool nok, const int (&acc)[BN],
                                                const Prep &pr) const {
-        const int W4 = N >> 2, world = c->world, rank = c->rank;
+        const int W4 = N >> 2, Mr = M, nw = world;
+        const unsigned sq = seq;
         const int lane = threadIdx.x & 31;
-        const unsigned seq = *s_seq, p = seq & 1u;
+        float v[BN];
+#pragma unroll
+        for (int m = 0; m < BN; ++m) v[m] = (m < Mr && nok) ? dequant1(acc[m], sa_sm[m], pr.swn) : 0.0f;
 #pragma unroll
         for (int m = 0; m < BN; ++m) {
-            if (m >= M) break;   // M is uniform: the whole warp leaves together
-            const float v = nok ? dequant1(acc[m], sa_sm[m], pr.swn) : 0.0f;
-            const float v1 = __shfl_down_sync(0xffffffffu, v, 1);
-            const float v2 = __shfl_down_sync(0xffffffffu, v, 2);
-            const float v3 = __shfl_down_sync(0xffffffffu, v, 3);
+            if (m >= Mr) break;   // M is uniform: the whole warp leaves together
+            const float v1 = __shfl_down_sync(0xffffffffu, v[m], 1);
+            const float v2 = __shfl_down_sync(0xffffffffu, v[m], 2);
+            const float v3 = __shfl_down_sync(0xffffffffu, v[m], 3);
             if ((lane & 3) == 0 && nok) {   // n % 4 == 0 here and N % 4 == 0: features n .. n + 3 all exist
-                const uint32_t lo = pack2<T>(v, v1), hi = pack2<T>(v2, v3);
-                for (int k = 0; k < world; ++k) {
-                    const int dst = (rank + k) % world;
-                    ll_store(c->ll_slot(dst, p, rank) + ((size_t)m * W4 + (n >> 2)) * 16, lo, hi, seq);
-                }
+                const uint32_t lo = pack2<T>(v[m], v1), hi = pack2<T>(v2, v3);
+                const size_t off = ((size_t)m * W4 + (n >> 2)) * 16;
+#pragma unroll
+                for (int k = 0; k < COMM_MAX_RANKS; ++k)
+                    if (k < nw) ll_store(dst[k] + off, lo, hi, sq);
             }
         }
     }
@@ -334,11 +366,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __shared__ float red[32];
     __shared__ float bcast;
     const CommView &c = P.c;
-    TcLLPushEpi<T, BN> push{&c, P.sa, P.sw, P.M, P.N, &s_seq, nullptr};
+    TcLLPushEpi<T, BN> push{&c, P.sa, P.sw, P.M, P.N, &s_seq, nullptr, 0u, 0, {}};
     tc_phase<T, BN, true, KBS>(&tmap_w, &tmap_a, G, smem_raw, push);   // ends with __syncthreads
     const unsigned seq = s_seq, p = seq & 1u;
-    row_epilogue<T>(P, c, seq, p, tc_align1024(smem_raw), red, &bcast);   // the stage ring is free now
-    comm_end(c, seq);
+    const bool publish = P.residual != nullptr;   // residual mode: row 0's CTA publishes the call number
+    row_epilogue<T, 4>(P, c, seq, p, tc_align1024(smem_raw), red, &bcast, publish);   // the stage ring is free now
+    if (!publish) comm_end(c, seq);
 }
 
 template <typename T, int BN, int KBS>
@@ -373,8 +406,8 @@ static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     if (P.M > g || tc_decode_slot_bytes(P.M, g) > P.c.L.scratch_bytes) return VT_EARG;
     const int E = row_ctas(P.c.world, P.M, g);
     P.E = E;
-    // row epilogue buffer: ceil(N / 4 / E) words of 4 floats in the (free) stage ring
-    if ((size_t)((P.N / 4 + E - 1) / E) * 16 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
+    // row epilogue buffers: ceil(N / 4 / E) words of 4 floats and a norm weight word each, in the (free) stage ring
+    if ((size_t)((P.N / 4 + E - 1) / E) * 24 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
     return launch_k(tp_row_linear_tc_kernel<T, BN, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, mw, ma, G, P);
 }
 
@@ -407,7 +440,7 @@ static int launch_fused(FusedArgs<T> P, cudaStream_t s) {
     if (P.M > G) return VT_EARG;
     const int E = row_ctas(P.c.world, P.M, G);
     P.E = E;
-    if ((size_t)((P.N / 4 + E - 1) / E) * 16 + GV_HDR > (size_t)smem) return VT_EARG;   // row epilogue buffer
+    if ((size_t)((P.N / 4 + E - 1) / E) * 24 + GV_HDR > (size_t)smem) return VT_EARG;   // row epilogue buffers
     CUtensorMap wmap;
     if (!make_map_i8(&wmap, P.w, P.N, P.K, GV_SEGB / 2, GV_RB, CU_TENSOR_MAP_SWIZZLE_NONE)) return VT_EARG;
     tp_row_linear_kernel<T, MT><<<G, GV_THREADS, smem, s>>>(wmap, P);
