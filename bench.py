@@ -49,11 +49,18 @@ def parse():
     ap.add_argument("--layers", type=int, default=LAYERS)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--tokens", type=int, default=5)
+    ap.add_argument("--tokens", type=int, default=None, help="tokens per step (decode default 5, prefill 8192)")
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
+                    help="decode: the 64-layer MLP stack (the headline, config 1/2); prefill: the row-parallel layer "
+                         "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant)")
+    ap.add_argument("--proj", default="down", choices=["down", "o_proj"], help="prefill: K = 17408 or 6144 (per TP)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no clocks, e2e or CPU baseline")
-    return ap.parse_args()
+    a = ap.parse_args()
+    if a.tokens is None:
+        a.tokens = 8192 if a.mode == "prefill" else 5
+    return a
 
 
 def peaks():
@@ -169,6 +176,8 @@ def run_reference(args):
     M = args.tokens
     threads = cpu_cores()
     steps = max(1, min(args.steps, 20))
+    if args.mode == "prefill":
+        return run_reference_prefill(args, threads, steps)
     dt, n, threads = time_oracle_layer(M, threads, budget_s=60.0, max_steps=steps)
     tops = layer_ops(M, 1) / dt / 1e12
     sample = (f"{n} full layers (M={M}, gate_up 5120->34816 + silu_mul_quant + down 17408->5120 + RMSNorm + "
@@ -179,6 +188,39 @@ def run_reference(args):
         "dtype": "int8", "data": "synthetic", "us_per_layer": dt * 1e6, "bus_gbs": 0.0,
         "config": {"workload": f"decode W8A8 MLP layer M={M}, hidden 5120, intermediate 17408 (BASELINE config 1)",
                    "tokens": M, "tp": 1, "device": "cpu"},
+        "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own path is CUDA for sm_75 only; this arm is its CPU restatement (oracle/)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_prefill(args, threads, steps, sample_rows=256):
+    """The prefill row-parallel tail (config 3) through the C oracle on the host cores, TP1, on a bounded sample of
+    the batch's rows (the per-row work is identical, so time scales with rows); reported for the full batch."""
+    from oracle import oracle as O
+    from vllm_turing_b200.synthetic import make_layer_inputs
+    O.set_threads(threads)
+    M = args.tokens
+    K = INTER if args.proj == "down" else 6144
+    rows = min(M, sample_rows)
+    li = make_layer_inputs(rows, HIDDEN, K, seed=300, rank=0)
+    a, w, sa, sw = li.a.numpy(), li.w.numpy(), li.sa.numpy(), li.sw.numpy()
+    res, nw = O.to_bits(li.residual), O.to_bits(li.norm_w)
+    O.row_linear_tp([a], [w], [sa], [sw], res, nw, 1e-6, 1)
+    n, t0 = 0, time.perf_counter()
+    while n < steps and (n < 2 or time.perf_counter() - t0 < 30.0):
+        O.row_linear_tp([a], [w], [sa], [sw], res, nw, 1e-6, 1)
+        n += 1
+    dt = (time.perf_counter() - t0) / n * (M / rows)   # seconds for the full batch
+    tops = 2.0 * M * HIDDEN * K / dt / 1e12
+    sample = f"{n} tails of {rows} of the {M} rows ({args.proj} K={K} -> 5120 + RMSNorm + quant), TP1, scaled by rows"
+    line = {
+        "metric": METRIC, "value": tops, "unit": "TOPS", "impl": "reference", "n_gpus": args.gpus, "steps": n,
+        "warmup": 1, "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic", "mode": "prefill", "us_per_layer": dt * 1e6, "bus_gbs": 0.0,
+        "config": {"workload": f"prefill row-parallel tail M={M} (BASELINE config 3)", "tokens": M, "tp": 1,
+                   "device": "cpu"},
         "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's own path is CUDA for sm_75 only; this arm is its CPU restatement (oracle/)",
@@ -205,6 +247,208 @@ def read_traffic():
     return out
 
 
+def dist_setup(args):
+    """One process per GPU: (world, rank, local rank, device, gloo group for set-up and barriers)."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29655")
+    if world > 1:
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
+        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
+    else:
+        dist.init_process_group("gloo", rank=0, world_size=1)
+        gloo = dist.group.WORLD
+    return world, rank, local, dev, gloo
+
+
+PREFILL_SETS = 3   # distinct layer buffers cycled by the captured step: every step's inputs are cold in L2
+
+
+def run_prefill(args, world, rank, local, dev, gloo):
+    """Config 3: the row-parallel tail of a prefill layer -- this rank's W8A8 GEMM (tcgen05, 128 x 256 tiles) ->
+    two-shot all-reduce over NVLink P2P -> residual add + RMSNorm + per-token int8 quant -- through the public API
+    (vllm_turing::scaled_mm_, TPComm.all_reduce, quantfuse.rms_norm_dynamic_per_token_quant), captured in a CUDA graph.
+    value = whole-job int8 TOPS of the GEMM part; us_per_layer, bus_gbs (the all-reduce's nccl-tests convention)."""
+    import torch
+    import torch.distributed as dist
+
+    from vllm_turing_b200 import _build, w8a8
+    from vllm_turing_b200.comm import TPComm
+    from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant
+    from vllm_turing_b200.synthetic import make_layer_inputs
+
+    _build.load()
+    M, N = args.tokens, HIDDEN
+    K_full = INTER if args.proj == "down" else 6144
+    assert K_full % world == 0
+    K = K_full // world
+    sets = []
+    for i in range(PREFILL_SETS):
+        li = make_layer_inputs(M, N, K, seed=300 + i, rank=rank)
+        sets.append(dict(a=li.a.to(dev), w=li.w.to(dev), sa=li.sa.to(dev).view(-1, 1), sw=li.sw.to(dev).view(-1, 1),
+                         res=li.residual.to(dev), nw=li.norm_w.to(dev),
+                         out=torch.empty(M, N, dtype=torch.bfloat16, device=dev),
+                         q=torch.empty(M, N, dtype=torch.int8, device=dev),
+                         s=torch.empty(M, 1, dtype=torch.float32, device=dev)))
+        del li
+    comm = TPComm(gloo, dev, big_bytes=2 * M * N)
+    stream = torch.cuda.current_stream()
+
+    def gemm(st):
+        torch.ops.vllm_turing.scaled_mm_(st["out"], st["a"], st["w"].t(), st["sa"], st["sw"], None)
+
+    def allreduce(st):
+        comm.all_reduce(st["out"], out=st["out"])
+
+    def norm(st):
+        rms_norm_dynamic_per_token_quant(st["out"], st["nw"], 1e-6, st["res"], q=st["q"], s=st["s"])
+
+    STEP = (gemm, allreduce, norm)
+
+    def run(fns):
+        for st in sets:
+            for fn in fns:
+                fn(st)
+
+    def barrier():
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    def timed(fn, n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / n) / 1e3
+
+    K_steps, W = args.steps, max(args.warmup, 3)
+    if args.profile:
+        for _ in range(W + K_steps):
+            run(STEP)
+        barrier()
+        comm.check()
+        if rank == 0:
+            print(json.dumps({"profile": True, "mode": "prefill", "steps": K_steps}), flush=True)
+        comm.close()
+        dist.destroy_process_group()
+        return
+    for _ in range(2):
+        run(STEP)
+    barrier()
+    comm.check()
+
+    def capture(fns):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            run(fns)
+        return g
+
+    g_step = capture(STEP)
+    g_k = {"gemm": capture((gemm,)), "allreduce": capture((allreduce,)), "norm": capture((norm,))}
+    barrier()
+    with ClockSampler(local) as clk:
+        t_w = time.perf_counter()
+        i = 0
+        while i < W or time.perf_counter() - t_w < 1.0:
+            g_step.replay()
+            i += 1
+            if i % 4 == 0:
+                torch.cuda.synchronize()
+        barrier()
+        t_step = timed(g_step.replay, K_steps)
+    W = max(W, i)
+    t_layer = t_step / PREFILL_SETS
+    t_k = {k: timed(g.replay, max(1, min(K_steps, 10))) / PREFILL_SETS for k, g in g_k.items()}
+    comm.check()
+
+    # end to end: the layer's activation (int8 + scales) and residual from pinned host memory, outputs read back
+    e2e = None
+    if not args.no_e2e:
+        st0 = sets[0]
+        h_a, h_sa, h_res = st0["a"].cpu().pin_memory(), st0["sa"].cpu().pin_memory(), st0["res"].cpu().pin_memory()
+        o_q, o_s, o_res = (torch.empty_like(st0["q"], device="cpu").pin_memory(),
+                           torch.empty_like(st0["s"], device="cpu").pin_memory(), torch.empty_like(h_res).pin_memory())
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            for fn in STEP:
+                fn(st0)
+
+        def e2e_step():
+            st0["a"].copy_(h_a, non_blocking=True)
+            st0["sa"].copy_(h_sa, non_blocking=True)
+            st0["res"].copy_(h_res, non_blocking=True)
+            g1.replay()
+            o_q.copy_(st0["q"], non_blocking=True)
+            o_s.copy_(st0["s"], non_blocking=True)
+            o_res.copy_(st0["res"], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        t_e2e = timed(e2e_step, max(1, min(K_steps, 10)))
+        h2d = h_a.numel() + h_sa.numel() * 4 + h_res.numel() * 2
+        d2h = o_q.numel() + o_s.numel() * 4 + o_res.numel() * 2
+        e2e = {"value": 2.0 * M * N * K_full / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": int(d2h), "us_per_layer": t_e2e * 1e6,
+               "api": "scaled_mm_ + TPComm.all_reduce + rms_norm_dynamic_per_token_quant, captured; host copies"}
+        del g1
+
+    # roofline of the dominant part: the GEMM on the tensor cores (int8 dense = 2x the measured bf16 GEMM rate), or
+    # the all-reduce on NVLink (measured 770 GB/s peer copy per direction)
+    ops_rank = 2.0 * M * N * K
+    S = 2 * M * N
+    bus = 2.0 * (world - 1) / world * S / t_k["allreduce"] / 1e9 if world > 1 else 0.0
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            int8_peak, pk = 2.0 * float(json.load(f)["bf16_tflops"]), "2x measured bf16 GEMM"
+    except Exception:   # noqa: BLE001
+        int8_peak, pk = 2.0 * 1590.0, "2x fallback bf16"
+    if t_k["gemm"] >= t_k["allreduce"] or world == 1:
+        ach = ops_rank / t_k["gemm"] / 1e12
+        roof = {"bound": "tensor", "kernel": "tc_gemm_kernel (prefill, 128 x 256 tiles)", "achieved": ach,
+                "peak": int8_peak, "unit": "TOP/s", "frac": ach / int8_peak, "traffic": None, "peak_kind": pk}
+    else:
+        roof = {"bound": "nvlink", "kernel": "ar_twoshot_kernel", "achieved": bus, "peak": 770.0, "unit": "GB/s",
+                "frac": bus / 770.0, "traffic": None, "peak_kind": "measured peer copy per direction"}
+    line = {
+        "metric": METRIC, "value": 2.0 * M * N * K_full / t_layer / 1e12, "unit": "TOPS", "n_gpus": world,
+        "steps": K_steps, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic", "mode": "prefill",
+        "us_per_layer": t_layer * 1e6, "bus_gbs": bus,
+        "config": {"workload": f"prefill row-parallel tail M={M}: {args.proj} GEMM {K_full}/{world} -> {N} + two-shot "
+                               f"all-reduce + residual add + RMSNorm + int8 quant (BASELINE config 3)",
+                   "tokens": M, "tp": world, "K_local": K, "N": N, "layers_cycled": PREFILL_SETS,
+                   "l2": "inputs larger than L2 (three layer buffer sets cycled)", "launch": "CUDA graph",
+                   "parallelism": f"tp{world}"},
+        "kernel_us": {k: v * 1e6 for k, v in t_k.items()},
+        "roofline": roof, "clocks": clk.summary(), "gpu_launches": 3 * PREFILL_SETS * K_steps, "e2e": e2e,
+        "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del g_step, g_k
+    comm.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -217,22 +461,9 @@ def main():
     from vllm_turing_b200.synthetic import make_layer_inputs, quant_per_token
     from vllm_turing_b200.tailoverlap import silu_mul_quant
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-    os.environ.setdefault("MASTER_PORT", "29655")
-    from datetime import timedelta
-    if world > 1:
-        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev, timeout=timedelta(seconds=120))
-        gloo = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
-    else:
-        dist.init_process_group("gloo", rank=0, world_size=1)
-        gloo = dist.group.WORLD
+    world, rank, local, dev, gloo = dist_setup(args)
+    if args.mode == "prefill":
+        return run_prefill(args, world, rank, local, dev, gloo)
     _build.load()
     M = args.tokens
     NL = args.layers

@@ -130,8 +130,8 @@ unsigned vt_comm_seq(void *comm);
 
 /* out[n] = sum over ranks of in[n], float32 accumulation in rank order, one rounding (the arithmetic of
  * host_ar.cu:90-101). algo 0 auto, 1 one-shot LL (n % 4 == 0, up to ll_data), 2 two-shot (n % 8 == 0).
- * in may equal out; 16-byte aligned. Replaces har_all_reduce (host_ar.cu:114-131) and ce_all_reduce
- * (ce_ar.cu:103-146) for any rank count. */
+ * in may equal out; 16-byte aligned. One rank: no kernel (a device-to-device copy when in != out). Replaces
+ * har_all_reduce (host_ar.cu:114-131) and ce_all_reduce (ce_ar.cu:103-146) for any rank count. */
 int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype, int algo, void *stream);
 
 /* gathered [world * m bytes] with this rank's payload pre-written at [rank * m, (rank + 1) * m); fills the peers'

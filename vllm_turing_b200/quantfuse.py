@@ -44,12 +44,15 @@ def scaled_int8_quant_cuda(x: torch.Tensor):
     return q.view(x.shape), s
 
 
-def rms_norm_dynamic_per_token_quant(x, weight, eps, residual, normed=None):
+def rms_norm_dynamic_per_token_quant(x, weight, eps, residual, normed=None, q=None, s=None):
     """residual += x (in place); returns (q int8, scales float32 [rows, 1]) of RMSNorm(residual) * weight.
-    The contract of vLLM's op as the reference calls it (vllm_turing/tailoverlap.py:200-201)."""
+    The contract of vLLM's op as the reference calls it (vllm_turing/tailoverlap.py:200-201); q / s are written in
+    place when given (static buffers of a captured step)."""
     M, N = residual.shape
-    q = torch.empty(M, N, dtype=torch.int8, device=x.device)
-    s = torch.empty(M, 1, dtype=torch.float32, device=x.device)
+    q = q if q is not None else torch.empty(M, N, dtype=torch.int8, device=x.device)
+    s = s if s is not None else torch.empty(M, 1, dtype=torch.float32, device=x.device)
+    if q.shape != (M, N) or q.dtype != torch.int8 or not q.is_contiguous() or s.numel() != M:
+        raise ValueError("rms_norm_dynamic_per_token_quant: q must be int8 [M, N] contiguous and s hold M floats")
     rc = _build.load().vt_rms_norm_quant(x.data_ptr(), residual.data_ptr(), weight.data_ptr(), float(eps),
                                          q.data_ptr(), s.data_ptr(), normed.data_ptr() if normed is not None else None,
                                          M, N, _code(x.dtype), torch.cuda.current_stream().cuda_stream)
