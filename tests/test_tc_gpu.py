@@ -46,9 +46,10 @@ def test_small_s32(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(33, 256, 128), (128, 5120, 3072), (200, 1000, 5136), (2048, 5120, 8704),
-                                   (1680, 8704, 5120), (300, 136, 5168)])
+                                   (1680, 8704, 5120), (300, 136, 5168), (2600, 1000, 256)])
 def test_big_s32(M, N, K):
-    """prefill orientation (activations as the A operand, 128 x 256 tiles)"""
+    """prefill orientation (activations as the A operand, 128 x 256 tiles, grouped raster of 16 A tiles: 2600 rows
+    make a full group and a 5-tile one)"""
     a, w = rand_int8((M, K), 5 * M + K), rand_int8((N, K), 7 * N + K)
     acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
     ac, wc = a.cuda(), w.cuda()

@@ -1,7 +1,12 @@
-"""The kernel variants chosen by environment switches that are read once per process -- the fused row-linear's dp4a
-GEMV phase (VLLM_TURING_FUSED_GEMV=1) and the tcgen05 decode kernel's K blocks per pipeline stage
-(VLLM_TURING_TC_KBS = 1 or 2; 4 is the default the other tests run) -- each checked in a child process against the
-oracle: int32 accumulators and the fused layer's reduced sum and residual bit-exact, int8 within 1 LSB."""
+"""The kernel variants chosen by environment switches that are read once per process, each checked in a child
+process against the oracle (int32 accumulators and the fused layer's reduced sum and residual bit-exact, int8 within
+1 LSB):
+  - the fused row-linear's dp4a GEMV phase (VLLM_TURING_FUSED_GEMV=1);
+  - the tcgen05 decode kernel's K blocks per pipeline stage (VLLM_TURING_TC_KBS = 1 or 2; 4 is the default);
+  - several CTAs per token row in the fused row epilogue, with the mailbox combine that tensor parallelism above two
+    ranks uses (VLLM_TURING_ROW_CTAS);
+  - launches without programmatic dependent launch (VLLM_TURING_PDL=0), and the weight prefetch into L2 ahead of the
+    launch wait (VLLM_TURING_L2_PREFETCH_KB, off by default)."""
 import os
 import subprocess
 import sys
@@ -60,7 +65,10 @@ def child():
 
 
 @pytest.mark.parametrize("env", [{"VLLM_TURING_FUSED_GEMV": "1"}, {"VLLM_TURING_TC_KBS": "1"},
-                                 {"VLLM_TURING_TC_KBS": "2"}], ids=["fused_gemv", "kbs1", "kbs2"])
+                                 {"VLLM_TURING_TC_KBS": "2"}, {"VLLM_TURING_ROW_CTAS": "4"},
+                                 {"VLLM_TURING_FUSED_GEMV": "1", "VLLM_TURING_ROW_CTAS": "3"},
+                                 {"VLLM_TURING_PDL": "0"}, {"VLLM_TURING_L2_PREFETCH_KB": "256"}],
+                         ids=["fused_gemv", "kbs1", "kbs2", "row_ctas4", "gemv_row_ctas3", "no_pdl", "l2_prefetch"])
 def test_variant_in_child(env):
     e = dict(os.environ, **env)
     r = subprocess.run([sys.executable, "-c", "import tests.test_variants_gpu as t; t.child()"], cwd=ROOT, env=e,

@@ -103,6 +103,11 @@ __device__ __forceinline__ void tma_load_2d_hint(void *dst, const CUtensorMap *m
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// L2 prefetch of one 2-D box (no shared memory, no completion to wait for; same coordinates as tma_load_2d)
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
+    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
+                 : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }

@@ -270,7 +270,12 @@ __device__ __forceinline__ void row_epilogue(const FusedArgs<T> &P, const CommVi
 // CTAs per token row in the row epilogue: one up to two ranks (no cross-CTA combine); more ranks bring world x more
 // LL words per row, shared by world / 2 CTAs (at most the mailbox's groups and one CTA per row per SM).
 inline int row_ctas(int world, int M, int grid) {
-    int E = world / 2;
+    static int forced = -1;   // VLLM_TURING_ROW_CTAS: a fixed E (tests run the multi-CTA combine on one GPU)
+    if (forced < 0) {
+        const char *e = getenv("VLLM_TURING_ROW_CTAS");
+        forced = e ? atoi(e) : 0;
+    }
+    int E = forced > 0 ? forced : world / 2;
     if (E < 1) E = 1;
     if (E > COMM_MBOX_GROUPS) E = COMM_MBOX_GROUPS;
     while (E > 1 && E * M > grid) --E;

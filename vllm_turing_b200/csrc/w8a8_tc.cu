@@ -64,6 +64,7 @@ static int big_gemm(const void *a, const void *w, const float *sa, const float *
     P.nkb = (K + TC_BK - 1) / TC_BK;
     P.units = P.n_tiles_a * P.n_tiles_b;
     P.stream_k = 0;
+    P.group_m = P.n_tiles_a < 16 ? P.n_tiles_a : 16;   // a group's A tiles + all of B stay in L2 across a wave
     P.sa = sa;
     P.sw = sw;
     P.sa_rows = 1;
