@@ -51,16 +51,20 @@ def test_rms_norm_quant_golden(golden, shape):
     assert np.max(np.abs(so - golden[key + "_s"]) / golden[key + "_s"]) < 1e-2
 
 
-@pytest.mark.parametrize("M,N", [(5, 5120), (300, 5120), (8192, 5120)])
-def test_rms_norm_quant_vs_oracle(M, N):
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N", [(5, 5120), (300, 5120), (8192, 5120), (64, 4096), (7, 16384), (33, 512),
+                                 (40, 1000), (3, 20480)])
+def test_rms_norm_quant_vs_oracle(M, N, dtype):
+    """the register-resident kernel (N % 8 == 0, N <= 16384) and the shared-memory one (N = 1000, 20480)"""
     from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant
+    code = 0 if dtype == torch.float16 else 1
     g = torch.Generator().manual_seed(N + M)
-    x = (torch.randn(M, N, generator=g) * 3).to(torch.bfloat16)
-    r = torch.randn(M, N, generator=g).to(torch.bfloat16)
-    w = (1 + torch.randn(N, generator=g) * 0.1).to(torch.bfloat16)
+    x = (torch.randn(M, N, generator=g) * 3).to(dtype)
+    r = torch.randn(M, N, generator=g).to(dtype)
+    w = (1 + torch.randn(N, generator=g) * 0.1).to(dtype)
     rc = r.cuda()
     q, s = rms_norm_dynamic_per_token_quant(x.cuda(), w.cuda(), 1e-6, rc)
-    ro, qo, so, _ = O.add_rms_norm_quant(O.to_bits(x), O.to_bits(r), O.to_bits(w), 1e-6, 1)
+    ro, qo, so, _ = O.add_rms_norm_quant(O.to_bits(x), O.to_bits(r), O.to_bits(w), 1e-6, code)
     assert_bits_equal(rc, ro, "residual")
     assert q_off(q.cpu().numpy(), qo) <= 1
     assert (q.cpu().numpy() != qo).mean() < 1e-2

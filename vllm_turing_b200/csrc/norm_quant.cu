@@ -119,6 +119,84 @@ __global__ void __launch_bounds__(RQ_THREADS)
                            quant1(hbuf[4 * i + 3], inv));
 }
 
+// Register-resident variant for rows of N % 8 == 0 (16-byte aligned, N <= 16384): one CTA of N / 8 / VPT threads
+// (64..256) per row, each
+// thread holding VPT 16-byte vectors of x, residual and weight, all loads issued before any arithmetic (one memory
+// round trip per row, no shared-memory row buffer). Same arithmetic and rounding points as rms_norm_quant_kernel;
+// only the float32 summation order of the mean of squares differs (per-thread partials, then warps in order).
+template <typename T, int VPT>
+__global__ void __launch_bounds__(256)
+    rms_norm_quant_vec_kernel(const T *__restrict__ x, T *__restrict__ residual, const T *__restrict__ w, float eps,
+                              int8_t *__restrict__ q, float *__restrict__ scales, T *__restrict__ normed, int N) {
+    __shared__ float red[32];
+    const size_t row = blockIdx.x;
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + row * N);
+    uint4 *rr = reinterpret_cast<uint4 *>(residual + row * N);
+    const uint4 *wr = reinterpret_cast<const uint4 *>(w);
+    uint4 xv[VPT], rv[VPT], wv[VPT];
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const int i = threadIdx.x + k * blockDim.x;
+        xv[k] = xr[i];
+        rv[k] = rr[i];
+        wv[k] = __ldg(wr + i);
+    }
+    float h[VPT * 8];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const uint32_t xs[4] = {xv[k].x, xv[k].y, xv[k].z, xv[k].w};
+        const uint32_t rs_[4] = {rv[k].x, rv[k].y, rv[k].z, rv[k].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 a = unpack2<T>(xs[e]), b = unpack2<T>(rs_[e]);
+            const float h0 = rnd<T>(a.x + b.x), h1 = rnd<T>(a.y + b.y);
+            h[8 * k + 2 * e] = h0;
+            h[8 * k + 2 * e + 1] = h1;
+            ss += h0 * h0 + h1 * h1;
+            o[e] = pack2<T>(h0, h1);
+        }
+        rr[threadIdx.x + k * blockDim.x] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    ss = block_sum(ss, red);
+    const float rs = __frsqrt_rn(__fdiv_rn(ss, (float)N) + eps);
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        const uint32_t ws[4] = {wv[k].x, wv[k].y, wv[k].z, wv[k].w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float2 wf = unpack2<T>(ws[e]);
+            const float y0 = rnd<T>(__fmul_rn(__fmul_rn(h[8 * k + 2 * e], rs), wf.x));
+            const float y1 = rnd<T>(__fmul_rn(__fmul_rn(h[8 * k + 2 * e + 1], rs), wf.y));
+            h[8 * k + 2 * e] = y0;
+            h[8 * k + 2 * e + 1] = y1;
+            amax = fmaxf(amax, fmaxf(fabsf(y0), fabsf(y1)));
+            o[e] = pack2<T>(y0, y1);
+        }
+        if (normed)
+            reinterpret_cast<uint4 *>(normed + row * N)[threadIdx.x + k * blockDim.x] = make_uint4(o[0], o[1], o[2],
+                                                                                                   o[3]);
+    }
+    amax = block_max(amax, red);
+    const float inv = quant_inv(amax);
+    if (threadIdx.x == 0) scales[row] = __fdiv_rn(amax, 127.0f);
+    uint2 *qr = reinterpret_cast<uint2 *>(q + row * N);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+        uint32_t b[2];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const float *v = &h[8 * k + 4 * hh];
+            b[hh] = (uint32_t)(uint8_t)quant1(v[0], inv) | ((uint32_t)(uint8_t)quant1(v[1], inv) << 8) |
+                    ((uint32_t)(uint8_t)quant1(v[2], inv) << 16) | ((uint32_t)(uint8_t)quant1(v[3], inv) << 24);
+        }
+        qr[threadIdx.x + k * blockDim.x] = make_uint2(b[0], b[1]);
+    }
+}
+
 // SiLU(g) rounded to the 16-bit type, times u rounded (vllm_turing/csrc/silu_quant.cu:11-14, 39), then quant.
 template <typename T>
 __global__ void __launch_bounds__(RQ_THREADS) silu_mul_quant_kernel(const T *__restrict__ gu, int8_t *__restrict__ q,
@@ -210,6 +288,27 @@ static int smem_attr(const void *fn, int bytes) {
     return (int)cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+template <typename T>
+static int launch_norm_vec(int vpt, int t, const void *x, void *residual, const void *weight, float eps, void *q,
+                           void *scales, void *normed, int M, int N, cudaStream_t s) {
+    const T *xp = (const T *)x;
+    const T *wp = (const T *)weight;
+    T *rp = (T *)residual, *np = (T *)normed;
+    int8_t *qp = (int8_t *)q;
+    float *sp = (float *)scales;
+    switch (vpt) {
+        case 8: rms_norm_quant_vec_kernel<T, 8><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        case 7: rms_norm_quant_vec_kernel<T, 7><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        case 6: rms_norm_quant_vec_kernel<T, 6><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        case 5: rms_norm_quant_vec_kernel<T, 5><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        case 4: rms_norm_quant_vec_kernel<T, 4><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        case 3: rms_norm_quant_vec_kernel<T, 3><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        case 2: rms_norm_quant_vec_kernel<T, 2><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+        default: rms_norm_quant_vec_kernel<T, 1><<<M, t, 0, s>>>(xp, rp, wp, eps, qp, sp, np, N); break;
+    }
+    return (int)cudaGetLastError();
+}
+
 // Few rows: the row-split kernel on up to one CTA per SM (at least 256 elements per CTA); many rows: a CTA per row.
 template <typename T>
 static int launch_silu(const void *gu, void *q, void *scales, int M, int I, cudaStream_t s) {
@@ -264,6 +363,18 @@ int vt_rms_norm_quant(const void *x, void *residual, const void *weight, float e
         return VT_EARG;
     if (M == 0) return 0;
     cudaStream_t s = (cudaStream_t)stream;
+    if ((N & 7) == 0 && !((uintptr_t)x & 15) && !((uintptr_t)residual & 15) && !((uintptr_t)weight & 15) &&
+        !((uintptr_t)normed & 15) && !((uintptr_t)q & 7)) {
+        const int nv = N / 8;
+        for (int vpt = 8; vpt >= 1; --vpt) {   // threads = nv / vpt: a multiple of 32 in [64, 256]
+            if (nv % vpt) continue;
+            const int t = nv / vpt;
+            if ((t & 31) || t < 64 || t > 256) continue;
+            return dtype == 0 ? launch_norm_vec<__half>(vpt, t, x, residual, weight, eps, q, scales, normed, M, N, s)
+                              : launch_norm_vec<__nv_bfloat16>(vpt, t, x, residual, weight, eps, q, scales, normed, M,
+                                                               N, s);
+        }
+    }
     const int sm = N * 4;
     if (dtype == 0) {
         if (int rc = smem_attr((const void *)rms_norm_quant_kernel<__half>, sm)) return rc;
