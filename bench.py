@@ -3,9 +3,10 @@
 
 Workload (BASELINE.json config 1 at N = 1, the same layer tensor-parallel at N > 1, config 2's split): one "layer" is a
 decode MLP through the public API, each kernel's output feeding the next:
-  gate_up : column-parallel W8A8 linear, M tokens, [5120 -> 34816 / N] (vllm_turing::scaled_mm_, the cutlass_scaled_mm
-            replacement: the tcgen05 decode kernel)
-  silu    : SiLU(gate) * up and per-token int8 quantisation (silu_mul_quant)
+  gate_up : column-parallel W8A8 linear, M tokens, [5120 -> 34816 / N], with SiLU(gate) * up and per-token int8
+            quantisation fused in (w8a8.gate_up_silu_quant: one tcgen05 decode kernel; --mlp unfused runs the
+            reference's two ops instead: vllm_turing::scaled_mm_, the cutlass_scaled_mm replacement, then
+            silu_mul_quant)
   down    : row-parallel W8A8 linear, [17408 / N -> 5120], fused with the TP all-reduce, residual add, RMSNorm and
             per-token int8 re-quantisation (TPComm.row_linear -> vt_tp_row_linear; at N = 1 the "fused epilogue without
             collective"), whose int8 output is the next layer's input
@@ -54,6 +55,9 @@ def parse():
                     help="decode: the 64-layer MLP stack (the headline, config 1/2); prefill: the row-parallel layer "
                          "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant)")
     ap.add_argument("--proj", default="down", choices=["down", "o_proj"], help="prefill: K = 17408 or 6144 (per TP)")
+    ap.add_argument("--mlp", default="fused", choices=["fused", "unfused"],
+                    help="decode: gate_up + SiLU*up + quant as one kernel (fused, default) or the reference's two ops "
+                         "(scaled_mm_ then silu_mul_quant)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no clocks, e2e or CPU baseline")
@@ -475,11 +479,15 @@ def main():
     for i in range(min(NL, 2)):
         gu = make_layer_inputs(M, N_gu, HIDDEN, seed=100 + i, rank=rank, with_norm=False)
         dn = make_layer_inputs(M, HIDDEN, K_dn, seed=i, rank=rank)
-        base.append(dict(gu_w=gu.w.to(dev), gu_sw=gu.sw.to(dev).view(-1, 1),
+        gw, gsw = gu.w.to(dev), gu.sw.to(dev).view(-1, 1)
+        gwi, gsi = w8a8.interleave_gate_up(gw, gsw)   # once, at load time
+        base.append(dict(gu_w=gw, gu_sw=gsw, gu_wi=gwi, gu_si=gsi,
                          dn_w=dn.w.to(dev), dn_sw=dn.sw.to(dev).view(-1, 1)))
         if i == 0:
             residual0, norm_w = dn.residual.to(dev), dn.norm_w.to(dev)
-    layers = [{k: v.clone() for k, v in base[i % len(base)].items()} for i in range(NL)]
+    keep = ("gu_wi", "gu_si") if args.mlp == "fused" else ("gu_w", "gu_sw")
+    layers = [{k: v.clone() for k, v in base[i % len(base)].items() if k in keep or k.startswith("dn_")}
+              for i in range(NL)]
     del base
     # the stack's input: one hidden state every rank holds (seeded independently of the rank), quantised per token
     x0, xs0 = quant_per_token(torch.randn(M, HIDDEN, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16))
@@ -502,6 +510,9 @@ def main():
     def silu(s):
         silu_mul_quant(out_gu, h_q, h_s)
 
+    def gate_up_silu(s):
+        w8a8.gate_up_silu_quant(x_q, s["gu_wi"], x_s, s["gu_si"], q=h_q, scales=h_s)
+
     def down(s):
         comm.row_linear(h_q, s["dn_w"], h_s, s["dn_sw"], residual=residual, norm_w=norm_w, eps=1e-6, q=x_q, scales=x_s)
 
@@ -521,7 +532,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
-    LAYER = (gate_up, silu, down)
+    LAYER = (gate_up_silu, down) if args.mlp == "fused" else (gate_up, silu, down)
     K, W = args.steps, max(args.warmup, 1 if args.profile else 3)
     if args.profile:   # eager launches of two layers, for ncu launch lists and captures
         for i in range(W + K):
@@ -548,7 +559,10 @@ def main():
         return g
 
     g_step = capture(LAYER)
-    g_k = {"gate_up": capture((gate_up,)), "silu": capture((silu,)), "down": capture((down,))}
+    if args.mlp == "fused":
+        g_k = {"gate_up_silu": capture((gate_up_silu,)), "down": capture((down,))}
+    else:
+        g_k = {"gate_up": capture((gate_up,)), "silu": capture((silu,)), "down": capture((down,))}
     barrier()
 
     def timed(fn, n):
@@ -615,8 +629,9 @@ def main():
         comm.check()
         e2e = {"value": layer_ops(M, world) * NL / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "us_per_layer": t_e2e / NL * 1e6,
-               "api": "vllm_turing::scaled_mm_ + silu_mul_quant + TPComm.row_linear per layer, captured in a CUDA "
-                      "graph; pinned host inputs copied in and outputs read back every step"}
+               "api": ("w8a8.gate_up_silu_quant" if args.mlp == "fused" else "vllm_turing::scaled_mm_ + silu_mul_quant")
+                   + " + TPComm.row_linear per layer, captured in a CUDA graph; pinned host inputs copied in and "
+                     "outputs read back every step"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -627,9 +642,11 @@ def main():
 
     # algorithmic HBM bytes per launch (one layer) of each kernel
     alg = {"gate_up": bytes_gu_w + M * HIDDEN + 4 * M + 4 * N_gu + 2 * M * N_gu,
+           "gate_up_silu": bytes_gu_w + M * HIDDEN + 4 * M + 4 * N_gu + M * K_dn + 4 * M,
            "silu": 2 * M * N_gu + M * K_dn + 4 * M,
            "down": bytes_dn_w + M * K_dn + 4 * M + 4 * HIDDEN + M * HIDDEN * (2 + 2 + 1) + 4 * M + 2 * HIDDEN}
     names = {"gate_up": "tc_gemm_kernel (gate_up, tcgen05 decode)", "silu": "silu_mul_quant_kernel",
+             "gate_up_silu": "gate_up_silu_kernel (gate_up + SiLU*up + int8 quant, tcgen05 decode)",
              "down": "tp_row_linear_tc_kernel (down + all-reduce + RMSNorm + quant)"}
     dom = max(t_k, key=t_k.get)
     hbm, peak_kind = peaks()
@@ -644,9 +661,10 @@ def main():
         "steps": K, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
         "us_per_layer": t_layer * 1e6, "bus_gbs": bus,
-        "config": {"workload": f"decode W8A8 MLP stack of {NL} layers, M={M}: gate_up 5120->34816 column-parallel, "
-                               f"silu_mul_quant, down 17408->5120 row-parallel fused with TP all-reduce + RMSNorm + "
-                               f"int8 quant (BASELINE config 1 per layer at N=1, config 2 split at N>1)",
+        "config": {"workload": f"decode W8A8 MLP stack of {NL} layers, M={M}: gate_up 5120->34816 column-parallel "
+                               f"with SiLU*up + int8 quant ({'one kernel' if args.mlp == 'fused' else 'two ops'}), "
+                               f"down 17408->5120 row-parallel fused with TP all-reduce + RMSNorm + int8 quant "
+                               f"(BASELINE config 1 per layer at N=1, config 2 split at N>1)",
                    "tokens": M, "layers": NL, "tp": world, "K_down_local": K_dn, "N_gate_up_local": N_gu,
                    "l2": f"inputs larger than L2: {NL} layers with their own weights, "
                          f"{NL * (bytes_gu_w + bytes_dn_w) / 2**20:.0f} MiB of weights per step",
@@ -656,7 +674,7 @@ def main():
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "bytes_per_launch": alg[dom],
                      "peak_kind": peak_kind},
-        "clocks": clocks, "gpu_launches": 3 * NL * K, "e2e": e2e, "cpu_baseline": cpu,
+        "clocks": clocks, "gpu_launches": len(LAYER) * NL * K, "e2e": e2e, "cpu_baseline": cpu,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -114,3 +114,17 @@ def test_synthetic_inputs_are_deterministic():
 @pytest.mark.parametrize("mod", ["w8a8", "hostar", "quantfuse", "customar", "dmaag", "tailoverlap", "comm"])
 def test_modules_import_without_gpu(mod):
     __import__(f"vllm_turing_b200.{mod}")
+
+
+def test_interleave_gate_up_order():
+    """tile t of the interleaved weight = gate rows 64t..64t+63, then up rows 64t..64t+63 (CPU, no kernel)"""
+    from vllm_turing_b200 import w8a8
+    I, K = 192, 32
+    w = torch.arange(2 * I, dtype=torch.int32).view(-1, 1).expand(2 * I, K).to(torch.int16)
+    s = torch.arange(2 * I, dtype=torch.float32)
+    wi, si = w8a8.interleave_gate_up(w, s)
+    rows = wi[:, 0].tolist()
+    for t in range(I // 64):
+        assert rows[128 * t:128 * t + 64] == list(range(64 * t, 64 * t + 64))
+        assert rows[128 * t + 64:128 * t + 128] == list(range(I + 64 * t, I + 64 * t + 64))
+    assert si.tolist() == [float(r) for r in rows]

@@ -42,6 +42,21 @@ def child():
     assert L.vt_status(1) == 0
     assert L.vt_workspace_nonzero(8 << 20) == 0
 
+    from vllm_turing_b200 import w8a8
+    from vllm_turing_b200.tailoverlap import silu_mul_quant
+    for M, I, K in ((5, 4352, 5120), (24, 1088, 2176)):   # the fused gate/up + SiLU + quant kernel
+        a, w = rand_int8((M, K), 3 * M), rand_int8((2 * I, K), 5 * I)
+        ac, wc = a.cuda(), w.cuda()
+        sa = (torch.rand(M, 1, generator=torch.Generator().manual_seed(M)) * 2e-2).cuda()
+        sw = (torch.rand(2 * I, 1, generator=torch.Generator().manual_seed(I)) * 2e-4).cuda()
+        wi, si = w8a8.interleave_gate_up(wc, sw)
+        q, sc = w8a8.gate_up_silu_quant(ac, wi, sa, si)
+        out = torch.empty(M, 2 * I, dtype=torch.bfloat16, device="cuda")
+        w8a8.mma(out, ac, wc.t(), sa, sw, None)
+        q0, s0 = silu_mul_quant(out)
+        torch.cuda.synchronize()
+        assert torch.equal(q, q0) and torch.equal(sc.view(-1), s0.view(-1)), (M, I, K)
+
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=os.environ.get("VT_TEST_PORT", "29631"))
     dist.init_process_group("gloo", rank=0, world_size=1)
     torch.cuda.set_device(0)

@@ -20,7 +20,7 @@ _csrc = os.path.join(_here, "csrc")
 _include = os.path.join(os.path.dirname(_here), "include")
 LIB_NAME = "libvllm_turing_b200.so"
 LIB_PATH = os.path.join(_here, LIB_NAME)
-SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "norm_quant.cu", "tp_comm.cu", "tp_fused.cu")
+SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "norm_quant.cu", "tp_comm.cu", "tp_fused.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 _lib = None
 
@@ -114,6 +114,8 @@ SIGNATURES = {
     "w8a8_mma_ws": (_I, [_P] * 6 + [_I] * 6 + [_P, _SZ, _P]),
     "w8a8_big": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "vt_gemm_s32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
+    "vt_gate_up_silu_quant_ws_bytes": (_SZ, [_I, _I]),
+    "vt_gate_up_silu_quant": (_I, [_P] * 6 + [_I] * 5 + [_P, _SZ, _P]),
     "vt_scaled_int8_quant": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_rms_norm_quant": (_I, [_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _P]),
     "silu_mul_quant": (_I, [_P, _P, _P, _I, _I, _P]),

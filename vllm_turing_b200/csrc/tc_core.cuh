@@ -144,7 +144,7 @@ template <int BN, int KBS> struct TcLayout {
     static constexpr int KB_BYTES = A_BYTES + B_BYTES;
     static constexpr int STAGE = KBS * KB_BYTES;    // stage = [KBS A blocks][KBS B blocks]
     static constexpr int TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-    static constexpr int BAR_BYTES = 1024;          // mbarriers, TMEM slot, flags and the finisher's 64 floats
+    static constexpr int BAR_BYTES = 512;           // mbarriers, TMEM slot and flags; the finisher's floats follow
 };
 
 // The CTA's pieces: (A tile, B tile, K-block range). Identical sequence in every role of the CTA.
@@ -206,12 +206,13 @@ __device__ __forceinline__ unsigned char *tc_align1024(unsigned char *p) {
 }
 
 // Output finisher of the decode orientation: thread = output feature n, acc[m] for the token rows. Finisher
-// interface: on_start(P, sm) once per epilogue thread after pdl_wait (sm: 64 floats of shared memory the finisher may
-// fill), then the epilogue warps synchronise and each calls post_start() (per-thread state in registers); prep(P, n)
+// interface: on_start(P, sm) once per epilogue thread after pdl_wait (sm: Fin::kSmemFloats >= 64 floats of shared
+// memory the finisher owns), then the epilogue warps synchronise and each calls post_start() (per-thread state in registers); prep(P, n)
 // before the piece's accumulators are ready (global loads whose latency then hides behind the MMAs);
 // operator()(P, n, nok, acc, prep) with the accumulators.
 template <typename T, int BN>
 struct TcOutEpi {
+    static constexpr int kSmemFloats = 64;
     struct Prep {
         float swn, bn;
     };
@@ -309,7 +310,8 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
     uint64_t *drain = tempty + 2;    // [1]: the MMA issuer's last commit
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 4);   // [0] abort
-    float *epi_sm = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(full) + 512);   // [64] for the finisher
+    // the finisher's shared floats (Fin::kSmemFloats, at least 64) after the barriers
+    float *epi_sm = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(full) + Lay::BAR_BYTES);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_launch_dependents();   // once every CTA of this grid got here, the next kernel may take SMs as they free up
@@ -568,17 +570,17 @@ inline bool tc_make_map(CUtensorMap *m, const void *base, int rows, int K, int b
     return make_map_i8(m, base, rows, K, TC_BK, box_rows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// stages that fit the opt-in shared memory (less the 1024-byte alignment slack, the barriers and up to 1 KB of static
-// shared variables of the kernel)
+// Stages that fit the opt-in shared memory, less the 1024-byte alignment slack, the barriers, the finisher's
+// `epi_floats` shared floats and up to 1 KB of static shared variables of the kernel.
 template <int BN, int KBS>
-inline int tc_stages(int dev) {
+inline int tc_stages(int dev, int epi_floats = 64) {
     using Lay = TcLayout<BN, KBS>;
-    int s = (max_smem_optin(dev) - 1024 - Lay::BAR_BYTES - 1024) / Lay::STAGE;
+    int s = (max_smem_optin(dev) - 1024 - Lay::BAR_BYTES - 4 * epi_floats - 1024) / Lay::STAGE;
     return s > 16 ? 16 : s;
 }
 template <int BN, int KBS>
-inline int tc_smem_bytes(int stages) {
-    return stages * TcLayout<BN, KBS>::STAGE + 1024 + TcLayout<BN, KBS>::BAR_BYTES;
+inline int tc_smem_bytes(int stages, int epi_floats = 64) {
+    return stages * TcLayout<BN, KBS>::STAGE + 1024 + TcLayout<BN, KBS>::BAR_BYTES + 4 * epi_floats;
 }
 
 // K blocks per pipeline stage of the decode orientation: VLLM_TURING_TC_KBS (1, 2 or 4; default 4)

@@ -307,6 +307,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1)
 // n .. n + 3 (gathered by shuffles) to every rank's receive slot.
 template <typename T, int BN>
 struct TcLLPushEpi {
+    static constexpr int kSmemFloats = 64;
     struct Prep {
         float swn;
     };

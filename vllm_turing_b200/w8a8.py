@@ -59,6 +59,44 @@ def workspace(device, M, N):
     return ws
 
 
+def interleave_gate_up(w, sw):
+    """The gate/up weight [2I, K] (gate rows, then up rows) and its scales [2I] in the row order gate_up_silu_quant
+    takes: 128-row tile t = gate rows 64t..64t+63, then up rows 64t..64t+63. Made once, when the weights are loaded."""
+    n2, K = w.shape
+    I = n2 // 2
+    if n2 != 2 * I or I % 64:
+        raise ValueError("interleave_gate_up: 2I rows with I % 64 == 0")
+    wi = torch.stack((w[:I].reshape(I // 64, 64, K), w[I:].reshape(I // 64, 64, K)), dim=1).reshape(n2, K)
+    s = sw.reshape(-1)
+    si = torch.stack((s[:I].reshape(I // 64, 64), s[I:].reshape(I // 64, 64)), dim=1).reshape(n2)
+    return wi.contiguous(), si.contiguous()
+
+
+_silu_ws = {}   # device -> zeroed workspace of gate_up_silu_quant (graph capture keeps its address)
+
+
+def gate_up_silu_quant(a, w_il, sa, sw_il, q=None, scales=None, dtype=torch.bfloat16):
+    """(q int8 [M, I], scales float32 [M, 1]) = silu_mul_quant(scaled_mm(a, w.t(), sa, sw)) in one kernel, for the
+    interleaved weight of interleave_gate_up. Bit-identical to the two-op chain."""
+    M, K = a.shape
+    I = w_il.shape[0] // 2
+    L = lib()
+    need = L.vt_gate_up_silu_quant_ws_bytes(M, I)
+    ws = _silu_ws.get(a.device)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("vllm_turing_b200: gate_up_silu_quant workspace must be sized before CUDA graph capture")
+        ws = _silu_ws[a.device] = torch.zeros(max(need, 4 << 20), dtype=torch.uint8, device=a.device)
+    q = q if q is not None else torch.empty(M, I, dtype=torch.int8, device=a.device)
+    scales = scales if scales is not None else torch.empty(M, 1, dtype=torch.float32, device=a.device)
+    rc = L.vt_gate_up_silu_quant(a.data_ptr(), w_il.data_ptr(), sa.data_ptr(), sw_il.data_ptr(), q.data_ptr(),
+                                 scales.data_ptr(), M, I, K, int(sa.numel() > 1), _dtype_code(dtype), ws.data_ptr(),
+                                 ws.numel(), _stream())
+    if rc != 0:
+        raise RuntimeError(f"vt_gate_up_silu_quant failed: {rc}")
+    return q, scales
+
+
 def gemv(out, a, b, sa, sb, bias):
     """out[M, N] = (a . w^T) * sa * sb (+ bias), w = b.t() the row-major [N, K] weight."""
     M, K = a.shape
