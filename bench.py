@@ -51,9 +51,10 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="tokens per step (decode default 5, prefill 8192)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "prefill"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce"],
                     help="decode: the 64-layer MLP stack (the headline, config 1/2); prefill: the row-parallel layer "
-                         "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant)")
+                         "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant); "
+                         "allreduce: config 4's size sweep, 1 KB .. 256 MB, against NCCL on the same ranks")
     ap.add_argument("--proj", default="down", choices=["down", "o_proj"], help="prefill: K = 17408 or 6144 (per TP)")
     ap.add_argument("--mlp", default="fused", choices=["fused", "unfused"],
                     help="decode: gate_up + SiLU*up + quant as one kernel (fused, default) or the reference's two ops "
@@ -453,6 +454,89 @@ def run_prefill(args, world, rank, local, dev, gloo):
     dist.destroy_process_group()
 
 
+def run_allreduce(args, world, rank, local, dev, gloo):
+    """Config 4's all-reduce sweep: bf16 messages of 1 KB .. 256 MB through TPComm.all_reduce (one-shot LL up to the
+    LL capacity, two-shot above) and through NCCL (torch.distributed, the library baseline) on the same ranks. Each
+    size: R calls captured in a CUDA graph, in place, CUDA events, max over ranks; bus GB/s = 2 (n-1)/n x bytes / t."""
+    import torch
+    import torch.distributed as dist
+
+    from vllm_turing_b200 import _build
+    from vllm_turing_b200.comm import TPComm
+
+    _build.load()
+    sizes = [1 << k for k in range(10, 29, 2)]   # 1 KB .. 256 MB
+    comm = TPComm(gloo, dev)
+    stream = torch.cuda.current_stream()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    rows = []
+    for nbytes in sizes:
+        n = nbytes // 2
+        x = torch.randn(n, generator=torch.Generator().manual_seed(rank)).to(torch.bfloat16).to(dev)
+        reps = 50 if nbytes <= (1 << 20) else (10 if nbytes <= (16 << 20) else 3)
+        res = {}
+        for impl in ("ours", "nccl"):
+            if impl == "nccl" and world == 1:
+                continue
+
+            def once():
+                if impl == "ours":
+                    comm.all_reduce(x, out=x)
+                else:
+                    dist.all_reduce(x)
+
+            for _ in range(3):
+                once()
+            torch.cuda.synchronize()
+            dist.barrier(group=gloo)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for _ in range(reps):
+                    once()
+            g.replay()
+            torch.cuda.synchronize()
+            dist.barrier(group=gloo)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            g.replay()
+            b.record(stream)
+            torch.cuda.synchronize()
+            dist.barrier(group=gloo)
+            t = max_over_ranks(a.elapsed_time(b) / reps) / 1e3
+            res[impl] = t
+            del g
+        comm.check()
+        bus = lambda t: (2.0 * (world - 1) / world * nbytes / t / 1e9) if world > 1 else 0.0   # noqa: E731
+        rows.append({"bytes": nbytes, "us": res["ours"] * 1e6, "bus_gbs": bus(res["ours"]),
+                     "nccl_us": res["nccl"] * 1e6 if "nccl" in res else None,
+                     "nccl_bus_gbs": bus(res["nccl"]) if "nccl" in res else None})
+        del x
+    top = rows[-1]
+    line = {
+        "metric": METRIC, "value": top["bus_gbs"], "unit": "GB/s", "n_gpus": world, "steps": 1, "warmup": 3,
+        "ms_per_step": top["us"] / 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic", "mode": "allreduce",
+        "config": {"workload": "TP all-reduce sweep 1 KB .. 256 MB, bf16, in place (BASELINE config 4)",
+                   "tp": world, "launch": "CUDA graph of R calls per size", "parallelism": f"tp{world}"},
+        "sweep": rows,
+        "roofline": {"bound": "nvlink", "kernel": "ar_twoshot_kernel (256 MB)", "achieved": top["bus_gbs"],
+                     "peak": 770.0, "unit": "GB/s", "frac": top["bus_gbs"] / 770.0, "traffic": None,
+                     "peak_kind": "measured peer copy per direction"},
+        "gpu_launches": None, "e2e": None, "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    comm.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -468,6 +552,8 @@ def main():
     world, rank, local, dev, gloo = dist_setup(args)
     if args.mode == "prefill":
         return run_prefill(args, world, rank, local, dev, gloo)
+    if args.mode == "allreduce":
+        return run_allreduce(args, world, rank, local, dev, gloo)
     _build.load()
     M = args.tokens
     NL = args.layers

@@ -86,6 +86,21 @@ __device__ __forceinline__ void acc8(float (&s)[8], const uint4 &v, bool first) 
     for (int k = 0; k < 8; ++k) s[k] = first ? f[k] : s[k] + f[k];
 }
 
+// dst[u - off] = src[u] for u in [b, e), TS_UNROLL independent loads in flight per thread (NVLink and HBM latency)
+constexpr int TS_UNROLL = 4;
+__device__ __forceinline__ void copy_units(uint4 *dst, long long off, const uint4 *src, long long b, long long e) {
+    const int nt = blockDim.x;
+    for (long long u0 = b + threadIdx.x; u0 < e; u0 += (long long)TS_UNROLL * nt) {
+        uint4 v[TS_UNROLL];
+#pragma unroll
+        for (int k = 0; k < TS_UNROLL; ++k)
+            if (u0 + k * nt < e) v[k] = src[u0 + k * nt];
+#pragma unroll
+        for (int k = 0; k < TS_UNROLL; ++k)
+            if (u0 + k * nt < e) dst[u0 + k * nt - off] = v[k];
+    }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, const uint4 *in, uint4 *out,
                                                                 long long U,
@@ -100,8 +115,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, cons
     for (int k = 1; k < W; ++k) {
         const int dst = (R + k) % W;
         slice_of(U, W, dst, G, j, cs, b, e);
-        uint4 *rb = reinterpret_cast<uint4 *>(c.rs_buf(dst, p, R));
-        for (long long u = b + tid; u < e; u += blockDim.x) rb[u - cs] = in[u];
+        copy_units(reinterpret_cast<uint4 *>(c.rs_buf(dst, p, R)), cs, in, b, e);
     }
     __syncthreads();
     if (tid < W && tid != R) st_release_sys(c.flag(tid, p, 0, R, j), seq);
@@ -115,16 +129,30 @@ __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, cons
     (void)ok;
     slice_of(U, W, R, G, j, cs, b, e);
     uint4 *ag = reinterpret_cast<uint4 *>(c.ag_buf(R, p));
-    for (long long u = b + tid; u < e; u += blockDim.x) {
-        float s[8];
-        for (int r = 0; r < W; ++r) {
-            const uint4 v = (r == R) ? in[u] : reinterpret_cast<const uint4 *>(c.rs_buf(R, p, r))[u - cs];
-            acc8<T>(s, v, r == 0);
+    const int nt = blockDim.x;
+    for (long long u0 = b + tid; u0 < e; u0 += 2LL * nt) {   // two units per step: 2 x world loads in flight
+        uint4 v[2][COMM_MAX_RANKS];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const long long u = u0 + k * nt;
+            if (u >= e) continue;
+#pragma unroll
+            for (int r = 0; r < COMM_MAX_RANKS; ++r)
+                if (r < W) v[k][r] = (r == R) ? in[u] : reinterpret_cast<const uint4 *>(c.rs_buf(R, p, r))[u - cs];
         }
-        const uint4 o = make_uint4(pack2<T>(s[0], s[1]), pack2<T>(s[2], s[3]), pack2<T>(s[4], s[5]),
-                                   pack2<T>(s[6], s[7]));
-        out[u] = o;
-        ag[u - cs] = o;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const long long u = u0 + k * nt;
+            if (u >= e) continue;
+            float s[8];
+#pragma unroll
+            for (int r = 0; r < COMM_MAX_RANKS; ++r)
+                if (r < W) acc8<T>(s, v[k][r], r == 0);   // rank order: identical bits on every rank
+            const uint4 o = make_uint4(pack2<T>(s[0], s[1]), pack2<T>(s[2], s[3]), pack2<T>(s[4], s[5]),
+                                       pack2<T>(s[6], s[7]));
+            out[u] = o;
+            ag[u - cs] = o;
+        }
     }
     __syncthreads();
     if (tid < W && tid != R) st_release_sys(c.flag(tid, p, 1, R, j), seq);
@@ -135,8 +163,8 @@ __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, cons
     for (int k = 1; k < W; ++k) {
         const int src = (R + k) % W;
         slice_of(U, W, src, G, j, cs, b, e);
-        const uint4 *sb = reinterpret_cast<const uint4 *>(c.ag_buf(src, p));
-        for (long long u = b + tid; u < e; u += blockDim.x) out[u] = sb[u - cs];
+        // out[cs + i] = the peer's reduced slice, read over NVLink
+        copy_units(out + cs, 0, reinterpret_cast<const uint4 *>(c.ag_buf(src, p)), b - cs, e - cs);
     }
     comm_end(c, seq);
 }
