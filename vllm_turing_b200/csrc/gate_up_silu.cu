@@ -168,7 +168,7 @@ static int launch_silu_gemm(const CUtensorMap &mw, const CUtensorMap &ma, TcArgs
     const int dev = cur_device();
     if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
     constexpr int EF = TcSiluEpi<T, BN>::kSmemFloats;
-    const int stages = tc_stages<BN, KBS>(dev, EF);
+    const int stages = tc_stages<BN, KBS>(dev, EF, decode_smem_budget());
     if (stages < 2) return VT_EARG;
     P.stages = stages;
     const int smem = tc_smem_bytes<BN, KBS>(stages, EF);

@@ -572,11 +572,27 @@ inline bool tc_make_map(CUtensorMap *m, const void *base, int rows, int K, int b
 
 // Stages that fit the opt-in shared memory, less the 1024-byte alignment slack, the barriers, the finisher's
 // `epi_floats` shared floats and up to 1 KB of static shared variables of the kernel.
+// budget: dynamic shared memory to stay under (0 = the device's opt-in maximum).
 template <int BN, int KBS>
-inline int tc_stages(int dev, int epi_floats = 64) {
+inline int tc_stages(int dev, int epi_floats = 64, int budget = 0) {
     using Lay = TcLayout<BN, KBS>;
-    int s = (max_smem_optin(dev) - 1024 - Lay::BAR_BYTES - 4 * epi_floats - 1024) / Lay::STAGE;
+    const int cap = budget > 0 && budget < max_smem_optin(dev) ? budget : max_smem_optin(dev);
+    int s = (cap - 1024 - Lay::BAR_BYTES - 4 * epi_floats - 1024) / Lay::STAGE;
     return s > 16 ? 16 : s;
+}
+
+// Shared-memory budget of the decode kernels: VLLM_TURING_TC_SMEM_KB (default 0 = all of it). Under half an SM's
+// shared memory, the next decode kernel's CTAs can become resident beside the current one's (programmatic dependent
+// launch) and fill their pipelines during its tail. Measured on the 64-layer stack: 112 KB with 2 K blocks per stage
+// is even at TP4 and 5 % slower at TP1 (the halved pipeline costs more than the overlap gains), so it is off.
+inline int decode_smem_budget() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_TC_SMEM_KB");
+        v = e ? atoi(e) * 1024 : 0;
+        if (v < 0) v = 0;
+    }
+    return v;
 }
 template <int BN, int KBS>
 inline int tc_smem_bytes(int stages, int epi_floats = 64) {

@@ -396,7 +396,7 @@ static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     G.slots = reinterpret_cast<uint4 *>(local + P.c.L.scratch_off);
     G.status = reinterpret_cast<unsigned *>(local + 128);
     G.timeout_ns = P.pipe_timeout;
-    const int stages = tc_stages<BN, KBS>(dev);
+    const int stages = tc_stages<BN, KBS>(dev, 64, decode_smem_budget());
     if (stages < 2) return VT_EARG;
     G.stages = stages;
     const int smem = tc_smem_bytes<BN, KBS>(stages);

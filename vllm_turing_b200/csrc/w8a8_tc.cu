@@ -36,7 +36,7 @@ template <typename T, int BN, bool SWAP, int KBS>
 static int launch_tc(const CUtensorMap &ma, const CUtensorMap &mb, TcArgs P, cudaStream_t s) {
     const int dev = cur_device();
     if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
-    const int stages = tc_stages<BN, KBS>(dev);
+    const int stages = tc_stages<BN, KBS>(dev, 64, SWAP ? decode_smem_budget() : 0);
     if (stages < 2) return VT_EARG;
     P.stages = stages;
     const int smem = tc_smem_bytes<BN, KBS>(stages);
