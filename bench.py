@@ -3,10 +3,10 @@
 
 Workload (BASELINE.json config 1 at N = 1, the same layer tensor-parallel at N > 1, config 2's split): one "layer" is a
 decode MLP through the public API, each kernel's output feeding the next:
-  gate_up : column-parallel W8A8 linear, M tokens, [5120 -> 34816 / N], with SiLU(gate) * up and per-token int8
-            quantisation fused in (w8a8.gate_up_silu_quant: one tcgen05 decode kernel; --mlp unfused runs the
-            reference's two ops instead: vllm_turing::scaled_mm_, the cutlass_scaled_mm replacement, then
-            silu_mul_quant)
+  gate_up : column-parallel W8A8 linear, M tokens, [5120 -> 34816 / N] (vllm_turing::scaled_mm_, the
+            cutlass_scaled_mm replacement: the tcgen05 decode kernel)
+  silu    : SiLU(gate) * up and per-token int8 quantisation (silu_mul_quant); --mlp fused runs gate_up and silu as one
+            kernel instead (w8a8.gate_up_silu_quant)
   down    : row-parallel W8A8 linear, [17408 / N -> 5120], fused with the TP all-reduce, residual add, RMSNorm and
             per-token int8 re-quantisation (TPComm.row_linear -> vt_tp_row_linear; at N = 1 the "fused epilogue without
             collective"), whose int8 output is the next layer's input
@@ -56,9 +56,9 @@ def parse():
                          "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant); "
                          "allreduce: config 4's size sweep, 1 KB .. 256 MB, against NCCL on the same ranks")
     ap.add_argument("--proj", default="down", choices=["down", "o_proj"], help="prefill: K = 17408 or 6144 (per TP)")
-    ap.add_argument("--mlp", default="fused", choices=["fused", "unfused"],
-                    help="decode: gate_up + SiLU*up + quant as one kernel (fused, default) or the reference's two ops "
-                         "(scaled_mm_ then silu_mul_quant)")
+    ap.add_argument("--mlp", default="unfused", choices=["fused", "unfused"],
+                    help="decode: gate_up then SiLU*up + quant as the reference's two ops (scaled_mm_, silu_mul_quant; "
+                         "default) or as one kernel (w8a8.gate_up_silu_quant; measured ~1 us per layer slower)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true", help="short run for ncu: no clocks, e2e or CPU baseline")

@@ -73,8 +73,8 @@ int vt_gemm_s32(const void *a, const void *w, void *acc, int M, int N, int K, vo
  * SiLU(gate) * up, [gate | up] the W8A8 linear a [M, K] . w^T with w [2I, K] int8 and sw [2I] float32 in the
  * interleaved row order (128-row tile t = gate rows 64t..64t+63, then up rows 64t..64t+63; made once at load time),
  * sa [M] (sa_rows = 1) or [1]. Bit-identical to w8a8_mma / scaled_mm_ with the plain weight followed by
- * silu_mul_quant. 1 <= M <= 32, I % 64 == 0, K % 16 == 0; a zeroed, 256-byte aligned workspace of
- * vt_gate_up_silu_quant_ws_bytes(M, I) bytes that the kernel leaves zeroed; calls sharing it must be stream-ordered.
+ * silu_mul_quant. 1 <= M <= 32, I % 64 == 0, K % 16 == 0; a 256-byte aligned workspace of
+ * vt_gate_up_silu_quant_ws_bytes(M, I) bytes, zeroed once before first use; calls sharing it must be stream-ordered.
  * dtype (0 fp16 / 1 bf16): the type of the gate / up / product values. Replaces the pair scaled_mm_ (w8a8.py:235-244)
  * + silu_mul_quant (silu_quant.cu:71-77, tailoverlap.py:148-151). */
 size_t vt_gate_up_silu_quant_ws_bytes(int M, int I);

@@ -11,11 +11,14 @@
 // gate rows of features 64t .. 64t+63 followed by the up rows of the same features (vllm_turing_b200.w8a8
 // .interleave_gate_up). The GEMM is the tcgen05 decode core (tc_core.cuh) with a finisher that, per finished tile, has
 // the up half of its epilogue threads hand their bf16 values to the gate half through shared memory; the gate half
-// forms p, parks it in a bf16 scratch and raises the token row's absmax (atomicMax on the float's bits: p's magnitude
-// is non-negative, so the maximum does not depend on arrival order). After the last tile -- a bounded grid-wide
-// arrival count; the grid is one CTA per SM, all resident -- every CTA quantises an even share of p with the final
-// maxima, returns its share of the scratch to zero, and the last CTA out resets the maxima and counters: the
-// workspace is zero again for the next call.
+// forms p, parks it in a bf16 scratch and keeps a running max |p| per token row. Then each CTA publishes its row
+// maxima as 8-byte words tagged with the call's epoch (value and tag in one store, after a fence for its products)
+// and leaves, freeing its SM for the next kernel in the stream: under programmatic dependent launch the down
+// projection's CTAs take those SMs and start streaming weights while the slowest tiles here finish. Sixteen CTAs
+// stay: they read every CTA's words -- a bounded wait; the grid is one CTA per SM, all resident -- take the maximum
+// (order-independent) and quantise an even share of p. CTA 0 advances the epoch once it has seen every CTA's word
+// (every CTA has read the old epoch by then), so an earlier call's words are never taken for this call's. Only the
+// split-K slots must be zero between calls, and the GEMM leaves them so.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -31,22 +34,24 @@ namespace vt {
 
 constexpr int SILU_MAX_M = 32;
 
-// Workspace of one call, all zero between calls: [status 256 B][split-K slots][sync 256 B][p: bf16 M x I]
+// Workspace of one call: [status 256 B][split-K slots (zero between calls)][sync 256 B][max words][p: bf16 M x I].
+// The max words are tagged with the call's epoch, so nothing but the slots needs to return to zero.
 struct SiluSync {
-    unsigned amax[SILU_MAX_M];   // float bits of max |p| per token row
-    unsigned arrive, leave;
+    unsigned epoch;   // calls completed on this workspace (advanced by CTA 0 once every CTA has read it)
 };
 
 template <typename T>
 struct SiluArgs {
     SiluSync *sync;
-    T *p;               // [M, I] scratch
-    int8_t *q;          // [M, I]
-    float *scales;      // [M]
+    unsigned long long *words;   // [grid][M] {float bits of this CTA's max |p| of row m, epoch + 1}
+    T *p;                        // [M, I] scratch: written by the tile's finisher, read back by the same thread
+    int8_t *q;                   // [M, I]
+    float *scales;               // [M]
     int I;
 };
 
 // Tile finisher: thread = tile row `row` (0..63 gate of feature 64 ta + row, 64..127 up of feature 64 ta + row - 64).
+// Keeps, per gate thread, the running max |p| of each token row over the tiles it finished (lmax).
 template <typename T, int BN>
 struct TcSiluEpi {
     static constexpr int kSmemFloats = 64 + 64 * BN;   // token scales, then the up values [BN][64]
@@ -55,79 +60,112 @@ struct TcSiluEpi {
     };
     SiluArgs<T> S;
     float *sa_sm, *ubuf;
+    unsigned *s_tag;   // shared: this call's tag (epoch + 1), read after pdl_wait, before the GEMM's tail
+    float lmax[BN];
     __device__ __forceinline__ void on_start(const TcArgs &P, float *sm) {
         sa_sm = sm;
         ubuf = sm + 64;
         const int t = threadIdx.x - TC_EPI_LEAD;
         if (t < P.M) sm[t] = P.sa[P.sa_rows ? t : 0];
+        if (t == 0) *s_tag = *reinterpret_cast<volatile unsigned *>(&S.sync->epoch) + 1u;
+#pragma unroll
+        for (int m = 0; m < BN; ++m) lmax[m] = 0.0f;
     }
     __device__ __forceinline__ void post_start() {}
     __device__ __forceinline__ Prep prep(const TcArgs &P, int n) const { return Prep{n < P.N ? P.sw[n] : 0.0f}; }
     __device__ __forceinline__ void operator()(const TcArgs &P, int n, bool nok, const int (&acc)[BN],
-                                               const Prep &pr) const {
+                                               const Prep &pr) {
         const int row = n & (TC_BM - 1), M = P.M;
-        const int lane = threadIdx.x & 31;
         if (row >= 64) {   // up half: bf16 values to the gate half
 #pragma unroll
             for (int m = 0; m < BN; ++m)
                 if (m < M) ubuf[m * 64 + row - 64] = nok ? rnd<T>(dequant1(acc[m], sa_sm[m], pr.swn)) : 0.0f;
         }
         named_sync(TC_EPI_BAR, 128);
-        if (row < 64) {
+        if (row < 64 && nok) {
             const int j = (n >> 7) * 64 + row;   // feature index in [0, I)
 #pragma unroll
             for (int m = 0; m < BN; ++m) {
-                if (m >= M) break;   // uniform
+                if (m >= M) break;
                 const float g = rnd<T>(dequant1(acc[m], sa_sm[m], pr.swn));
                 const float sg = rnd<T>(__fdiv_rn(g, 1.0f + expf(-g)));
-                const float p = nok ? rnd<T>(__fmul_rn(sg, ubuf[m * 64 + row])) : 0.0f;
-                if (nok) S.p[(size_t)m * S.I + j] = f2t<T>(p);
-                float a = fabsf(p);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-                if (lane == 0) atomicMax(&S.sync->amax[m], __float_as_uint(a));
+                const float p = rnd<T>(__fmul_rn(sg, ubuf[m * 64 + row]));
+                S.p[(size_t)m * S.I + j] = f2t<T>(p);
+                lmax[m] = fmaxf(lmax[m], fabsf(p));
             }
         }
         named_sync(TC_EPI_BAR, 128);   // the up values are read: the next tile may overwrite them
     }
 };
 
+constexpr int SILU_QUANT_CTAS = 16;   // CTAs that stay for the quantisation; the rest leave their SMs at once
+
 template <typename T, int BN, int KBS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     gate_up_silu_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
                         TcArgs P, SiluArgs<T> S) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ float s_part[2][SILU_MAX_M];   // the two gate warps' maxima
+    __shared__ unsigned s_gmax[SILU_MAX_M];   // the grid's maxima (float bits)
     __shared__ float s_inv[SILU_MAX_M];
-    TcSiluEpi<T, BN> fin{S, nullptr, nullptr};
+    __shared__ unsigned s_tag;
+    TcSiluEpi<T, BN> fin{S, nullptr, nullptr, &s_tag, {}};
     tc_phase<T, BN, true, KBS>(&tmap_w, &tmap_a, P, smem_raw, fin);   // ends with __syncthreads
 
-    // every CTA's tiles are finished once all CTAs arrived: the row maxima are final
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&S.sync->arrive, 1u);
-        const uint64_t deadline = globaltimer() + P.timeout_ns;
-        uint32_t it = 0;
-        while (ld_acquire_gpu(reinterpret_cast<const int *>(&S.sync->arrive)) < (int)gridDim.x) {
-            if ((++it & 63u) == 0 && globaltimer() > deadline) {
-                report(P.status, ST_GROUP_TIMEOUT | 0x600000u);
-                break;
-            }
+    const int M = P.M, I = S.I, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // 1. this CTA's max |p| per token row, published as one tagged word each after its products are visible
+    if (threadIdx.x < SILU_MAX_M) s_gmax[threadIdx.x] = 0u;
+    if (warp >= 4) {   // epilogue warps 4, 5 hold tile rows 0..63 (the gate half)
+#pragma unroll
+        for (int m = 0; m < BN; ++m) {
+            if (m >= M) break;
+            float a = fin.lmax[m];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+            if (lane == 0) s_part[warp - 4][m] = a;
         }
-        __threadfence();
     }
     __syncthreads();
-    const int M = P.M, I = S.I;
+    const unsigned tag = s_tag;
     if (threadIdx.x < M) {
-        const float amax = __uint_as_float(__ldcg(&S.sync->amax[threadIdx.x]));
+        const float a = fmaxf(s_part[0][threadIdx.x], s_part[1][threadIdx.x]);
+        __threadfence();   // this CTA's products (stored before the barrier above) before its word
+        st_volatile8(&S.words[(size_t)blockIdx.x * M + threadIdx.x],
+                     ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(a));
+    }
+    // The other CTAs are done: their SMs go to the next kernel in the stream (the down projection's weight stream
+    // starts there while the slowest tiles of this one finish).
+    const int QC = (int)gridDim.x < SILU_QUANT_CTAS ? (int)gridDim.x : SILU_QUANT_CTAS;
+    if ((int)blockIdx.x >= QC) return;
+    // 2. every CTA's words: the grid's maxima (every tile is finished once all words carry this call's tag)
+    const uint64_t deadline = globaltimer() + P.timeout_ns;
+    const int nwords = (int)gridDim.x * M;
+    for (int w = threadIdx.x; w < nwords; w += blockDim.x) {
+        unsigned long long x = ld_volatile8(&S.words[w]);
+        uint32_t it = 0;
+        while ((unsigned)(x >> 32) != tag) {
+            if ((++it & 63u) == 0 && globaltimer() > deadline) {
+                report(P.status, ST_GROUP_TIMEOUT | 0x600000u | (unsigned)w);
+                break;
+            }
+            x = ld_volatile8(&S.words[w]);
+        }
+        atomicMax(&s_gmax[w % M], (unsigned)(x & 0xffffffffu));   // |p| bits: order-independent
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x < M) {
+        const float amax = __uint_as_float(s_gmax[threadIdx.x]);
         s_inv[threadIdx.x] = quant_inv(amax);
         if (blockIdx.x == 0) S.scales[threadIdx.x] = __fdiv_rn(amax, 127.0f);
     }
+    if (blockIdx.x == 0 && threadIdx.x == 0) S.sync->epoch = tag;   // every CTA has read the old epoch
     __syncthreads();
-    // this CTA's share of the [M, I] products, 8 at a time (I % 64 == 0: a group never crosses a row)
+    // 3. an even share of the [M, I] products per quantising CTA, 8 at a time (I % 64 == 0: never across a row)
     const int groups = M * (I >> 3);
-    const int g0 = (int)((long long)groups * blockIdx.x / gridDim.x);
-    const int g1 = (int)((long long)groups * (blockIdx.x + 1) / gridDim.x);
-    uint4 *pv = reinterpret_cast<uint4 *>(S.p);
+    const int g0 = (int)((long long)groups * blockIdx.x / QC);
+    const int g1 = (int)((long long)groups * (blockIdx.x + 1) / QC);
+    const uint4 *pv = reinterpret_cast<const uint4 *>(S.p);
     uint2 *qv = reinterpret_cast<uint2 *>(S.q);
     for (int gi = g0 + threadIdx.x; gi < g1; gi += blockDim.x) {
         const float inv = s_inv[gi / (I >> 3)];
@@ -141,15 +179,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             b[e >> 1] |= two << (16 * (e & 1));
         }
         qv[gi] = make_uint2(b[0], b[1]);
-        pv[gi] = make_uint4(0u, 0u, 0u, 0u);   // the scratch is zero again
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {   // every CTA read the maxima before it left: the last one out resets them
-        if (atomicAdd(&S.sync->leave, 1u) == gridDim.x - 1) {
-            for (int m = 0; m < SILU_MAX_M; ++m) S.sync->amax[m] = 0u;
-            S.sync->arrive = 0u;
-            S.sync->leave = 0u;
-        }
     }
 }
 
@@ -157,10 +186,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
 namespace vt {
 
-// [status 256][slots][sync 256][p]
+// [status 256][slots][sync 256][max words: SMs x M x 8][p: M x I x 2]
 inline size_t silu_slots_bytes(int M) { return tc_decode_slot_bytes(M, num_sms(cur_device())); }
+inline size_t silu_words_bytes(int M) { return ((size_t)num_sms(cur_device()) * M * 8 + 255) & ~(size_t)255; }
 inline size_t silu_ws_bytes(int M, int I) {
-    return 256 + ((silu_slots_bytes(M) + 255) & ~(size_t)255) + 256 + (((size_t)M * I * 2 + 255) & ~(size_t)255);
+    return 256 + ((silu_slots_bytes(M) + 255) & ~(size_t)255) + 256 + silu_words_bytes(M) +
+           (((size_t)M * I * 2 + 255) & ~(size_t)255);
 }
 
 template <typename T, int BN, int KBS>
@@ -213,7 +244,8 @@ static int gate_up_silu(const void *a, const void *w, const float *sa, const flo
     P.timeout_ns = pipe_timeout_ns();
     SiluArgs<T> S;
     S.sync = (SiluSync *)(ws + 256 + ((silu_slots_bytes(M) + 255) & ~(size_t)255));
-    S.p = (T *)((char *)S.sync + 256);
+    S.words = (unsigned long long *)((char *)S.sync + 256);
+    S.p = (T *)((char *)S.words + silu_words_bytes(M));
     S.q = (int8_t *)q;
     S.scales = (float *)scales;
     S.I = I;
@@ -227,7 +259,7 @@ using namespace vt;
 
 extern "C" {
 
-// Bytes of zeroed workspace vt_gate_up_silu_quant needs (256-byte status header included; the kernel leaves it zero).
+// Bytes of workspace vt_gate_up_silu_quant needs (256-byte status header included); zero it once before first use.
 size_t vt_gate_up_silu_quant_ws_bytes(int M, int I) { return silu_ws_bytes(M, I); }
 
 // q [M, I] int8, scales [M] float32 = per-token int8 quantisation of SiLU(gate) * up, where [gate | up] = the W8A8
@@ -235,7 +267,8 @@ size_t vt_gate_up_silu_quant_ws_bytes(int M, int I) { return silu_ws_bytes(M, I)
 // gate rows 64t..64t+63, then up rows 64t..64t+63), sw [2I] float32 in the same order, sa [M] (sa_rows = 1) or [1]
 // float32. Bit-identical to scaled_mm_ with the plain weight followed by silu_mul_quant. 1 <= M <= 32, I % 64 == 0,
 // K % 16 == 0, 16-byte aligned a / w / workspace, q 8-byte aligned. dtype (0 fp16 / 1 bf16) is the dtype of the
-// intermediate gate / up / product values. Calls sharing a workspace must be stream-ordered.
+// intermediate gate / up / product values. The workspace is zeroed once before first use; calls sharing it must be
+// stream-ordered.
 int vt_gate_up_silu_quant(const void *a, const void *w, const void *sa, const void *sw, void *q, void *scales, int M,
                           int I, int K, int sa_rows, int dtype, void *workspace, size_t ws_bytes, void *stream) {
     if (!a || !w || !sa || !sw || !q || !scales || !workspace || M < 1 || M > SILU_MAX_M || I < 64 || (I & 63) ||

@@ -295,10 +295,11 @@ __device__ __forceinline__ void tc_prefill_epilogue(const TcArgs &P, int m, int 
 }
 
 // The GEMM phase: every thread of the CTA (TC_THREADS) calls it; it returns after the CTA's pieces are done and its
-// TMEM is freed (a __syncthreads is the last thing it does, so the caller may reuse the shared memory).
+// TMEM is freed (a __syncthreads is the last thing it does, so the caller may reuse the shared memory). `fin` is the
+// calling thread's own finisher object: state it keeps (in the epilogue threads) is there after the phase.
 template <typename T, int BN, bool SWAP, int KBS, class Fin>
 __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtensorMap *tmap_b, const TcArgs &P,
-                                         unsigned char *smem_raw, Fin fin) {
+                                         unsigned char *smem_raw, Fin &fin) {
     using Lay = TcLayout<BN, KBS>;
     static_assert(!SWAP || BN <= 32, "decode orientation holds at most 32 token rows");
     unsigned char *tiles = tc_align1024(smem_raw);

@@ -29,7 +29,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                    TcArgs P) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    tc_phase<T, BN, SWAP, KBS>(&tmap_a, &tmap_b, P, smem_raw, TcOutEpi<T, BN>{});
+    TcOutEpi<T, BN> fin{};
+    tc_phase<T, BN, SWAP, KBS>(&tmap_a, &tmap_b, P, smem_raw, fin);
 }
 
 template <typename T, int BN, bool SWAP, int KBS>
