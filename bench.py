@@ -56,6 +56,8 @@ def parse():
                          "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant); "
                          "allreduce: config 4's size sweep, 1 KB .. 256 MB, against NCCL on the same ranks")
     ap.add_argument("--proj", default="down", choices=["down", "o_proj"], help="prefill: K = 17408 or 6144 (per TP)")
+    ap.add_argument("--blocked", action="store_true",
+                    help="decode gate_up on the tile-blocked weight layout (w8a8.block_weight / mma_blocked)")
     ap.add_argument("--mlp", default="unfused", choices=["fused", "unfused"],
                     help="decode: gate_up then SiLU*up + quant as the reference's two ops (scaled_mm_, silu_mul_quant; "
                          "default) or as one kernel (w8a8.gate_up_silu_quant; measured ~1 us per layer slower)")
@@ -567,11 +569,11 @@ def main():
         dn = make_layer_inputs(M, HIDDEN, K_dn, seed=i, rank=rank)
         gw, gsw = gu.w.to(dev), gu.sw.to(dev).view(-1, 1)
         gwi, gsi = w8a8.interleave_gate_up(gw, gsw)   # once, at load time
-        base.append(dict(gu_w=gw, gu_sw=gsw, gu_wi=gwi, gu_si=gsi,
+        base.append(dict(gu_w=gw, gu_sw=gsw, gu_wi=gwi, gu_si=gsi, gu_wb=w8a8.block_weight(gw),
                          dn_w=dn.w.to(dev), dn_sw=dn.sw.to(dev).view(-1, 1)))
         if i == 0:
             residual0, norm_w = dn.residual.to(dev), dn.norm_w.to(dev)
-    keep = ("gu_wi", "gu_si") if args.mlp == "fused" else ("gu_w", "gu_sw")
+    keep = ("gu_wi", "gu_si") if args.mlp == "fused" else (("gu_wb", "gu_sw") if args.blocked else ("gu_w", "gu_sw"))
     layers = [{k: v.clone() for k, v in base[i % len(base)].items() if k in keep or k.startswith("dn_")}
               for i in range(NL)]
     del base
@@ -591,7 +593,10 @@ def main():
     # silu_mul_quant, and the fused row-parallel tail (down GEMM + all-reduce + residual + RMSNorm + int8 quant, whose
     # output is the next layer's input)
     def gate_up(s):
-        torch.ops.vllm_turing.scaled_mm_(out_gu, x_q, s["gu_w"].t(), x_s, s["gu_sw"], None)
+        if args.blocked:
+            w8a8.mma_blocked(out_gu, x_q, s["gu_wb"], x_s, s["gu_sw"])
+        else:
+            torch.ops.vllm_turing.scaled_mm_(out_gu, x_q, s["gu_w"].t(), x_s, s["gu_sw"], None)
 
     def silu(s):
         silu_mul_quant(out_gu, h_q, h_s)

@@ -60,6 +60,14 @@ size_t w8a8_mma_ws_bytes(int M, int N);
 int w8a8_mma_ws(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out, int M,
                 int N, int K, int sa_rows, int sw_rows, int dtype, void *workspace, size_t ws_bytes, void *stream);
 
+/* w8a8_mma_ws with the weight in the tile-blocked layout [N / 128][K / 128][128][128] int8 (each 128 x 128 block of
+ * the row-major weight contiguous, a tile's blocks in K order; made once at load time): every TMA box the decode
+ * stream reads is one contiguous 16 KB block. N % 128 == 0, K % 128 == 0. Same results as w8a8_mma_ws. No
+ * counterpart in the reference (its GEMV reads the row-major weight). */
+int w8a8_mma_blocked_ws(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out,
+                        int M, int N, int K, int sa_rows, int sw_rows, int dtype, void *workspace, size_t ws_bytes,
+                        void *stream);
+
 /* Prefill GEMM (tcgen05 kind::i8, 128 x 256 tiles): A [M, K], W [N, K] int8, sa [M], sw [N] float32, out [M, N],
  * dequant order sa[m] * (sw[n] * acc). Returns 0 ok, 1 cannot implement (shape / alignment), 3 launch failed.
  * Replaces vllm_turing/csrc/w8a8_big.cu:66-73 (w8a8_big: same signature and return convention). */

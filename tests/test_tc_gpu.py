@@ -133,3 +133,21 @@ def test_back_to_back_small_and_big():
     refs = [O.gemm_s32(a.cpu().numpy(), w.cpu().numpy()) for a, w in ins]
     for i, o in enumerate(outs):
         assert np.array_equal(o.cpu().numpy(), refs[i % len(cases)]), f"launch {i}"
+
+
+@pytest.mark.parametrize("M,N,K", [(5, 34816, 5120), (16, 5120, 17408), (1, 128, 128), (32, 1024, 2176),
+                                   (9, 4352, 5120)])
+def test_mma_blocked_weight_layout(M, N, K):
+    """the decode GEMM on the tile-blocked weight layout (w8a8.block_weight): the same bits as on the row-major
+    weight, and as the oracle"""
+    from vllm_turing_b200 import w8a8
+    a, w = rand_int8((M, K), M + 31), rand_int8((N, K), N + 37)
+    sa, sw = rand_scales(M, 5, 1e-2), rand_scales(N, 6, 1e-3)
+    ac, wc, sac, swc = a.cuda(), w.cuda(), sa.cuda().view(-1, 1), sw.cuda().view(-1, 1)
+    out_b = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+    out_r = torch.empty_like(out_b)
+    w8a8.mma_blocked(out_b, ac, w8a8.block_weight(wc), sac, swc)
+    w8a8.mma(out_r, ac, wc.t(), sac, swc, None)
+    torch.cuda.synchronize()
+    assert torch.equal(out_b, out_r)
+    assert_bits_equal(out_b, O.scaled_mm(a.numpy(), w.numpy(), sa.numpy(), sw.numpy(), None, 1), f"blocked M={M}")

@@ -112,6 +112,7 @@ SIGNATURES = {
     "w8a8_mma": (_I, [_P] * 6 + [_I] * 6 + [_P]),
     "w8a8_mma_ws_bytes": (_SZ, [_I, _I]),
     "w8a8_mma_ws": (_I, [_P] * 6 + [_I] * 6 + [_P, _SZ, _P]),
+    "w8a8_mma_blocked_ws": (_I, [_P] * 6 + [_I] * 6 + [_P, _SZ, _P]),
     "w8a8_big": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "vt_gemm_s32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_gate_up_silu_quant_ws_bytes": (_SZ, [_I, _I]),

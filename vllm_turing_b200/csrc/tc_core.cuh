@@ -125,6 +125,7 @@ struct TcArgs {
     int units;                  // prefill: tiles (n_tiles_a * n_tiles_b); decode: K blocks of all tiles (n_tiles_a * nkb)
     int stream_k;               // 1: decode stream-K ranges; 0: whole tiles round robin
     int group_m;                // prefill raster: A tiles per group (each group covers all B tiles)
+    int blocked_a;              // decode: A (the weight) in the tile-blocked layout (tc_a_coords)
     int l2_prefetch_blocks;     // decode: weight K blocks past the ring prefetched into L2 before pdl_wait
     const float *sa, *sw;       // per token, per output feature (NULL in int32 mode)
     const void *bias;           // [N] output dtype or NULL
@@ -185,6 +186,19 @@ struct TcPieces {
         return true;
     }
 };
+
+// Box coordinates of K block kb of A tile ta: the plain row-major [rows, K] operand (x = bytes of K, y = rows), or
+// the tile-blocked weight layout [tile][K block][128 rows][128 B] seen as rows of 128 bytes, where each box is one
+// contiguous 16 KB block and a CTA's K range of a tile one contiguous stream.
+__device__ __forceinline__ void tc_a_coords(const TcArgs &P, int ta, int kb, int &x, int &y) {
+    if (P.blocked_a) {
+        x = 0;
+        y = (ta * P.nkb + kb) * TC_BM;
+    } else {
+        x = kb * TC_BK;
+        y = ta * TC_BM;
+    }
+}
 
 // First K-block unit of CTA c in the stream-K partition (the formula TcPieces uses), and the CTA holding unit u.
 __device__ __forceinline__ int tc_range_lo(const TcArgs &P, int c) {
@@ -362,9 +376,11 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                         const int nb = min(KBS, kb1 - kb);
                         mbar_arrive_expect_tx(&full[pre], (uint32_t)(nb * Lay::KB_BYTES));
                         unsigned char *st = tiles + (size_t)pre * Lay::STAGE;
-                        for (int j = 0; j < nb; ++j)
-                            tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[pre],
-                                             pol);
+                        for (int j = 0; j < nb; ++j) {
+                            int ax, ay;
+                            tc_a_coords(P, ta, kb + j, ax, ay);
+                            tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, ax, ay, &full[pre], pol);
+                        }
                     }
                 }
                 // and the next l2_prefetch_blocks weight blocks of the range into L2, so the stream keeps going past
@@ -374,8 +390,11 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                 while (left > 0 && pq.next(P, ta, tb, kb0, kb1)) {
                     for (int kb = kb0; kb < kb1 && left > 0; kb += KBS, ++stage) {
                         if (stage < pre) continue;
-                        for (int j = 0; j < min(KBS, kb1 - kb) && left > 0; ++j, --left)
-                            tma_prefetch_l2_2d(tmap_a, (kb + j) * TC_BK, ta * TC_BM);
+                        for (int j = 0; j < min(KBS, kb1 - kb) && left > 0; ++j, --left) {
+                            int ax, ay;
+                            tc_a_coords(P, ta, kb + j, ax, ay);
+                            tma_prefetch_l2_2d(tmap_a, ax, ay);
+                        }
                     }
                 }
             }
@@ -400,11 +419,12 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                         }
                         mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * Lay::KB_BYTES));
                         for (int j = 0; j < nb; ++j) {
+                            int ax, ay;
+                            tc_a_coords(P, ta, kb + j, ax, ay);
                             if (SWAP)
-                                tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s],
-                                                 pol);
+                                tma_load_2d_hint(st + j * Lay::A_BYTES, tmap_a, ax, ay, &full[s], pol);
                             else
-                                tma_load_2d(st + j * Lay::A_BYTES, tmap_a, (kb + j) * TC_BK, ta * TC_BM, &full[s]);
+                                tma_load_2d(st + j * Lay::A_BYTES, tmap_a, ax, ay, &full[s]);
                         }
                     }
                     for (int j = 0; j < nb; ++j)

@@ -93,12 +93,19 @@ static int small_kbs(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs 
 template <typename T>
 static int small_gemm(const void *a, const void *w, const float *sa, const float *sw, const void *bias, void *out,
                       int M, int N, int K, int sa_rows, int sw_rows, int s32, void *scratch, unsigned *status,
-                      cudaStream_t s) {
+                      cudaStream_t s, bool blocked = false) {
     const int BN = M <= 16 ? 16 : 32;
     CUtensorMap ma, mb;
-    if (!tc_make_map(&ma, w, N, K, TC_BM) || !tc_make_map(&mb, a, M, K, BN)) return VT_EARG;
+    if (blocked) {   // [N / 128][K / 128][128][128]: rows of 128 bytes, one 16 KB box per block
+        if ((N % TC_BM) || (K % TC_BK) || !tc_make_map(&ma, w, (N / TC_BM) * (K / TC_BK) * TC_BM, TC_BK, TC_BM))
+            return VT_EARG;
+    } else if (!tc_make_map(&ma, w, N, K, TC_BM)) {
+        return VT_EARG;
+    }
+    if (!tc_make_map(&mb, a, M, K, BN)) return VT_EARG;
     TcArgs P{};
     tc_decode_args(P, M, N, K);
+    P.blocked_a = blocked ? 1 : 0;
     P.sa = sa;
     P.sw = sw;
     P.bias = bias;
@@ -123,9 +130,9 @@ static bool tc_args_ok(const void *a, const void *w, int M, int N, int K) {
 template <typename T>
 static int mma_dequant(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out,
                        int M, int N, int K, int sa_rows, int sw_rows, void *scratch, unsigned *status,
-                       cudaStream_t s) {
+                       cudaStream_t s, bool blocked = false) {
     return small_gemm<T>(a, w, (const float *)sa, (const float *)sw, bias, out, M, N, K, sa_rows, sw_rows, 0, scratch,
-                         status, s);
+                         status, s, blocked);
 }
 
 }  // namespace vt
@@ -165,6 +172,23 @@ int w8a8_mma_ws(const void *a, const void *w, const void *sa, const void *sw, co
     if (dtype == 0)
         return mma_dequant<__half>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, scratch, status, s);
     return mma_dequant<__nv_bfloat16>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, scratch, status, s);
+}
+
+// w8a8_mma_ws with the weight in the tile-blocked layout [N / 128][K / 128][128][128] (int8; every 128 x 128 block of
+// the row-major weight stored contiguously, blocks of a 128-row tile in K order): each TMA box of the stream is one
+// contiguous 16 KB block. N % 128 == 0, K % 128 == 0. Same results as w8a8_mma_ws on the row-major weight.
+int w8a8_mma_blocked_ws(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out,
+                        int M, int N, int K, int sa_rows, int sw_rows, int dtype, void *workspace, size_t ws_bytes,
+                        void *stream) {
+    if (!tc_args_ok(a, w, M, N, K) || M > 32 || (N % 128) || (K % 128) || !workspace ||
+        ws_bytes < w8a8_mma_ws_bytes(M, N) || ((uintptr_t)workspace & 255))
+        return VT_EARG;
+    cudaStream_t s = (cudaStream_t)stream;
+    unsigned *status = (unsigned *)workspace;
+    void *scratch = (char *)workspace + 256;
+    if (dtype == 0)
+        return mma_dequant<__half>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, scratch, status, s, true);
+    return mma_dequant<__nv_bfloat16>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, scratch, status, s, true);
 }
 
 // The reference's prefill entry (vllm_turing/csrc/w8a8_big.cu:66-73: A [M, K], W [N, K] int8, sa [M], sw [N]

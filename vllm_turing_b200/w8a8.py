@@ -147,6 +147,28 @@ def mma(out, a, b, sa, sb, bias):
         raise RuntimeError(f"w8a8_mma launch failed: {rc}")
 
 
+def block_weight(w):
+    """The row-major weight [N, K] int8 in the tile-blocked layout mma_blocked reads: [N/128, K/128, 128, 128], each
+    128 x 128 block contiguous and a 128-row tile's blocks in K order (made once, at load time)."""
+    N, K = w.shape
+    if N % 128 or K % 128:
+        raise ValueError("block_weight: N and K must be multiples of 128")
+    return w.reshape(N // 128, 128, K // 128, 128).permute(0, 2, 1, 3).contiguous()
+
+
+def mma_blocked(out, a, wb, sa, sb, bias=None):
+    """out[M, N] = (a . w^T) * sa * sb (+ bias) for the weight of block_weight(w) (the decode GEMM, M <= 32)."""
+    M, K = a.shape
+    N = wb.shape[0] * 128
+    ws = workspace(a.device, M, N)
+    rc = lib().w8a8_mma_blocked_ws(a.data_ptr(), wb.data_ptr(), sa.data_ptr(), sb.data_ptr(),
+                                   bias.data_ptr() if bias is not None else None, out.data_ptr(), M, N, K,
+                                   int(sa.numel() > 1), int(sb.numel() > 1), _dtype_code(out.dtype), ws.data_ptr(),
+                                   ws.numel(), _stream())
+    if rc != 0:
+        raise RuntimeError(f"w8a8_mma_blocked failed: {rc}")
+
+
 def big_ok(out, a, b, sa, sb, bias):
     """The prefill kernel's requirements (vllm_turing/w8a8.py:185-193, same checks)."""
     M, K = a.shape
