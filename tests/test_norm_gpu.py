@@ -88,11 +88,13 @@ def test_silu_mul_quant_reference_abi():
         assert s[0].item() == 0.0 and not q[0].any().item()
 
 
-@pytest.mark.parametrize("M,I", [(1, 17408), (5, 17408), (5, 2176), (24, 8704), (64, 136), (100, 4352)])
+@pytest.mark.parametrize("M,I", [(1, 17408), (5, 17408), (5, 2176), (24, 8704), (64, 136), (100, 4352), (5, 4352),
+                                 (3, 4100)])
 def test_silu_mul_quant_bf16_row_split(M, I):
-    """bf16 SiLU-mul-quant at decode shapes (rows split over several CTAs, the row absmax combined across them) and
-    at 100 rows (a CTA per row); ten back-to-back calls with different inputs and no host sync in between check that
-    the per-row slots and counters are left reset for the next call."""
+    """bf16 SiLU-mul-quant at decode shapes -- rows split over 4..17 CTAs (the row absmax combined through epoch-tagged
+    words; 4100 takes the scalar loads, the others the 8-element vectors) or one CTA per row (2176, and 100 rows) --
+    ten back-to-back calls with different inputs and no host sync in between: a call never takes an earlier call's
+    words for its own."""
     from vllm_turing_b200 import _build
     L = _build.load()
     ins, outs = [], []

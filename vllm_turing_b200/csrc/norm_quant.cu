@@ -197,55 +197,42 @@ __global__ void __launch_bounds__(256)
     }
 }
 
-// SiLU(g) rounded to the 16-bit type, times u rounded (vllm_turing/csrc/silu_quant.cu:11-14, 39), then quant.
+// SiLU(g) * u of elements [i0, i1) of one row into pbuf[0 ..), returning this thread's max |p|; same rounding points
+// as below. When the range and rows are 16-byte aligned: 8-element vector loads, a thread's (up to 4) vectors of gate
+// and up issued before any arithmetic -- the loop is latency-bound otherwise, one memory round trip per element.
 template <typename T>
-__global__ void __launch_bounds__(RQ_THREADS) silu_mul_quant_kernel(const T *__restrict__ gu, int8_t *__restrict__ q,
-                                                                    float *__restrict__ scales, int I) {
-    extern __shared__ float abuf[];
-    __shared__ float red[32];
-    const long long row = blockIdx.x;
-    const T *g = gu + row * 2 * I;
-    const T *u = g + I;
+__device__ __forceinline__ float silu_range(const T *gr, const T *ur, int i0, int i1, float *pbuf) {
     float amax = 0.0f;
-    for (int i = threadIdx.x; i < I; i += blockDim.x) {
-        const float gf = t2f<T>(g[i]);
-        const float sg = rnd<T>(__fdiv_rn(gf, 1.0f + expf(-gf)));
-        const float p = rnd<T>(__fmul_rn(sg, t2f<T>(u[i])));
-        abuf[i] = p;
-        amax = fmaxf(amax, fabsf(p));
+    if (((i0 | i1) & 7) == 0 && !((uintptr_t)gr & 15) && !((uintptr_t)ur & 15)) {
+        const int nv = (i1 - i0) >> 3, nt = blockDim.x;
+        const uint4 *gv = reinterpret_cast<const uint4 *>(gr + i0), *uv = reinterpret_cast<const uint4 *>(ur + i0);
+        for (int b = threadIdx.x; b < nv; b += 4 * nt) {
+            uint4 gq[4], uq[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (b + k * nt < nv) {
+                    gq[k] = gv[b + k * nt];
+                    uq[k] = uv[b + k * nt];
+                }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int v = b + k * nt;
+                if (v >= nv) continue;
+                const uint32_t gw[4] = {gq[k].x, gq[k].y, gq[k].z, gq[k].w};
+                const uint32_t uw[4] = {uq[k].x, uq[k].y, uq[k].z, uq[k].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 gf = unpack2<T>(gw[e]), uf = unpack2<T>(uw[e]);
+                    const float p0 = rnd<T>(__fmul_rn(rnd<T>(__fdiv_rn(gf.x, 1.0f + expf(-gf.x))), uf.x));
+                    const float p1 = rnd<T>(__fmul_rn(rnd<T>(__fdiv_rn(gf.y, 1.0f + expf(-gf.y))), uf.y));
+                    pbuf[8 * v + 2 * e] = p0;
+                    pbuf[8 * v + 2 * e + 1] = p1;
+                    amax = fmaxf(amax, fmaxf(fabsf(p0), fabsf(p1)));
+                }
+            }
+        }
+        return amax;
     }
-    amax = block_max(amax, red);
-    const float inv = quant_inv(amax);
-    if (threadIdx.x == 0) scales[row] = __fdiv_rn(amax, 127.0f);
-    for (int i = threadIdx.x; i < I; i += blockDim.x) q[row * I + i] = quant1(abuf[i], inv);
-}
-
-// Row-split variant for few rows: CTA (m, g) of an M x E grid computes the SiLU products of the g-th 1/E slice of
-// row m, then the row's absmax is combined across its E CTAs through a per-row slot in device memory (atomicMax of
-// the float's bits: the values are non-negative, so the order of arrival does not matter and the result is
-// deterministic) and an arrival counter; each CTA then quantises its own slice. The last CTA of a row to leave resets
-// the row's slot and counters, so the next (stream-ordered) call starts from zero. Calls that overlap on the GPU
-// would share the slots: they must be stream-ordered (as every decode step is). The wait for the row's other CTAs
-// is bounded; a timeout lands in the library status word. Launched with programmatic dependent launch (it waits for
-// the kernel that wrote gate_up before reading it).
-constexpr int SQ_THREADS = 256;
-constexpr int SQ_ROWS = 64;   // rows the split path serves
-static __device__ unsigned g_sq_amax[SQ_ROWS], g_sq_arrive[SQ_ROWS], g_sq_leave[SQ_ROWS];
-
-template <typename T>
-__global__ void __launch_bounds__(SQ_THREADS)
-    silu_mul_quant_split_kernel(const T *__restrict__ gu, int8_t *__restrict__ q, float *__restrict__ scales, int I,
-                                int E, uint64_t timeout_ns, unsigned *status) {
-    extern __shared__ float pbuf[];
-    __shared__ float red[32];
-    __shared__ float s_amax;
-    pdl_launch_dependents();
-    pdl_wait();   // gate_up comes from the previous kernel
-    const int m = blockIdx.x / E, g = blockIdx.x - m * E;
-    const int i0 = (int)((long long)I * g / E), i1 = (int)((long long)I * (g + 1) / E);
-    const T *gr = gu + (size_t)m * 2 * I;
-    const T *ur = gr + I;
-    float amax = 0.0f;
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
         const float gf = t2f<T>(gr[i]);
         const float sg = rnd<T>(__fdiv_rn(gf, 1.0f + expf(-gf)));
@@ -253,30 +240,87 @@ __global__ void __launch_bounds__(SQ_THREADS)
         pbuf[i - i0] = p;
         amax = fmaxf(amax, fabsf(p));
     }
+    return amax;
+}
+
+// SiLU(g) rounded to the 16-bit type, times u rounded (vllm_turing/csrc/silu_quant.cu:11-14, 39), then quant.
+template <typename T>
+__global__ void __launch_bounds__(RQ_THREADS) silu_mul_quant_kernel(const T *__restrict__ gu, int8_t *__restrict__ q,
+                                                                    float *__restrict__ scales, int I) {
+    extern __shared__ float abuf[];
+    __shared__ float red[32];
+    pdl_launch_dependents();
+    pdl_wait();   // gate_up comes from the previous kernel
+    const long long row = blockIdx.x;
+    const T *g = gu + row * 2 * I;
+    const T *u = g + I;
+    float amax = silu_range<T>(g, u, 0, I, abuf);
     amax = block_max(amax, red);
+    const float inv = quant_inv(amax);
+    if (threadIdx.x == 0) scales[row] = __fdiv_rn(amax, 127.0f);
+    for (int i = threadIdx.x; i < I; i += blockDim.x) q[row * I + i] = quant1(abuf[i], inv);
+}
+
+// Row-split variant for few rows: CTA (m, g) of an M x E grid computes the SiLU products of the g-th 1/E slice of
+// row m; the row's absmax is combined across its E CTAs through one 8-byte word per CTA, {max |p| bits, tag}, tagged
+// with the row's epoch + 1 (value and tag in one store: no atomics, no fence). Every CTA of the row polls the row's E
+// words in parallel (one round trip once they are all in), takes the maximum (order-independent: deterministic) and
+// quantises its own slice; CTA (m, 0) advances the row's epoch after it has seen all E words -- every CTA of the row
+// has read the old epoch by then -- so an earlier call's words are never taken for this call's. Calls that overlap on
+// the GPU would share the words: they must be stream-ordered (as every decode step is). The wait is bounded; a
+// timeout lands in the library status word. Launched with programmatic dependent launch (it waits for the kernel
+// that wrote gate_up before reading it).
+constexpr int SQ_THREADS = 256;
+constexpr int SQ_ROWS = 64;      // rows the split path serves
+constexpr int SQ_MAX_E = 64;     // CTAs per row
+static __device__ unsigned g_sq_epoch[SQ_ROWS];
+static __device__ unsigned long long g_sq_word[SQ_ROWS][SQ_MAX_E];
+
+template <typename T>
+__global__ void __launch_bounds__(SQ_THREADS)
+    silu_mul_quant_split_kernel(const T *__restrict__ gu, int8_t *__restrict__ q, float *__restrict__ scales, int I,
+                                int E, uint64_t timeout_ns, unsigned *status) {
+    extern __shared__ float pbuf[];
+    __shared__ float red[32];
+    __shared__ unsigned s_tag, s_max;
+    pdl_launch_dependents();
+    pdl_wait();   // gate_up comes from the previous kernel
+    const int m = blockIdx.x / E, g = blockIdx.x - m * E;
     if (threadIdx.x == 0) {
-        atomicMax(&g_sq_amax[m], __float_as_uint(amax));
-        __threadfence();
-        atomicAdd(&g_sq_arrive[m], 1u);
-        const uint64_t deadline = globaltimer() + timeout_ns;
+        s_tag = *reinterpret_cast<volatile unsigned *>(&g_sq_epoch[m]) + 1u;
+        s_max = 0u;
+    }
+    int i0, i1;
+    if ((I & 7) == 0) {   // slices in whole 8-element vectors
+        i0 = (int)((long long)(I >> 3) * g / E) * 8;
+        i1 = (int)((long long)(I >> 3) * (g + 1) / E) * 8;
+    } else {
+        i0 = (int)((long long)I * g / E);
+        i1 = (int)((long long)I * (g + 1) / E);
+    }
+    const T *gr = gu + (size_t)m * 2 * I;
+    const T *ur = gr + I;
+    float amax = silu_range<T>(gr, ur, i0, i1, pbuf);
+    amax = block_max(amax, red);   // (its barriers also publish s_tag)
+    const unsigned tag = s_tag;
+    if (threadIdx.x == 0)
+        st_volatile8(&g_sq_word[m][g], ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(amax));
+    const uint64_t deadline = globaltimer() + timeout_ns;
+    for (int k = threadIdx.x; k < E; k += blockDim.x) {
+        unsigned long long x = ld_volatile8(&g_sq_word[m][k]);
         uint32_t it = 0;
-        while (atomicAdd(&g_sq_arrive[m], 0u) < (unsigned)E) {
+        while ((unsigned)(x >> 32) != tag) {
             if ((++it & 63u) == 0 && globaltimer() > deadline) {
                 report(status, ST_GROUP_TIMEOUT | 0x800000u | (unsigned)m);
                 break;
             }
+            x = ld_volatile8(&g_sq_word[m][k]);
         }
-        __threadfence();
-        s_amax = __uint_as_float(atomicAdd(&g_sq_amax[m], 0u));
-        if (atomicAdd(&g_sq_leave[m], 1u) == (unsigned)E - 1u) {   // every CTA of the row has read the slot
-            g_sq_amax[m] = 0u;
-            g_sq_arrive[m] = 0u;
-            g_sq_leave[m] = 0u;
-            __threadfence();
-        }
+        atomicMax(&s_max, (unsigned)(x & 0xffffffffu));   // shared memory; |p| bits: order-independent
     }
     __syncthreads();
-    amax = s_amax;
+    amax = __uint_as_float(s_max);
+    if (g == 0 && threadIdx.x == 0) g_sq_epoch[m] = tag;   // every CTA of the row has read the old epoch
     const float inv = quant_inv(amax);
     if (g == 0 && threadIdx.x == 0) scales[m] = __fdiv_rn(amax, 127.0f);
     int8_t *qr = q + (size_t)m * I;
@@ -287,6 +331,12 @@ static int smem_attr(const void *fn, int bytes) {
     if (bytes <= 48 * 1024) return 0;
     return (int)cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
+
+}  // namespace vt
+
+using namespace vt;
+
+namespace vt {
 
 template <typename T>
 static int launch_norm_vec(int vpt, int t, const void *x, void *residual, const void *weight, float eps, void *q,
@@ -309,19 +359,29 @@ static int launch_norm_vec(int vpt, int t, const void *x, void *residual, const 
     return (int)cudaGetLastError();
 }
 
-// Few rows: the row-split kernel on up to one CTA per SM (at least 256 elements per CTA); many rows: a CTA per row.
+// Few rows: the row-split kernel (about 2048 products per CTA, at most one CTA per SM); else a CTA per row.
 template <typename T>
 static int launch_silu(const void *gu, void *q, void *scales, int M, int I, cudaStream_t s) {
     const int dev = cur_device();
     const int sms = num_sms(dev);
+    // About 1024 products per CTA, and no split into fewer than 4 (then one CTA per row: no cross-CTA step at all).
+    // Measured (M = 5, graph replay, us per call; I = 17408 / 8704 / 4352 / 2176): 1024 per CTA 4.24 / 3.73 / 3.38 /
+    // (E = 2) 3.30; 2048 per CTA 4.40 / 4.09 / (E = 2) 4.04 / 2.42; one CTA per row 7.48 / 4.61 / 3.33 / 2.47.
+    static int per_cta = -1;   // VLLM_TURING_SILU_SPLIT: products per CTA of the row split
+    if (per_cta < 0) {
+        const char *e = getenv("VLLM_TURING_SILU_SPLIT");
+        per_cta = e && atoi(e) > 0 ? atoi(e) : 1024;
+    }
     int E = sms / M;
-    const int E_max = (I + 255) / 256;
-    if (E > E_max) E = E_max;
+    int E_want = I / per_cta;
+    if (E_want < 4) E_want = 1;
+    if (E > E_want) E = E_want;
+    if (E > SQ_MAX_E) E = SQ_MAX_E;
     if (M <= SQ_ROWS && E >= 2) {
-        const int chunk = (I + E - 1) / E;
+        const int chunk = ((I + 7) / 8 + E - 1) / E * 8 + 8;   // the largest slice, vector-aligned slices included
         static bool attr[VT_MAX_DEV] = {false};
         if (dev >= 0 && dev < VT_MAX_DEV && !attr[dev]) {
-            if (int rc = smem_attr((const void *)silu_mul_quant_split_kernel<T>, 49152 * 2)) return rc;
+            if (int rc = smem_attr((const void *)silu_mul_quant_split_kernel<T>, 100 * 1024)) return rc;
             attr[dev] = true;
         }
         void *scratch = nullptr;
@@ -331,8 +391,8 @@ static int launch_silu(const void *gu, void *q, void *scales, int M, int I, cuda
                         (const T *)gu, (int8_t *)q, (float *)scales, I, E, pipe_timeout_ns(), status);
     }
     if (int rc = smem_attr((const void *)silu_mul_quant_kernel<T>, I * 4)) return rc;
-    silu_mul_quant_kernel<T><<<M, RQ_THREADS, I * 4, s>>>((const T *)gu, (int8_t *)q, (float *)scales, I);
-    return (int)cudaGetLastError();
+    return launch_k(silu_mul_quant_kernel<T>, dim3(M), dim3(RQ_THREADS), (size_t)I * 4, s, true, (const T *)gu,
+                    (int8_t *)q, (float *)scales, I);
 }
 
 }  // namespace vt
