@@ -1,8 +1,9 @@
 """B200 (sm_100a) tensor-parallel W8A8 linear for vLLM, loaded as a `vllm.general_plugins` entry point.
 
 The drop-in replacement for vllm-turing's hot path (vllm_turing/__init__.py:38-72 registers it there):
-  - w8a8: INT8 W8A8 GEMM behind vLLM's cutlass_scaled_mm -- a bulk-copy (TMA) streamed GEMV for decode rows and
-    tcgen05 kind::i8 tensor-core kernels with TMEM accumulators for larger M
+  - w8a8: INT8 W8A8 GEMM behind vLLM's cutlass_scaled_mm -- tcgen05 kind::i8 tensor-core kernels with TMEM
+    accumulators (a stream-K decode kernel for M <= 32, 128 x 256 tiles above); the TMA-streamed dp4a GEMV on request;
+    the fused gate/up + SiLU*up + quant kernel (gate_up_silu_quant)
   - hostar: the tensor-parallel all-reduce of CudaCommunicator replaced by P2P kernels over NVLink (one-shot LL for
     decode messages, two-shot reduce-scatter + all-gather for prefill)
   - quantfuse: per-token int8 activation quantisation (the formula inductor fuses into the producer)

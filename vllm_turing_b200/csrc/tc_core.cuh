@@ -11,12 +11,12 @@
 //            (tile, K block) index space is cut into one contiguous range per CTA, so every SM streams the same number
 //            of weight bytes (+-1 K block of 16 KB). A CTA's range falls into "pieces" (one tile, a K-block range).
 //            A piece that covers its whole tile is finished in registers. A split tile is finished by the CTA holding
-//            its first K blocks (the "head" piece, the last piece of that CTA's range): the other pieces add their
-//            int32 partial sums into a zeroed scratch [M, N] (atomicAdd: exact) and count their K blocks on the tile's
-//            ticket; the head CTA waits (bounded) for the count, adds the scratch to its own sums, returns scratch and
-//            ticket to zero and hands the accumulators to the caller's finisher `fin(P, n, n_ok, acc[BN])` (thread =
-//            output feature n, acc[m] for token rows m;
-//            fin.on_start() runs once in every epilogue thread before the first piece).
+//            its first K blocks (the "head" piece, the last piece of that CTA's range). Every other piece of it is
+//            the first piece of its CTA, whose int32 sums go into that CTA's slot of LL words ({sum, 1, sum, 1}:
+//            value and flag in each 8-byte half). The head CTA collects the slots (bounded waits) while its own MMAs
+//            run, clears them, adds them to its registers (integer sums: exact in any order) and hands the
+//            accumulators to the caller's finisher `fin(P, n, n_ok, acc[BN])` (thread = output feature n, acc[m]
+//            for token rows m; fin.on_start() runs once in every epilogue thread before the first piece).
 //
 // CTA = 6 warps: warp 0 issues TMA loads into a ring of shared-memory stages (KBS K blocks of 128 bytes per stage, so
 // one barrier round trip moves KBS x 16 KB of weights), warp 1 allocates TMEM and one of its threads issues the MMAs
