@@ -568,9 +568,12 @@ def main():
         gu = make_layer_inputs(M, N_gu, HIDDEN, seed=100 + i, rank=rank, with_norm=False)
         dn = make_layer_inputs(M, HIDDEN, K_dn, seed=i, rank=rank)
         gw, gsw = gu.w.to(dev), gu.sw.to(dev).view(-1, 1)
-        gwi, gsi = w8a8.interleave_gate_up(gw, gsw)   # once, at load time
-        base.append(dict(gu_w=gw, gu_sw=gsw, gu_wi=gwi, gu_si=gsi, gu_wb=w8a8.block_weight(gw),
-                         dn_w=dn.w.to(dev), dn_sw=dn.sw.to(dev).view(-1, 1)))
+        st = dict(gu_w=gw, gu_sw=gsw, dn_w=dn.w.to(dev), dn_sw=dn.sw.to(dev).view(-1, 1))
+        if args.mlp == "fused":   # weight layouts are made once, at load time
+            st["gu_wi"], st["gu_si"] = w8a8.interleave_gate_up(gw, gsw)
+        if args.blocked:
+            st["gu_wb"] = w8a8.block_weight(gw)
+        base.append(st)
         if i == 0:
             residual0, norm_w = dn.residual.to(dev), dn.norm_w.to(dev)
     keep = ("gu_wi", "gu_si") if args.mlp == "fused" else (("gu_wb", "gu_sw") if args.blocked else ("gu_w", "gu_sw"))
