@@ -89,6 +89,28 @@ size_t vt_gate_up_silu_quant_ws_bytes(int M, int I);
 int vt_gate_up_silu_quant(const void *a, const void *w, const void *sa, const void *sw, void *q, void *scales, int M,
                           int I, int K, int sa_rows, int dtype, void *workspace, size_t ws_bytes, void *stream);
 
+/* ---- LM head: W8A16 (int8 weight rows + fp32 row scales, 16-bit activations) ------------------------------------ */
+
+/* out [M, N] = x [M, K] . (w [N, K] int8 * s [N])^T + bias [N], fp32 sums, one rounding to dtype (0 fp16 / 1 bf16).
+ * tcgen05 kind::f16 with the weights converted to 16-bit in tensor memory, stream-K over the SMs. M 1..16, K % 16 == 0,
+ * x and w 16-byte aligned; -1 on bad arguments, else a cudaError. Replaces w8a16_gemv (w8a16_gemv.cu:114-123). */
+int w8a16_gemv(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K,
+               int dtype, void *stream);
+/* rows (int32 [N] indices into w, or NULL): the output covers those weight rows only (CUDA-core kernel; the caller
+ * guarantees the indices are in range). Replaces w8a16_gemv_rows (w8a16_gemv.cu:125-145). */
+int w8a16_gemv_rows(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K,
+                    int dtype, const void *rows, void *stream);
+/* fp16 activations, M 1..64, N even; cfg (the reference's tiling choice) is ignored. Same kernel as w8a16_gemv.
+ * Replaces w8a16_mma (w8a16_mma.cu:160-175). */
+int w8a16_mma(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int cfg,
+              void *stream);
+/* The same for M 1..64 in either dtype, output row stride ldo >= N (write one rank's columns of a [M, world * N]
+ * logits buffer), caller-owned workspace of vt_w8a16_ws_bytes(M) bytes (256-byte aligned, zeroed once; the kernel
+ * leaves it zeroed; calls sharing it must be stream-ordered). New entries. */
+size_t vt_w8a16_ws_bytes(int M);
+int vt_w8a16_mm(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int ldo,
+                int dtype, void *workspace, size_t ws_bytes, void *stream);
+
 /* Non-zero 32-bit words in the first `bytes` of the current device's library workspace scratch (kernels leave it
  * zeroed; a test hook). Synchronises the device; -1 on error. New entry. */
 long long vt_workspace_nonzero(long long bytes);
@@ -157,6 +179,11 @@ int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype,
 /* gathered [world * m bytes] with this rank's payload pre-written at [rank * m, (rank + 1) * m); fills the peers'
  * slots. m % 8 == 0 (LL) or m % 16 == 0 (bulk). Replaces dag_all_gather (dma_ag.cu:45-74) for N ranks over P2P. */
 int vt_all_gather(void *comm, void *gathered, long long m, void *stream);
+/* gathered [rows, ld_bytes]: world column blocks of row_bytes per row, this rank's block (offset rank * row_bytes)
+ * pre-written; fills the peers' blocks (vLLM's all_gather along the last dimension, e.g. vocabulary-parallel logits,
+ * with no transpose). row_bytes, ld_bytes % 8 == 0, rows * row_bytes within the one-shot LL capacity. New entry. */
+int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row_bytes, long long ld_bytes,
+                       void *stream);
 
 /* The fused row-parallel layer tail, one kernel: this rank's W8A8 GEMM partial (tcgen05; the dp4a GEMV for M <= 16
  * with VLLM_TURING_FUSED_GEMV=1) -> all-reduce over the communicator -> residual add (in place) -> RMSNorm * norm_w

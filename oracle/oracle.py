@@ -42,6 +42,8 @@ def lib():
             "orc_row_linear_tp": [_I, _P, _P, _P, _P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I],
             "orc_silu_mul_quant": [_P, _P, _P, _I, _I, _I],
             "orc_all_gather": [_P, _I, _P, _L],
+            "orc_lmhead_quant": [_P, _P, _P, _I, _I, _I],
+            "orc_w8a16": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I],
             "orc_set_threads": [_I],
             "orc_num_threads": [],
         }
@@ -204,3 +206,43 @@ def all_gather(payloads):
     arr = (ctypes.c_void_p * len(payloads))(*[p.ctypes.data for p in payloads])
     lib().orc_all_gather(arr, len(payloads), _p(out), m)
     return out
+
+
+def lmhead_quant(w, device="cpu"):
+    """(int8 [N, K], float32 [N]) per-row quantisation of the LM head (vllm_turing/lmhead.py:52-61) as torch computes
+    it on `device`: "cuda" divides by 127 as a multiplication by its float32 reciprocal, "cpu" divides."""
+    w = np.ascontiguousarray(w, np.float32)
+    N, K = w.shape
+    q = np.empty((N, K), np.int8)
+    s = np.empty((N,), np.float32)
+    lib().orc_lmhead_quant(_p(w), _p(q), _p(s), N, K, int(device == "cuda"))
+    return q, s
+
+
+def w8a16(x_bits, w, s, bias_bits=None, dtype=1, want_acc=False):
+    """bits [M, N] of the W8A16 LM head, plus (acc, mag) float64 [M, N] when want_acc: the exact sums and the sums of
+    |products| (the scale of any fp32 summation error)."""
+    x_bits = np.ascontiguousarray(x_bits, np.uint16)
+    w = np.ascontiguousarray(w, np.int8)
+    s = np.ascontiguousarray(s, np.float32).reshape(-1)
+    M, K = x_bits.shape
+    N = w.shape[0]
+    out = np.empty((M, N), np.uint16)
+    acc = np.empty((M, N), np.float64) if want_acc else None
+    mag = np.empty((M, N), np.float64) if want_acc else None
+    bias_bits = np.ascontiguousarray(bias_bits, np.uint16) if bias_bits is not None else None
+    lib().orc_w8a16(_p(x_bits), _p(w), _p(s), _p(bias_bits) if bias_bits is not None else None, _p(out),
+                    _p(acc) if want_acc else None, _p(mag) if want_acc else None, M, N, K, dtype)
+    return (out, acc, mag) if want_acc else out
+
+
+def w8a16_close(got_bits, want_bits, mag, s, dtype=1, rel_sum=2.0 ** -16):
+    """The W8A16 parity test: |got - want| <= 1 unit in the last place of the 16-bit type at |want| plus
+    rel_sum * s[n] * mag[m, n] (fp32 summation-order error, generously bounded). Returns the worst ratio of error to
+    tolerance (<= 1 passes)."""
+    g = bits_to_float(got_bits, dtype).astype(np.float64)
+    w = bits_to_float(want_bits, dtype).astype(np.float64)
+    mant = 8 if dtype == 1 else 11
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(w), 1e-30))) - (mant - 1))
+    tol = ulp + rel_sum * np.abs(np.asarray(s, np.float64).reshape(1, -1)) * mag
+    return float(np.max(np.abs(g - w) / np.maximum(tol, 1e-30))) if g.size else 0.0

@@ -295,3 +295,59 @@ void orc_silu_mul_quant(const uint16_t *gu, int8_t *q, float *scales, int M, int
 void orc_all_gather(const uint8_t *const *payloads, int nranks, uint8_t *gathered, long m) {
     for (int r = 0; r < nranks; ++r) memcpy(gathered + (long)r * m, payloads[r], (size_t)m);
 }
+
+/* ---- LM head: per-row weight quantisation -------------------------------------------------------------------------
+ * Reference: vllm_turing/lmhead.py:52-61 (quantize_rows): sc = max(amax(|w|, row), 1e-12) / 127 in float32,
+ * q = round(w / sc) (half to even) clamped to [-128, 127]. w float32 [N, K] (the fp16 / bf16 head widened).
+ * The reference runs it on the GPU after loading (lmhead.py:125-128), where torch evaluates a tensor divided by a
+ * Python scalar as a multiplication by the float32 reciprocal: sc = amax * fl(1 / 127) (recip = 1). On the CPU torch
+ * divides (recip = 0). The division w / sc is a true float32 division on both. */
+void orc_lmhead_quant(const float *w, int8_t *q, float *scale, int N, int K, int recip) {
+    const float inv127 = 1.0f / 127.0f;
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        const float *wr = w + (long)n * K;
+        float amax = 0.0f;
+        for (int k = 0; k < K; ++k) {
+            const float v = fabsf(wr[k]);
+            amax = v > amax ? v : amax;
+        }
+        const float a = amax < 1e-12f ? 1e-12f : amax;
+        const float s = recip ? a * inv127 : a / 127.0f;
+        scale[n] = s;
+        for (int k = 0; k < K; ++k) {
+            float r = rintf(wr[k] / s);
+            r = r < -128.0f ? -128.0f : (r > 127.0f ? 127.0f : r);
+            q[(long)n * K + k] = (int8_t)r;
+        }
+    }
+}
+
+/* ---- LM head: W8A16 GEMM -----------------------------------------------------------------------------------------
+ * out[m, n] = round_dtype(fma(acc, s[n], bias[n])) with acc = sum_k x[m, k] * w[n, k]; x [M, K] 16-bit bits, w [N, K]
+ * int8, s [N] float32, bias [N] 16-bit bits or NULL.
+ * Reference: vllm_turing/csrc/w8a16_gemv.cu:64-106 (fp32 FMAs of an int8 weight and a 16-bit activation per lane,
+ * a shuffle tree, then `acc * s[ns] + b`, which nvcc contracts to one fma). Every product is exact in fp32; the
+ * reference's fp32 sum depends on its lane order, so the oracle takes the sum in double (the value every fp32 order
+ * approximates) and reports mag[m, n] = sum_k |x w|, which bounds the summation error of any fp32 order by
+ * about K * 2^-24 * mag. acc and mag may be NULL. */
+void orc_w8a16(const uint16_t *x, const int8_t *w, const float *s, const uint16_t *bias, uint16_t *out, double *acc,
+               double *mag, int M, int N, int K, int dtype) {
+#pragma omp parallel for schedule(static)
+    for (int n = 0; n < N; ++n) {
+        const int8_t *wr = w + (long)n * K;
+        const float b = bias ? ld16(bias, n, dtype) : 0.0f;
+        for (int m = 0; m < M; ++m) {
+            const uint16_t *xr = x + (long)m * K;
+            double sum = 0.0, mg = 0.0;
+            for (int k = 0; k < K; ++k) {
+                const double p = (double)wr[k] * (double)ld16(xr, k, dtype);
+                sum += p;
+                mg += fabs(p);
+            }
+            out[(long)m * N + n] = rnd16(fmaf((float)sum, s[n], b), dtype);
+            if (acc) acc[(long)m * N + n] = sum;
+            if (mag) mag[(long)m * N + n] = mg;
+        }
+    }
+}

@@ -11,6 +11,10 @@ exact formulas the reference's tests compute where the reference is CUDA:
   dequant    (float)acc * sa * sw rounded to the 16-bit type, in the order of vllm_turing/csrc/w8a8_gemv.cu:91
   allreduce  (x0.float() + x1.float()).half() (tests/bench_devll.py:28-36), rank order for more ranks
   norm+quant h = x + r; h.float() * rsqrt(mean(h^2) + eps) * w; quant_torch  (tests/test_quantfuse.py:45-48)
+  lm head    vllm_turing.lmhead.quantize_rows, imported from the reference tree (lmhead.py:52-61), on fp16 / bf16
+             heads; the W8A16 GEMM as the reference's kernel computes it (vllm_turing/csrc/w8a16_gemv.cu:64-106:
+             products exact in fp32, the sum, then acc * s + b in one fp32 rounding), with the sum in float64; and
+             the reference's large-M path (lmhead.py:104-110: dequantise to the activation dtype, matmul), run on CPU
   config 0   the whole chain at BASELINE config 0 (M=16, K_local=8704, N=5120, 2 ranks, seed 0): digests of the
              exact parts plus the int8 / scales arrays
 Inputs come from seeded torch CPU generators (vllm_turing_b200.synthetic for config 0) and are stored (small cases)
@@ -111,6 +115,30 @@ def main():
         out[key + "_x"], out[key + "_r"], out[key + "_w"] = bits(x), bits(r), bits(w)
         out[key + "_h"], out[key + "_y"] = bits(h), bits(y)
         out[key + "_q"], out[key + "_s"] = q.numpy(), s.reshape(-1).numpy()
+
+    # ---- LM head: the reference's row quantiser and the W8A16 arithmetic -----------------------------------------
+    from vllm_turing import lmhead   # the reference's module (its CUDA libraries are loaded lazily, not here)
+    for dt, code in ((torch.float16, 0), (torch.bfloat16, 1)):
+        for M, N, K in ((1, 64, 256), (5, 300, 1040), (17, 136, 512)):
+            w = (torch.randn(N, K, generator=g) * 0.02).to(dt)
+            w[3, 11] = 0.5                           # an outlier weight: its row's scale follows it
+            w[7] = 0.0                               # an all-zero row: scale clamps at 1e-12 / 127
+            q, sc = lmhead.quantize_rows(w)
+            x = torch.randn(M, K, generator=g).to(dt)
+            b = (torch.randn(N, generator=g) * 0.1).to(dt)
+            acc = x.double() @ q.double().t()
+            o = ((acc.float().double() * sc.double().view(1, -1) + b.double().view(1, -1)).float()).to(dt)
+            key = f"lm_{code}_{M}x{N}x{K}"
+            out[key + "_w"], out[key + "_q"], out[key + "_s"] = bits(w), q.numpy(), sc.numpy()
+            out[key + "_x"], out[key + "_b"] = bits(x), bits(b)
+            out[key + "_acc"], out[key + "_out"] = acc.numpy(), bits(o)
+    # the reference's own op above GEMV_MAX_M rows (dequantise, matmul), fp16, on CPU
+    Mb, Nb, Kb = 300, 40, 256
+    wb16 = (torch.randn(Nb, Kb, generator=g) * 0.02).half()
+    qb, sb = lmhead.quantize_rows(wb16)
+    xb = torch.randn(Mb, Kb, generator=g).half()
+    ob = lmhead._w8a16_mm(xb, qb, sb, None)
+    out["lmbig_x"], out["lmbig_q"], out["lmbig_s"], out["lmbig_out"] = bits(xb), qb.numpy(), sb.numpy(), bits(ob)
 
     # ---- M=16, K_local=8704, N=5120, 2 ranks, seed 0 ---------------------------------------------
     M, N, K = 16, 5120, 8704

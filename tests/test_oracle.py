@@ -124,3 +124,47 @@ def test_all_gather():
     ps = [np.full(37, r + 1, np.uint8) for r in range(4)]
     g = O.all_gather(ps)
     assert g.size == 4 * 37 and all((g[r * 37:(r + 1) * 37] == r + 1).all() for r in range(4))
+
+
+LM_CASES = [(1, 64, 256), (5, 300, 1040), (17, 136, 512)]
+
+
+@pytest.mark.parametrize("code", [0, 1])
+@pytest.mark.parametrize("case", LM_CASES)
+def test_lmhead_quant_matches_reference_quantize_rows(golden, code, case):
+    """vllm_turing/lmhead.py:52-61 (the reference's own function made the golden q, s), incl. an all-zero row."""
+    key = f"lm_{code}_{case[0]}x{case[1]}x{case[2]}"
+    w = O.bits_to_float(golden[key + "_w"], code)
+    q, s = O.lmhead_quant(w)                      # torch's CPU semantics, which made the golden vectors
+    assert np.array_equal(s, golden[key + "_s"])
+    assert np.array_equal(q, golden[key + "_q"])
+    qc, sc = O.lmhead_quant(w, device="cuda")      # the GPU form: scales within one float32 ulp
+    assert np.all(np.abs(sc.view(np.int32) - s.view(np.int32)) <= 1)
+    assert np.abs(qc.astype(np.int32) - q.astype(np.int32)).max() <= 1
+
+
+@pytest.mark.parametrize("code", [0, 1])
+@pytest.mark.parametrize("case", LM_CASES)
+def test_w8a16_formula(golden, code, case):
+    """The W8A16 arithmetic of vllm_turing/csrc/w8a16_gemv.cu:64-106: the exact sum (float64 here and in the golden
+    vectors, in different orders) and the one-rounding epilogue fma(acc, s, b)."""
+    key = f"lm_{code}_{case[0]}x{case[1]}x{case[2]}"
+    out, acc, mag = O.w8a16(golden[key + "_x"], golden[key + "_q"], golden[key + "_s"], golden[key + "_b"], code,
+                            want_acc=True)
+    np.testing.assert_allclose(acc, golden[key + "_acc"], rtol=1e-12, atol=1e-9)
+    assert (mag >= np.abs(acc)).all()
+    assert np.array_equal(out, golden[key + "_out"])
+    # the tolerance check used by the GPU tests accepts the oracle itself and rejects a planted error
+    assert O.w8a16_close(out, golden[key + "_out"], mag, golden[key + "_s"], code) == 0.0
+    bad = out.copy()
+    bad[0, 0] ^= 0x0100                                        # a wrong exponent bit
+    assert O.w8a16_close(bad, golden[key + "_out"], mag, golden[key + "_s"], code) > 1.0
+
+
+def test_w8a16_matches_reference_large_m_path(golden):
+    """Above 256 rows the reference dequantises the head to fp16 and multiplies (lmhead.py:104-110); that differs from
+    the kernels' arithmetic only by the fp16 rounding of the dequantised weights."""
+    out = O.w8a16(golden["lmbig_x"], golden["lmbig_q"], golden["lmbig_s"], None, 0)
+    got = O.bits_to_float(out, 0).astype(np.float64)
+    ref = O.bits_to_float(golden["lmbig_out"], 0).astype(np.float64)
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-3

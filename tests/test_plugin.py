@@ -111,7 +111,7 @@ def test_synthetic_inputs_are_deterministic():
     assert torch.equal(a.residual, c.residual) and torch.equal(a.norm_w, c.norm_w)   # shared across ranks
 
 
-@pytest.mark.parametrize("mod", ["w8a8", "hostar", "quantfuse", "customar", "dmaag", "tailoverlap", "comm"])
+@pytest.mark.parametrize("mod", ["w8a8", "hostar", "quantfuse", "customar", "dmaag", "tailoverlap", "comm", "lmhead"])
 def test_modules_import_without_gpu(mod):
     __import__(f"vllm_turing_b200.{mod}")
 
@@ -128,3 +128,70 @@ def test_interleave_gate_up_order():
         assert rows[128 * t:128 * t + 64] == list(range(64 * t, 64 * t + 64))
         assert rows[128 * t + 64:128 * t + 128] == list(range(I + 64 * t, I + 64 * t + 64))
     assert si.tolist() == [float(r) for r in rows]
+
+
+def test_w8a16_op_registered_and_quantize_rows_matches_oracle():
+    """vllm_turing::w8a16_mm exists (the reference's op name, lmhead.py:80-81) and the package's quantize_rows is the
+    oracle's restatement of the reference's formula (bit-exact on CPU)."""
+    from oracle import oracle as O
+    from vllm_turing_b200 import lmhead
+    assert hasattr(torch.ops.vllm_turing, "w8a16_mm")
+    w = (torch.randn(40, 96, generator=torch.Generator().manual_seed(4)) * 0.02).half()
+    w[2] = 0
+    q, s = lmhead.quantize_rows(w)
+    qo, so = O.lmhead_quant(w.float().numpy())
+    assert np.array_equal(q.numpy(), qo) and np.array_equal(s.numpy(), so)
+
+
+class _FakeComm:
+    """The communicator's all-gather contract on CPU tensors: fills the peers' blocks from the given peers' inputs."""
+
+    def __init__(self, xs, rank, ll=1 << 20):
+        self.xs, self.rank, self.world, self.ll_capacity = xs, rank, len(xs), ll
+        self.calls = []
+
+    def all_gather_rows(self, out, rows, row_bytes, ld_bytes):
+        self.calls.append("rows")
+        b = out.view(-1).view(torch.uint8).view(rows, ld_bytes)
+        for r, x in enumerate(self.xs):
+            if r != self.rank:
+                b[:, r * row_bytes:(r + 1) * row_bytes] = x.reshape(rows, -1).view(torch.uint8)
+        return out
+
+    def all_gather(self, g, m):
+        self.calls.append("slots")
+        for r, x in enumerate(self.xs):
+            if r != self.rank:
+                g[r * m:(r + 1) * m] = x.reshape(-1).view(torch.uint8)
+        return g
+
+
+@pytest.mark.parametrize("shape,dim", [((5, 24), -1), ((2, 3, 8), -1), ((6, 16), 0), ((4, 6, 8), 1), ((3, 5), -1),
+                                       ((4, 6), -1)])
+@pytest.mark.parametrize("world", [2, 4])
+def test_all_gather_dim_layout(shape, dim, world):
+    """dmaag.all_gather_dim gives vLLM's all_gather(dim) result (torch.cat of the ranks' tensors along dim) for every
+    layout path: row-strided in place (last dim), contiguous slots (dim 0), slots + movedim (other dims, or payloads
+    whose row is not a multiple of 8 bytes)."""
+    from vllm_turing_b200 import dmaag
+    g = torch.Generator().manual_seed(world)
+    xs = [torch.randn(*shape, generator=g).to(torch.bfloat16) for _ in range(world)]
+    want = torch.cat(xs, dim=dim)
+    m = xs[0].numel() * 2
+    for rank in range(world):
+        fc = _FakeComm(xs, rank)
+        got = dmaag.all_gather_dim(fc, xs[rank], dim)
+        if m % 8:                                      # no 8-byte words: left to vLLM's all-gather
+            assert got is None and fc.calls == []
+            continue
+        assert got is not None and torch.equal(got, want), (rank, fc.calls)
+        last = dim in (-1, len(shape) - 1)
+        assert fc.calls == (["rows"] if last and (shape[-1] * 2) % 8 == 0 else ["slots"])
+
+
+def test_all_gather_dim_large_last_dim_uses_slots():
+    from vllm_turing_b200 import dmaag
+    xs = [torch.full((3, 64), float(r)).to(torch.bfloat16) for r in range(2)]
+    fc = _FakeComm(xs, 1, ll=128)                                     # payload 384 B > the one-shot capacity
+    got = dmaag.all_gather_dim(fc, xs[1], -1)
+    assert torch.equal(got, torch.cat(xs, -1)) and fc.calls == ["slots"]

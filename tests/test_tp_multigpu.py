@@ -2,7 +2,9 @@
 torch.multiprocessing.spawn, a gloo group for set-up, tests/test_hostar.py:13-20), against the CPU oracle:
   - one-shot and two-shot all-reduce bit-exact to the rank-ordered float32 sum (tests/bench_devll.py:28-36 for 2 ranks)
     at decode / odd / prefill sizes, fp16 and bf16, identical on every rank;
-  - all-gather (LL and bulk) exact;
+  - all-gather (LL and bulk, contiguous slots and row-strided along the last dimension) exact;
+  - the int8 LM head's vocabulary-parallel logits at config 4's TP8 shard (151936 / 8 rows x 5120) gathered in place
+    on every rank, within the W8A16 tolerance of the oracle;
   - the fused GEMV + all-reduce + residual + RMSNorm + quant at BASELINE config 0 (M=16, K_local=8704, N=5120) and
     config 2 (M in {1, 5}, K = 17408 / world): reduced sum bit-exact, residual bit-exact, int8 within 1 LSB;
   - 64 back-to-back calls without host syncs, and a captured CUDA graph of mixed calls replayed with fresh inputs
@@ -77,6 +79,35 @@ def _worker(rank, world, port, q):
             for r in range(world):
                 exp = (r * 37 + torch.arange(m) % 251).to(torch.uint8)
                 check(torch.equal(g[r * m:(r + 1) * m].cpu(), exp), f"all_gather m={m} slot {r}")
+
+        # ---- row-strided all-gather, and the int8 LM head's vocabulary-parallel logits gathered in place ----
+        from vllm_turing_b200 import dmaag, lmhead
+        for shape in ((5, 24), (3, 2, 40)):
+            xs_ = [(torch.randn(*shape, generator=torch.Generator().manual_seed(7 + r)) * 2).to(torch.bfloat16)
+                   for r in range(world)]
+            got = dmaag.all_gather_dim(comm, xs_[rank].to(dev), -1)
+            torch.cuda.synchronize()
+            check(got is not None and torch.equal(got.cpu(), torch.cat(xs_, -1)), f"all_gather_dim {shape}")
+        Vs, Kh = 151936 // 8, 5120                       # one TP8 rank's share of the vocabulary (config 4's head)
+        for M in (1, 5):
+            xh = torch.randn(M, Kh, generator=torch.Generator().manual_seed(300 + M)).to(torch.bfloat16)
+            heads = []
+            for r in range(world):
+                gw = torch.Generator().manual_seed(400 + r)
+                heads.append((torch.randint(-128, 128, (Vs, Kh), generator=gw, dtype=torch.int8),
+                              torch.rand(Vs, generator=gw) * 1e-3))
+            logits = lmhead.logits_gathered(xh.to(dev), heads[rank][0].to(dev), heads[rank][1].to(dev), comm=comm)
+            torch.cuda.synchronize()
+            lb = O.to_bits(logits.cpu())
+            for r in range(world):
+                if r in (rank, (rank + 1) % world):   # own columns and one peer's: the CPU oracle is slow at this size
+                    want, _, mag = O.w8a16(O.to_bits(xh), heads[r][0].numpy(), heads[r][1].numpy(), None, 1,
+                                           want_acc=True)
+                    err = O.w8a16_close(lb[:, r * Vs:(r + 1) * Vs], want, mag, heads[r][1].numpy(), 1)
+                    check(err <= 1.0, f"lm head logits M={M} block {r}: error {err:.2f} of tolerance")
+            l0 = logits.cpu().view(torch.int16).clone()
+            dist.broadcast(l0, src=0)
+            check(torch.equal(l0, logits.cpu().view(torch.int16)), f"lm head logits differ from rank 0 (M={M})")
 
         # ---- fused row-linear ----
         for (M, N, K) in ((16, 5120, 8704), (5, 5120, 17408 // world), (1, 5120, 17408 // world),

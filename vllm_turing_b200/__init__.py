@@ -8,7 +8,10 @@ The drop-in replacement for vllm-turing's hot path (vllm_turing/__init__.py:38-7
     decode messages, two-shot reduce-scatter + all-gather for prefill)
   - quantfuse: per-token int8 activation quantisation (the formula inductor fuses into the producer)
   - fused: row-parallel linear + all-reduce + residual add + RMSNorm + per-token int8 quantisation in one kernel
-  - dmaag: the all-gather primitive (each rank pre-writes its slot, the kernel fills the peers' slots)
+  - dmaag: the all-gather primitive (each rank pre-writes its slot, the kernel fills the peers' slots), also behind
+    CudaCommunicator.all_gather / gather
+  - lmhead: the int8 LM head (W8A16: int8 rows converted to 16-bit in tensor memory, tcgen05 kind::f16) and the
+    vocabulary-parallel logits gathered in place
   - customar / tailoverlap: the reference's vLLM-side switches on this path
 VLLM_TURING_DISABLE=1 turns everything off. Every module honours the reference's VLLM_TURING_<NAME> switches.
 """
@@ -25,7 +28,7 @@ def register():
     if _registered or os.environ.get("VLLM_TURING_DISABLE") == "1":
         return
     _registered = True
-    from . import customar, dmaag, hostar, quantfuse, tailoverlap, w8a8
+    from . import customar, dmaag, hostar, lmhead, quantfuse, tailoverlap, w8a8
 
     tailoverlap.install()
     quantfuse.install()
@@ -33,5 +36,6 @@ def register():
     w8a8.install()
     hostar.install()
     dmaag.install()
+    lmhead.install()
     logger.info("vllm_turing_b200: W8A8 GEMV for M <= %d, tensor-core kernels above; P2P all-reduce %s",
                 w8a8.MAX_M, "on" if hostar.ENABLED else "off")

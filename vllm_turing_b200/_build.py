@@ -20,7 +20,8 @@ _csrc = os.path.join(_here, "csrc")
 _include = os.path.join(os.path.dirname(_here), "include")
 LIB_NAME = "libvllm_turing_b200.so"
 LIB_PATH = os.path.join(_here, LIB_NAME)
-SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "norm_quant.cu", "tp_comm.cu", "tp_fused.cu")
+SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "w8a16_tc.cu", "norm_quant.cu", "tp_comm.cu",
+           "tp_fused.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 _lib = None
 
@@ -117,6 +118,11 @@ SIGNATURES = {
     "vt_gemm_s32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_gate_up_silu_quant_ws_bytes": (_SZ, [_I, _I]),
     "vt_gate_up_silu_quant": (_I, [_P] * 6 + [_I] * 5 + [_P, _SZ, _P]),
+    "w8a16_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
+    "w8a16_gemv_rows": (_I, [_P] * 5 + [_I] * 4 + [_P, _P]),
+    "w8a16_mma": (_I, [_P] * 5 + [_I] * 4 + [_P]),
+    "vt_w8a16_ws_bytes": (_SZ, [_I]),
+    "vt_w8a16_mm": (_I, [_P] * 5 + [_I] * 5 + [_P, _SZ, _P]),
     "vt_scaled_int8_quant": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_rms_norm_quant": (_I, [_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _P]),
     "silu_mul_quant": (_I, [_P, _P, _P, _I, _I, _P]),
@@ -135,6 +141,7 @@ SIGNATURES = {
     "vt_comm_seq": (_U, [_P]),
     "vt_all_reduce": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
     "vt_all_gather": (_I, [_P, _P, _LL, _P]),
+    "vt_all_gather_rows": (_I, [_P, _P, _LL, _LL, _LL, _P]),
     "vt_tp_row_linear": (_I, [_P] * 5 + [_P, _P, _F, _P, _P, _P] + [_I] * 4 + [_P]),
     "vt_tp_preload": (_I, []),
 }

@@ -153,9 +153,22 @@ class TPComm:
 
     def all_gather(self, gathered, m):
         """gathered: uint8 [world * m] with this rank's payload in slot `rank` already; fills the peers' slots."""
+        if not gathered.is_cuda:
+            raise CommError("vllm_turing_b200: all_gather needs a device buffer")
         rc = self.L.vt_all_gather(self.handle, gathered.data_ptr(), int(m), torch.cuda.current_stream().cuda_stream)
         if rc != 0:
             raise CommError(f"vt_all_gather failed: {rc}")
+        return gathered
+
+    def all_gather_rows(self, gathered, rows, row_bytes, ld_bytes):
+        """gathered: [rows, ld_bytes] device buffer holding world column blocks of row_bytes per row, this rank's
+        block pre-written; fills the peers' blocks (one-shot LL; rows * row_bytes within ll_capacity)."""
+        if not gathered.is_cuda:
+            raise CommError("vllm_turing_b200: all_gather_rows needs a device buffer")
+        rc = self.L.vt_all_gather_rows(self.handle, gathered.data_ptr(), int(rows), int(row_bytes), int(ld_bytes),
+                                       torch.cuda.current_stream().cuda_stream)
+        if rc != 0:
+            raise CommError(f"vt_all_gather_rows failed: {rc}")
         return gathered
 
     def row_linear(self, a, w, sa, sw, residual=None, norm_w=None, eps=1e-6, q=None, scales=None, reduced=None):

@@ -170,18 +170,20 @@ __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, cons
 }
 
 // ---- all-gather ------------------------------------------------------------------------------------------------------
-// LL variant (small payloads): m bytes per rank, m % 8 == 0.
-__global__ void __launch_bounds__(AR_THREADS) ag_ll_kernel(CommView c, char *__restrict__ gathered, long long m,
-                                                           uint64_t timeout) {
+// LL variant (small payloads). Rank r's payload is `rows` runs of row_bytes (% 8 == 0) at byte offset
+// i * ld + r * row_bytes of `gathered` (rows = 1: the contiguous slots [r * m, (r + 1) * m)); its 8-byte words travel
+// as LL words in payload order.
+__global__ void __launch_bounds__(AR_THREADS) ag_ll_kernel(CommView c, char *__restrict__ gathered, long long rows,
+                                                           long long row_bytes, long long ld, uint64_t timeout) {
     __shared__ unsigned s_seq;
     const unsigned seq = comm_begin(c, &s_seq);
     const unsigned p = seq & 1u;
     const uint64_t deadline = globaltimer() + timeout;
-    const long long nw = m >> 3, stride = (long long)gridDim.x * blockDim.x;
+    const long long wpr = row_bytes >> 3, nw = rows * wpr, stride = (long long)gridDim.x * blockDim.x;
     const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const uint2 *mine = reinterpret_cast<const uint2 *>(gathered + (long long)c.rank * m);
     for (long long i = i0; i < nw; i += stride) {
-        const uint2 d = mine[i];
+        const long long r = i / wpr, j = i - r * wpr;
+        const uint2 d = *reinterpret_cast<const uint2 *>(gathered + r * ld + (long long)c.rank * row_bytes + j * 8);
         for (int k = 1; k < c.world; ++k) {
             const int dst = (c.rank + k) % c.world;
             ll_store(c.ll_slot(dst, p, c.rank) + i * 16, d.x, d.y, seq);
@@ -189,6 +191,7 @@ __global__ void __launch_bounds__(AR_THREADS) ag_ll_kernel(CommView c, char *__r
     }
     bool dead = false;
     for (long long i = i0; i < nw; i += stride) {
+        const long long r = i / wpr, j = i - r * wpr;
         for (int k = 1; k < c.world; ++k) {
             const int src = (c.rank + k) % c.world;
             uint2 d = make_uint2(0u, 0u);
@@ -196,7 +199,7 @@ __global__ void __launch_bounds__(AR_THREADS) ag_ll_kernel(CommView c, char *__r
                 report(c.status(), ST_PEER_TIMEOUT | 0x300u | (unsigned)src);
                 dead = true;
             }
-            reinterpret_cast<uint2 *>(gathered + (long long)src * m)[i] = d;
+            *reinterpret_cast<uint2 *>(gathered + r * ld + (long long)src * row_bytes + j * 8) = d;
         }
     }
     comm_end(c, seq);
@@ -402,7 +405,7 @@ int vt_all_gather(void *comm, void *gathered, long long m, void *stream) {
         const long long nw = m >> 3;
         long long g = (nw + AR_THREADS - 1) / AR_THREADS;
         if (g > sms) g = sms;
-        ag_ll_kernel<<<(int)g, AR_THREADS, 0, s>>>(c->v, (char *)gathered, m, peer_timeout_ns());
+        ag_ll_kernel<<<(int)g, AR_THREADS, 0, s>>>(c->v, (char *)gathered, 1, m, m * c->v.world, peer_timeout_ns());
         return (int)cudaGetLastError();
     }
     if (m & 15) return VT_EARG;
@@ -417,6 +420,29 @@ int vt_all_gather(void *comm, void *gathered, long long m, void *stream) {
         if (cudaError_t e = cudaGetLastError()) return (int)e;
     }
     return 0;
+}
+
+// Row-strided all-gather: gathered [rows, ld_bytes] holds world column blocks of row_bytes per row; this rank's block
+// (byte offset rank * row_bytes of every row) is pre-written, the call fills the peers' blocks. The concatenation
+// along the last dimension that vLLM's all_gather(dim=-1) builds (logits [M, world * V / world]) without a separate
+// transpose. row_bytes % 8 == 0, ld_bytes % 8 == 0, ld_bytes >= world * row_bytes, rows * row_bytes at most the LL
+// capacity (one-shot LL words); larger payloads: VT_EARG (use vt_all_gather on contiguous slots).
+int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row_bytes, long long ld_bytes,
+                       void *stream) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    if (!c || rows < 0 || row_bytes < 0 || ((uintptr_t)gathered & 7) || (row_bytes & 7) || (ld_bytes & 7) ||
+        ld_bytes < (long long)c->v.world * row_bytes)
+        return VT_EARG;
+    if (rows == 0 || row_bytes == 0 || c->v.world == 1) return 0;
+    const long long m = rows * row_bytes;
+    if (m > (long long)(c->v.L.ll_slot / 2) || m > (1 << 20)) return VT_EARG;
+    const long long nw = m >> 3;
+    long long g = (nw + AR_THREADS - 1) / AR_THREADS;
+    const int sms = num_sms(c->dev);
+    if (g > sms) g = sms;
+    ag_ll_kernel<<<(int)g, AR_THREADS, 0, (cudaStream_t)stream>>>(c->v, (char *)gathered, rows, row_bytes, ld_bytes,
+                                                                   peer_timeout_ns());
+    return (int)cudaGetLastError();
 }
 
 }  // extern "C"

@@ -1,0 +1,589 @@
+// W8A16 GEMM for the LM head on the B200 tensor cores: int8 weight rows with one fp32 scale each, 16-bit float
+// activations (bf16 or fp16), tcgen05.mma kind::f16 with fp32 accumulators in tensor memory (TMEM).
+//
+//   out[m, n] = T((sum_k x[m, k] * W[n, k]) * s[n] + bias[n])      x [M, K], W [N, K] int8 row-major, s [N] fp32
+//
+// This is the arithmetic of the reference's W8A16 kernels (vllm_turing/csrc/w8a16_gemv.cu:27-107 on CUDA-core fp32
+// FMAs, vllm_turing/csrc/w8a16_mma.cu on fp16 mma.sync): every product of an int8 weight and a 16-bit activation is
+// exact in fp32, the sums are fp32, and the row scale and the bias are applied to the finished sum
+// (w8a16_gemv.cu:103). Only the order of the fp32 additions differs from the reference's, so results agree to the
+// rounding of fp32 sums, not bit for bit.
+//
+// Work layout (the decode orientation of the W8A8 core, tc_core.cuh): the weights are the MMA's A operand in 128-row
+// tiles of the vocabulary; the M <= 64 token rows are its B operand (BN = 16, 32 or 64 rows, zero-filled past M). The
+// (tile, K block) index space is cut into one contiguous range per CTA (stream-K), so every SM streams the same share
+// of the weights. A split tile is finished by its head CTA from the other CTAs' fp32 partial sums (LL slot words).
+//
+// The int8 -> 16-bit conversion runs between shared memory and the tensor core, into TMEM:
+//   - warp 0 (one thread) TMA-loads each K block (128 weight rows x 128 bytes, 128-byte swizzle) and the activations
+//     of that K block (two 64-element swizzle atoms of BN rows) into a ring of shared-memory stages;
+//   - warps 6..9 convert: a thread owns one weight row of its warp's TMEM lane quarter, reads that row's 128 bytes (the
+//     swizzle spreads the 32 row reads of a warp over all banks), converts them exactly to 16-bit floats and stores
+//     them with tcgen05.st into a ring of A stages in TMEM (64 columns of two elements per row and K block);
+//   - warp 1 (one thread) issues 8 MMAs (K = 16 each) per K block, A from TMEM, B from shared memory;
+//   - warps 2..5 drain the accumulators (tcgen05.ld), apply the row scale and the bias and store the logits.
+// Shared memory carries the weights once in and once out as int8, plus the small activation tiles. Converting into
+// shared memory instead would add the 16-bit copy's write and the tensor core's read of it: about three times the
+// shared-memory traffic per weight byte.
+//
+// Every wait is bounded (globaltimer); on a timeout the CTA records the status, stops issuing, waits (bounded) for the
+// copies and MMAs it issued, frees its TMEM and returns.
+//
+// C ABI (include/vllm_turing_b200.h): w8a16_gemv, w8a16_gemv_rows, w8a16_mma (the reference's signatures,
+// w8a16_gemv.cu:114-145 and w8a16_mma.cu:160-175), vt_w8a16_mm and vt_w8a16_ws_bytes (caller-owned workspace, an output
+// row stride, M up to 64 in either dtype).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "host_util.h"
+#include "tc_core.cuh"
+#include "tma_host.h"
+
+namespace vt {
+
+constexpr int WH_THREADS = 320;             // 10 warps: producer, MMA, 4 epilogue, 4 converter
+constexpr int WH_AS = 4;                    // A stages in TMEM, one K block (128 elements = 64 columns) each
+constexpr int WH_ACOL = 128;                // first TMEM column of the A stages (the accumulators use columns < 128)
+constexpr int WH_TMEM_COLS = 512;           // WH_ACOL + WH_AS * 64 = 384, rounded up to a power of two
+constexpr int WH_W_BYTES = TC_BM * TC_BK;   // int8 weights of one K block: 128 rows x 128 bytes
+constexpr int WH_BAR_BYTES = 512;
+constexpr int WH_MAX_M = 64;
+
+template <int BN> struct WhLayout {
+    static constexpr int X_ATOM = BN * 128;   // one 64-element, BN-row swizzle atom of the activations
+    static constexpr int STAGE = WH_W_BYTES + 2 * X_ATOM;
+};
+
+struct WhArgs {
+    TcArgs t;   // stream-K partition (tc_decode_args), t.sw = the row scales, t.bias, t.out, t.slots, t.status
+    int ldo;    // output row stride in elements (>= N)
+};
+
+// D (TMEM, fp32) (+)= A (TMEM, 16-bit) . B (shared-memory descriptor)^T, kind::f16
+__device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and B both bf16 (bits 7-9, 10-12 = 1) or
+// both fp16 (0), both K-major, MMA M x N.
+template <typename T> __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    constexpr uint32_t ab = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+    return (1u << 4) | (ab << 7) | (ab << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+// 32 consecutive 32-bit TMEM columns of the warp's 32 lanes (thread i writes lane base + i)
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+        "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+        "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Four int8 (one word, element k in the low byte) -> two words of 16-bit floats {k, k+1}, {k+2, k+3} (element k in the
+// low half), exactly. The bytes are first spread to 0x00b1_00b0 / 0x00b3_00b2.
+//   bf16: with b = v - 128 s (v = b & 127, s = the sign bit), 0x4300 | v is bf16(128 + v) and 0x4300 | (b & 128) is
+//         bf16(128 + 128 s); their difference is b (exact: both operands and the result are bf16 integers).
+//   fp16: 0x6400 | (b ^ 128) is fp16(1024 + b + 128); minus fp16(1152) = 0x6480 it is b.
+template <typename T> __device__ __forceinline__ uint32_t cvt_pair(uint32_t spread);
+template <> __device__ __forceinline__ uint32_t cvt_pair<__nv_bfloat16>(uint32_t p) {
+    const uint32_t hi = (p & 0x007F007Fu) | 0x43004300u, lo = (p & 0x00800080u) | 0x43004300u;
+    __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162 *>(&hi), b = *reinterpret_cast<const __nv_bfloat162 *>(&lo);
+    __nv_bfloat162 d = __hsub2(a, b);
+    return *reinterpret_cast<uint32_t *>(&d);
+}
+template <> __device__ __forceinline__ uint32_t cvt_pair<__half>(uint32_t p) {
+    const uint32_t u = (p ^ 0x00800080u) | 0x64006400u, c = 0x64806480u;
+    __half2 a = *reinterpret_cast<const __half2 *>(&u), b = *reinterpret_cast<const __half2 *>(&c);
+    __half2 d = __hsub2(a, b);
+    return *reinterpret_cast<uint32_t *>(&d);
+}
+template <typename T> __device__ __forceinline__ void cvt_word(uint32_t w, uint32_t &o0, uint32_t &o1) {
+    o0 = cvt_pair<T>(__byte_perm(w, 0u, 0x4140));
+    o1 = cvt_pair<T>(__byte_perm(w, 0u, 0x4342));
+}
+
+// all lanes of the warp wait on the same barrier; the warp continues only if every lane saw it complete
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, uint64_t deadline) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, deadline)) != 0;
+}
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(WH_THREADS, 1)
+    w8a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
+                    const WhArgs A) {
+    using Lay = WhLayout<BN>;
+    const TcArgs &P = A.t;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *tiles = tc_align1024(smem_raw);
+    const int S = P.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + (size_t)S * Lay::STAGE);
+    uint64_t *empty = full + S;
+    uint64_t *afull = empty + S;        // [WH_AS] converted K block in TMEM (4 converter warps arrive)
+    uint64_t *aempty = afull + WH_AS;   // [WH_AS] the MMAs reading it completed (commit)
+    uint64_t *tfull = aempty + WH_AS;   // [2]
+    uint64_t *tempty = tfull + 2;       // [2]
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 4);   // [0] abort
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < WH_AS; ++a) {
+            mbar_init(&afull[a], 4);
+            mbar_init(&aempty[a], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 4);
+        }
+        mbar_init(drain, 1);
+        flags[0] = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmap_w);
+        tma_prefetch_desc(&tmap_x);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, WH_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+    // only the producer runs ahead of the previous kernel: the weights and scales are no kernel's output
+    const bool producer = (warp == 0 && lane == 0);
+    if (!producer) pdl_wait();
+    uint64_t deadline = globaltimer() + P.timeout_ns;
+
+    int ta, tb, kb0, kb1;
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            const uint64_t pol = policy_evict_first();   // the head is read once per call
+            int pre = 0;
+            {
+                TcPieces pp(P);
+                while (pre < S && pp.next(P, ta, tb, kb0, kb1))
+                    for (int kb = kb0; kb < kb1 && pre < S; ++kb, ++pre) {
+                        mbar_arrive_expect_tx(&full[pre], (uint32_t)Lay::STAGE);
+                        tma_load_2d_hint(tiles + (size_t)pre * Lay::STAGE, &tmap_w, kb * TC_BK, ta * TC_BM, &full[pre],
+                                         pol);
+                    }
+            }
+            pdl_wait();
+            deadline = globaltimer() + P.timeout_ns;
+            int it = 0;
+            bool dead = false;
+            TcPieces pc(P);
+            while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t r = (uint32_t)(it / S);
+                    unsigned char *st = tiles + (size_t)s * Lay::STAGE;
+                    if (it >= pre) {
+                        if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
+                            if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x110u);
+                            flags[0] = 1;
+                            dead = true;
+                            break;
+                        }
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)Lay::STAGE);
+                        tma_load_2d_hint(st, &tmap_w, kb * TC_BK, ta * TC_BM, &full[s], pol);
+                    }
+                    tma_load_2d(st + WH_W_BYTES, &tmap_x, kb * TC_BK, 0, &full[s]);
+                    tma_load_2d(st + WH_W_BYTES + Lay::X_ATOM, &tmap_x, kb * TC_BK + 64, 0, &full[s]);
+                }
+            }
+            if (dead) {   // let the copies already issued land before the shared memory is released
+                const uint64_t d2 = globaltimer() + P.timeout_ns;
+                for (int j = (it > S ? it - S : 0); j < it; ++j) mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, d2);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_f16<T>(TC_BM, BN);
+            int it = 0, ut = 0;
+            TcPieces pc(P);
+            while (pc.next(P, ta, tb, kb0, kb1)) {
+                const int buf = ut & 1;
+                const uint32_t use = (uint32_t)(ut >> 1);
+                ++ut;
+                if (!flags[0] && !mbar_wait(&tempty[buf], (use & 1u) ^ 1u, deadline)) {
+                    report(P.status, ST_PIPE_TIMEOUT | 0x120u);
+                    flags[0] = 1;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * BN);
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    if (flags[0]) break;   // aborted: issue nothing more
+                    const int s = it % S, a = it % WH_AS;
+                    // full[s]: the activations landed (the converters saw it too); afull[a]: the weights are in TMEM
+                    if (!mbar_wait(&full[s], (uint32_t)(it / S) & 1u, deadline) ||
+                        !mbar_wait(&afull[a], (uint32_t)(it / WH_AS) & 1u, deadline)) {
+                        report(P.status, ST_PIPE_TIMEOUT | 0x130u);
+                        flags[0] = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t xb = smem_u32(tiles + (size_t)s * Lay::STAGE + WH_W_BYTES);
+                    const uint32_t at = tmem_base + (uint32_t)(WH_ACOL + a * 64);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {   // 16 elements (32 bytes, 8 TMEM columns) per MMA
+                        const uint64_t bdesc = sw128_desc(xb + (uint32_t)((k >> 2) * Lay::X_ATOM)) + 2 * (k & 3);
+                        umma_f16_ts(d, at + 8 * k, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&aempty[a]);
+                    umma_commit(&empty[s]);
+                }
+                if (!flags[0]) umma_commit(&tfull[buf]);
+            }
+            // every MMA this thread issued has completed once `drain` flips (bounded: TMEM is freed after it)
+            umma_commit(drain);
+            mbar_wait(drain, 0u, globaltimer() + P.timeout_ns);
+        }
+    } else if (warp >= 6) {
+        // ---------------- converters: int8 rows (shared memory) -> 16-bit rows (TMEM) ----------------
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)WH_ACOL;
+        int it = 0;
+        bool dead = false;
+        TcPieces pc(P);
+        while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
+            for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                const int s = it % S, a = it % WH_AS;
+                // warp-uniform decisions only: tcgen05.st below is a whole-warp instruction
+                const bool aborted = __any_sync(0xffffffffu, flags[0] != 0);
+                bool ok = !aborted;
+                if (ok) ok = warp_wait(&full[s], (uint32_t)(it / S) & 1u, deadline);
+                if (ok) ok = warp_wait(&aempty[a], ((uint32_t)(it / WH_AS) & 1u) ^ 1u, deadline);
+                if (!ok) {
+                    if (lane == 0 && !aborted) report(P.status, ST_PIPE_TIMEOUT | 0x140u);
+                    flags[0] = 1;
+                    dead = true;
+                    break;
+                }
+                tc_fence_after();   // the MMAs that read this A stage before have completed
+                const unsigned char *src = tiles + (size_t)s * Lay::STAGE + row * TC_BK;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t o[32];
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int j = h * 4 + c;   // 16-byte chunk j of the row sits at chunk j ^ (row % 8)
+                        const uint4 v = *reinterpret_cast<const uint4 *>(src + ((j ^ (row & 7)) << 4));
+                        cvt_word<T>(v.x, o[8 * c + 0], o[8 * c + 1]);
+                        cvt_word<T>(v.y, o[8 * c + 2], o[8 * c + 3]);
+                        cvt_word<T>(v.z, o[8 * c + 4], o[8 * c + 5]);
+                        cvt_word<T>(v.w, o[8 * c + 6], o[8 * c + 7]);
+                    }
+                    tmem_st32(lane_base + (uint32_t)(a * 64 + h * 32), o);
+                }
+                tmem_st_wait();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&afull[a]);
+            }
+        }
+    } else {
+        // ---------------- epilogue warps 2..5 ----------------
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
+        const int hw = (P.M + 1) >> 1;
+        const T *bias = reinterpret_cast<const T *>(P.bias);
+        T *out = reinterpret_cast<T *>(P.out);
+        int ut = 0;
+        TcPieces pc(P);
+        while (pc.next(P, ta, tb, kb0, kb1)) {
+            const int buf = ut & 1;
+            const uint32_t use = (uint32_t)(ut >> 1);
+            ++ut;
+            const int n = ta * TC_BM + row;
+            const bool nok = n < P.N;
+            const bool whole = (kb0 == 0 && kb1 == P.nkb);
+            const bool head = (kb0 == 0 && !whole);
+            float sn = 0.f, bn = 0.f;   // loads in flight while the MMAs run
+            if (nok) {
+                sn = P.sw[n];
+                if (bias) bn = t2f<T>(bias[n]);
+            }
+            float acc[BN];
+#pragma unroll
+            for (int m = 0; m < BN; ++m) acc[m] = 0.f;
+            if (head) {
+                // the CTAs holding the tile's later K blocks left their fp32 sums in their slots: add them in CTA
+                // order (a fixed order: the results do not depend on timing) and clear the slots for the next call
+                const int clast = tc_owner(P, ta * P.nkb + P.nkb - 1);
+                for (int c = blockIdx.x + 1; c <= clast; ++c) {
+#pragma unroll
+                    for (int h = 0; h < BN / 2; ++h) {
+                        if (h >= hw) continue;
+                        uint4 v = ld_volatile16(tc_slot(P, c, h, row));
+                        uint32_t spin = 0;
+                        while (v.y != 1u || v.w != 1u) {
+                            if ((++spin & 255u) == 0 && globaltimer() > deadline) {
+                                report(P.status, ST_PIPE_TIMEOUT | 0x150u);
+                                break;
+                            }
+                            v = ld_volatile16(tc_slot(P, c, h, row));
+                        }
+                        acc[2 * h] += __uint_as_float(v.x);
+                        acc[2 * h + 1] += __uint_as_float(v.z);
+                        *tc_slot(P, c, h, row) = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+            }
+            if (!__any_sync(0xffffffffu, flags[0] != 0) && !warp_wait(&tfull[buf], use & 1u, deadline)) {
+                if (lane == 0) report(P.status, ST_PIPE_TIMEOUT | 0x160u);
+                flags[0] = 1;
+            }
+            tc_fence_after();
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+            uint32_t r[2][32];
+            if (BN == 16) {
+                tmem_ld16(taddr, r[0]);
+            } else {
+                tmem_ld32(taddr, r[0]);
+                if (BN == 64) tmem_ld32(taddr + 32u, r[1]);
+            }
+            tmem_ld_wait();
+            tc_fence_before();   // this warp's TMEM reads are done: the MMA may refill the buffer
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[buf]);
+#pragma unroll
+            for (int m = 0; m < BN; ++m) acc[m] += __uint_as_float(r[m >> 5][m & 31]);
+            if (whole || head) {
+                if (nok) {
+#pragma unroll
+                    for (int m = 0; m < BN; ++m)   // (acc * s + b): the reference's fp32 epilogue, one rounding
+                        if (m < P.M) out[(size_t)m * A.ldo + n] = f2t<T>(__fmaf_rn(acc[m], sn, bn));
+                }
+            } else {
+                // the CTA's first piece, inside a tile another CTA finishes: leave its sums in this CTA's slot
+#pragma unroll
+                for (int h = 0; h < BN / 2; ++h)
+                    if (h < hw)
+                        ll_store(tc_slot(P, blockIdx.x, h, row), __float_as_uint(acc[2 * h]),
+                                 __float_as_uint(acc[2 * h + 1]), 1u);
+            }
+        }
+    }
+    // all roles done: free TMEM after every TMEM access and MMA of the CTA has completed
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, WH_TMEM_COLS);
+    }
+}
+
+// ---- CUDA-core gather variant (rows != NULL): out[m, i] = x[m] . W[rows[i]] * s[rows[i]] + bias[rows[i]] ------------
+// One warp per output row, lanes striding the weight row in 16-byte chunks (streamed past L1), fp32 FMAs, a shuffle
+// reduction. For a subset of the head (a pruned draft vocabulary), where the rows are not tiles of the weight.
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256) w8a16_rows_kernel(const T *__restrict__ x, const int8_t *__restrict__ w,
+                                                         const float *__restrict__ s, const T *__restrict__ bias,
+                                                         T *__restrict__ out, int M, int N, int K,
+                                                         const int *__restrict__ rows) {
+    const int i = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (i >= N) return;
+    const int src = rows ? rows[i] : i;
+    const char *wr = reinterpret_cast<const char *>(w) + (size_t)src * K;
+    float acc[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) acc[m] = 0.f;
+    for (int c = lane; c < (K >> 4); c += 32) {
+        const uint4 wv = ld_stream16(wr + (size_t)c * 16);
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        float wf[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) wf[j] = (float)(int8_t)(ww[j >> 2] >> (8 * (j & 3)));
+#pragma unroll
+        for (int m = 0; m < 16; ++m) {
+            if (m >= M) break;
+            const uint4 *xr = reinterpret_cast<const uint4 *>(x + (size_t)m * K + (size_t)c * 16);
+            const uint4 a = __ldg(xr), b = __ldg(xr + 1);
+            const uint32_t xs[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            float v = acc[m];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float2 f = unpack2<T>(xs[j]);
+                v = __fmaf_rn(wf[2 * j], f.x, v);
+                v = __fmaf_rn(wf[2 * j + 1], f.y, v);
+            }
+            acc[m] = v;
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < 16; ++m)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    if (lane == 0) {
+        const float sn = s[src], bn = bias ? t2f<T>(bias[src]) : 0.f;
+#pragma unroll
+        for (int m = 0; m < 16; ++m)
+            if (m < M) out[(size_t)m * N + i] = f2t<T>(__fmaf_rn(acc[m], sn, bn));
+    }
+}
+
+// ---- host side -------------------------------------------------------------------------------------------------------
+template <int BN> inline int wh_stages(int dev) {
+    const int s = (max_smem_optin(dev) - 1024 - WH_BAR_BYTES - 1024) / WhLayout<BN>::STAGE;
+    return s > 16 ? 16 : s;
+}
+template <int BN> inline int wh_smem_bytes(int stages) { return stages * WhLayout<BN>::STAGE + 1024 + WH_BAR_BYTES; }
+
+template <typename T, int BN>
+static int launch_wh(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cudaStream_t s) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    const int stages = wh_stages<BN>(dev);
+    if (stages < 2) return VT_EARG;
+    A.t.stages = stages;
+    const int smem = wh_smem_bytes<BN>(stages);
+    static bool attr[VT_MAX_DEV] = {false};
+    if (!attr[dev]) {
+        if (cudaFuncSetAttribute(w8a16_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return (int)cudaGetLastError();
+        attr[dev] = true;
+    }
+    int g = num_sms(dev);
+    if (g > A.t.units) g = A.t.units;
+    return launch_k(w8a16_tc_kernel<T, BN>, dim3(g), dim3(WH_THREADS), smem, s, true, mw, mx, A);
+}
+
+// split-K slot bytes for M token rows on this device (one fp32 contribution of 128 x M per CTA, grid <= SMs)
+static size_t wh_slot_bytes(int M) { return tc_decode_slot_bytes(M, num_sms(cur_device())); }
+
+static bool wh_args_ok(const void *x, const void *w, const void *s, const void *out, int M, int N, int K, int ldo) {
+    return x && w && s && out && M >= 1 && M <= WH_MAX_M && N >= 1 && K >= 16 && (K & 15) == 0 && ldo >= N &&
+           ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0;
+}
+
+template <typename T>
+static int w8a16_tc(const void *x, const void *w, const float *s, const void *bias, void *out, int M, int N, int K,
+                    int ldo, void *scratch, unsigned *status, cudaStream_t st) {
+    const int BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
+    CUtensorMap mw, mx;
+    if (!tc_make_map(&mw, w, N, K, TC_BM) || !make_map_b16(&mx, x, M, K, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+        return VT_EARG;
+    WhArgs A{};
+    tc_decode_args(A.t, M, N, K);
+    A.t.l2_prefetch_blocks = 0;
+    A.t.sw = s;
+    A.t.sw_rows = 1;
+    A.t.bias = bias;
+    A.t.out = out;
+    A.t.slots = (uint4 *)scratch;
+    A.t.timeout_ns = pipe_timeout_ns();
+    A.t.status = status;
+    A.ldo = ldo;
+    if (BN == 16) return launch_wh<T, 16>(mw, mx, A, st);
+    if (BN == 32) return launch_wh<T, 32>(mw, mx, A, st);
+    return launch_wh<T, 64>(mw, mx, A, st);
+}
+
+template <typename T>
+static int w8a16_rows(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K,
+                      const int *rows, cudaStream_t st) {
+    const long long threads = (long long)N * 32;
+    w8a16_rows_kernel<T><<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(
+        (const T *)x, (const int8_t *)w, (const float *)s, (const T *)bias, (T *)out, M, N, K, rows);
+    return (int)cudaGetLastError();
+}
+
+static int w8a16_dispatch(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N,
+                          int K, int ldo, int dtype, cudaStream_t st) {
+    void *scratch;
+    unsigned *status;
+    if (int rc = ws_acquire(wh_slot_bytes(M), st, &scratch, &status)) return rc;
+    if (dtype == 0) return w8a16_tc<__half>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
+    return w8a16_tc<__nv_bfloat16>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
+}
+
+}  // namespace vt
+
+using namespace vt;
+
+extern "C" {
+
+// The reference's W8A16 GEMV entry (vllm_turing/csrc/w8a16_gemv.cu:119-123: M 1..16, K % 16 == 0, dtype 0 fp16 /
+// 1 bf16, -1 on bad arguments): here the tcgen05 kernel above. Split-K slots come from the library's per-device
+// workspace (grown outside stream capture only).
+int w8a16_gemv(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K,
+               int dtype, void *stream) {
+    if (!wh_args_ok(x, w, s, out, M, N, K, N) || M > 16) return VT_EARG;
+    return w8a16_dispatch(x, w, s, bias, out, M, N, K, N, dtype, (cudaStream_t)stream);
+}
+
+// The reference's gathered variant (w8a16_gemv.cu:125-145): with rows (int32 [N], indices of weight rows) the output
+// is [M, N] over that subset, computed by the CUDA-core kernel; without rows it is w8a16_gemv. The caller guarantees
+// that every rows[i] indexes a row of w (the reference's contract; nothing here knows the weight's row count).
+int w8a16_gemv_rows(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K,
+                    int dtype, const void *rows, void *stream) {
+    if (!rows) return w8a16_gemv(x, w, s, bias, out, M, N, K, dtype, stream);
+    if (!wh_args_ok(x, w, s, out, M, N, K, N) || M > 16) return VT_EARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (dtype == 0) return w8a16_rows<__half>(x, w, s, bias, out, M, N, K, (const int *)rows, st);
+    return w8a16_rows<__nv_bfloat16>(x, w, s, bias, out, M, N, K, (const int *)rows, st);
+}
+
+// The reference's tensor-core W8A16 entry (vllm_turing/csrc/w8a16_mma.cu:160-175: fp16 activations, M 1..64, N even,
+// -1 on bad arguments; cfg picks the reference's tiling and is accepted and ignored here).
+int w8a16_mma(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int cfg,
+              void *stream) {
+    (void)cfg;
+    if (!wh_args_ok(x, w, s, out, M, N, K, N) || (N & 1)) return VT_EARG;
+    return w8a16_dispatch(x, w, s, bias, out, M, N, K, N, 0, (cudaStream_t)stream);
+}
+
+// Zeroed workspace bytes vt_w8a16_mm needs for M token rows (256-byte status header included).
+size_t vt_w8a16_ws_bytes(int M) { return 256 + wh_slot_bytes(M < 1 ? 1 : M); }
+
+// W8A16 for M 1..64 in either dtype, with an output row stride ldo (>= N: e.g. this rank's columns of a gathered
+// [M, world * N] logits buffer) and a caller-owned workspace of vt_w8a16_ws_bytes(M) bytes, zeroed once before its
+// first use (the kernel leaves it zeroed); calls sharing a workspace must be stream-ordered. The first 256 bytes hold
+// the status word.
+int vt_w8a16_mm(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int ldo,
+                int dtype, void *workspace, size_t ws_bytes, void *stream) {
+    if (!wh_args_ok(x, w, s, out, M, N, K, ldo) || !workspace || ws_bytes < vt_w8a16_ws_bytes(M) ||
+        ((uintptr_t)workspace & 255))
+        return VT_EARG;
+    cudaStream_t st = (cudaStream_t)stream;
+    unsigned *status = (unsigned *)workspace;
+    void *scratch = (char *)workspace + 256;
+    if (dtype == 0) return w8a16_tc<__half>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
+    return w8a16_tc<__nv_bfloat16>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
+}
+
+}  // extern "C"

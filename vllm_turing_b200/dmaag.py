@@ -43,6 +43,41 @@ class DmaAllGather:
         return g.view(x.dtype).view(self.world, *x.shape)
 
 
+def all_gather_dim(comm, x, dim=-1):
+    """vLLM's all_gather(input_, dim) contract on the communicator: the ranks' tensors concatenated along `dim`.
+    Along the last dimension (vocabulary-parallel logits, column-parallel outputs) the result is written in its final
+    layout by the row-strided gather (this rank's columns copied in, the peers' filled over NVLink); along the first
+    dimension the slots are contiguous; otherwise, or when the payload exceeds the one-shot capacity, the gather
+    runs on contiguous slots and the result is rearranged like vLLM's (movedim). Returns None if not applicable."""
+    if not (x.is_contiguous() and x.dim() >= 1 and x.numel() > 0):
+        return None
+    world, rank = comm.world, comm.rank
+    nd = x.dim()
+    dim = dim + nd if dim < 0 else dim
+    esz = x.element_size()
+    m = x.numel() * esz
+    if dim == nd - 1 and nd >= 1:
+        S = x.shape[-1]
+        rows = x.numel() // S
+        if (S * esz) % 8 == 0 and m <= comm.ll_capacity:
+            out = torch.empty(*x.shape[:-1], world * S, dtype=x.dtype, device=x.device)
+            out[..., rank * S:(rank + 1) * S].copy_(x)
+            comm.all_gather_rows(out, rows, S * esz, world * S * esz)
+            return out
+    if m % 16 != 0 and not (m % 8 == 0 and m <= comm.ll_capacity):
+        return None
+    g = torch.empty(world * m, dtype=torch.uint8, device=x.device)
+    g[rank * m:(rank + 1) * m].copy_(x.view(-1).view(torch.uint8))
+    comm.all_gather(g, m)
+    out = g.view(x.dtype).view(world, *x.shape)
+    if dim == 0:
+        return out.reshape(world * x.shape[0], *x.shape[1:])
+    out = out.movedim(0, dim)
+    return out.reshape(*x.shape[:dim], world * x.shape[dim], *x.shape[dim + 1:])
+
+
 def install():
-    """Nothing to patch: the all-gather is created by the layers that use it (as in the reference, dmaag.py:1-7)."""
+    """Nothing to install here: vLLM's CudaCommunicator.all_gather / gather are routed to all_gather_dim by the
+    communicator patch (hostar.install), and layers may create a DmaAllGather themselves (the reference's
+    dmaag.py:1-7 usage)."""
     return None

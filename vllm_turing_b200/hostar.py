@@ -6,7 +6,8 @@ custom all-reduce / NCCL. On B200 every TP size 2..8 with full NVLink peer acces
 whose kernels serve every size: one-shot LL up to VLLM_TURING_LL_KB, two-shot reduce-scatter + all-gather above it,
 both CUDA-graph capturable (device-resident call counter). Other messages (odd sizes, other dtypes) and failed set-ups
 keep vLLM's path. Switches: VLLM_TURING_HAR=0 disables the module; VLLM_TURING_LL=0 disables the one-shot path;
-VLLM_TURING_CE_AR=0 disables the two-shot path.
+VLLM_TURING_CE_AR=0 disables the two-shot path. all_gather / gather (vocabulary-parallel logits, column-parallel
+outputs) go to the communicator's P2P all-gather (dmaag.all_gather_dim; VLLM_TURING_DAG=0 keeps vLLM's).
 """
 import logging
 import os
@@ -70,6 +71,30 @@ def install():
             return comm.all_reduce(input_, algo=algo)
         return orig_ar(self, input_)
 
+    from . import dmaag
+    orig_ag, orig_gather = CudaCommunicator.all_gather, CudaCommunicator.gather
+
+    def all_gather(self, input_, dim=-1):
+        comm = getattr(self, "turing_comm", None)
+        if comm is not None and dmaag.ENABLED and input_.is_cuda and \
+                input_.numel() * input_.element_size() >= dmaag.MIN_BYTES:
+            out = dmaag.all_gather_dim(comm, input_, dim)
+            if out is not None:
+                return out
+        return orig_ag(self, input_, dim)
+
+    def gather(self, input_, dst=0, dim=-1):
+        # every rank takes part in the same all-gather (the communicator's calls are collective); only dst keeps it
+        comm = getattr(self, "turing_comm", None)
+        if comm is not None and dmaag.ENABLED and input_.is_cuda and \
+                input_.numel() * input_.element_size() >= dmaag.MIN_BYTES:
+            out = dmaag.all_gather_dim(comm, input_, dim)
+            if out is not None:
+                return out if self.rank_in_group == dst else None
+        return orig_gather(self, input_, dst, dim)
+
     CudaCommunicator.__init__ = __init__
     CudaCommunicator.all_reduce = all_reduce
+    CudaCommunicator.all_gather = all_gather
+    CudaCommunicator.gather = gather
     CudaCommunicator._vllm_turing_har = True
