@@ -38,6 +38,7 @@ sys.path.insert(0, HERE)
 
 METRIC = "W8A8 linear+TP all-reduce µs/layer, TOPS & bus GB/s at 1/2/4/8 B200"
 HIDDEN, INTER = 5120, 17408
+VOCAB = 151936                   # config 4's LM head: int8 [5120 -> 151936], logits all-gathered
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 LAYERS = 64
@@ -51,7 +52,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="tokens per step (decode default 5, prefill 8192)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce", "lmhead"],
                     help="decode: the 64-layer MLP stack (the headline, config 1/2); prefill: the row-parallel layer "
                          "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant); "
                          "allreduce: config 4's size sweep, 1 KB .. 256 MB, against NCCL on the same ranks")
@@ -185,6 +186,8 @@ def run_reference(args):
     steps = max(1, min(args.steps, 20))
     if args.mode == "prefill":
         return run_reference_prefill(args, threads, steps)
+    if args.mode == "lmhead":
+        return run_reference_lmhead(args, threads, steps)
     dt, n, threads = time_oracle_layer(M, threads, budget_s=60.0, max_steps=steps)
     tops = layer_ops(M, 1) / dt / 1e12
     sample = (f"{n} full layers (M={M}, gate_up 5120->34816 + silu_mul_quant + down 17408->5120 + RMSNorm + "
@@ -231,6 +234,43 @@ def run_reference_prefill(args, threads, steps, sample_rows=256):
         "cpu_baseline": {"value": tops, "unit": "TOPS", "cores": threads, "kind": "port", "sample": sample},
         "e2e": {"value": tops, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "the reference's own path is CUDA for sm_75 only; this arm is its CPU restatement (oracle/)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def time_oracle_lmhead(M, threads, budget_s=12.0, max_steps=20, sample_rows=8192):
+    """The W8A16 LM head through the C oracle on the host cores (TP1), on a bounded sample of the vocabulary's rows
+    (the per-row work is identical); returns (seconds for the full 151936-row head, calls, rows sampled)."""
+    import torch
+    from oracle import oracle as O
+    O.set_threads(threads)
+    g = torch.Generator().manual_seed(600)
+    x = O.to_bits(torch.randn(M, HIDDEN, generator=g).to(torch.bfloat16))
+    w = torch.randint(-128, 128, (sample_rows, HIDDEN), generator=g, dtype=torch.int8).numpy()
+    sc = (torch.rand(sample_rows, generator=g) * 1e-3).numpy()
+    O.w8a16(x, w, sc, None, 1)
+    n, t0 = 0, time.perf_counter()
+    while n < max_steps and (n < 2 or time.perf_counter() - t0 < budget_s):
+        O.w8a16(x, w, sc, None, 1)
+        n += 1
+    return (time.perf_counter() - t0) / n * (VOCAB / sample_rows), n, sample_rows
+
+
+def run_reference_lmhead(args, threads, steps):
+    M = args.tokens
+    dt, n, rows = time_oracle_lmhead(M, threads, budget_s=30.0, max_steps=steps)
+    gbs = VOCAB * HIDDEN / dt / 1e9
+    sample = f"{n} W8A16 calls on {rows} of the {VOCAB} head rows (M={M}, K=5120), TP1, scaled by rows"
+    line = {
+        "metric": "int8 LM head (W8A16) + logits all-gather, us per step", "value": dt * 1e6, "unit": "us",
+        "impl": "reference", "n_gpus": args.gpus, "steps": n, "warmup": 1, "ms_per_step": dt * 1e3,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "bf16 x int8 -> fp32",
+        "data": "synthetic", "mode": "lmhead", "weight_gbs": gbs,
+        "config": {"workload": f"LM head int8 [5120 -> {VOCAB}] W8A16, M={M} (BASELINE config 4)", "tokens": M,
+                   "tp": 1, "device": "cpu"},
+        "cpu_baseline": {"value": dt * 1e6, "unit": "us", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": dt * 1e6, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference's own W8A16 kernels are CUDA; this arm is their arithmetic restated in C (oracle/)",
     }
     print(json.dumps(line), flush=True)
 
@@ -456,6 +496,167 @@ def run_prefill(args, world, rank, local, dev, gloo):
     dist.destroy_process_group()
 
 
+LMHEAD_SETS = 3   # distinct head buffers cycled by the captured step: at TP8 one shard (97 MB) would fit in L2
+
+
+def run_lmhead(args, world, rank, local, dev, gloo):
+    """Config 4's LM head: int8 [5120 -> 151936] W8A16, vocabulary-parallel over the ranks (151936 / N rows each),
+    logits all-gathered on every rank -- lmhead.logits_gathered: the tcgen05 kernel writes this rank's columns of the
+    [M, 151936] logits in place, the row-strided P2P all-gather fills the peers' columns -- captured in a CUDA graph.
+    value = us per step (lower is better)."""
+    import torch
+    import torch.distributed as dist
+
+    from vllm_turing_b200 import _build, lmhead
+    from vllm_turing_b200.comm import TPComm
+
+    _build.load()
+    M, K = args.tokens, HIDDEN
+    assert VOCAB % world == 0
+    Vs = VOCAB // world
+    g = torch.Generator().manual_seed(700 + rank)
+    x = torch.randn(M, K, generator=torch.Generator().manual_seed(701)).to(torch.bfloat16).to(dev)
+    heads = []
+    for i in range(LMHEAD_SETS):
+        w = torch.randint(-128, 128, (Vs, K), generator=g, dtype=torch.int8).to(dev)
+        sc = (torch.rand(Vs, generator=g) * 1e-3 + 1e-5).to(dev)
+        heads.append((w, sc, torch.empty(M, VOCAB, dtype=torch.bfloat16, device=dev)))
+    comm = TPComm(gloo, dev) if world > 1 else None
+    stream = torch.cuda.current_stream()
+
+    def step_set(h):
+        lmhead.logits_gathered(x, h[0], h[1], comm=comm, out=h[2])
+
+    def kernel_set(h):
+        lmhead.mm_into(h[2][:, rank * Vs:], x, h[0], h[1], None, ldo=VOCAB)
+
+    def gather_set(h):
+        if comm is not None:
+            comm.all_gather_rows(h[2], M, Vs * 2, VOCAB * 2)
+
+    def run(fn):
+        for h in heads:
+            fn(h)
+
+    def barrier():
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    def timed(fn, n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / n) / 1e3
+
+    K_steps, W = args.steps, max(args.warmup, 3)
+    for _ in range(2):
+        run(step_set)
+    barrier()
+    if comm is not None:
+        comm.check()
+    if args.profile:
+        for _ in range(W + K_steps):
+            run(step_set)
+        barrier()
+        if rank == 0:
+            print(json.dumps({"profile": True, "mode": "lmhead", "steps": K_steps}), flush=True)
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+        return
+
+    def capture(fn):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            run(fn)
+        return gr
+
+    g_step, g_kern = capture(step_set), capture(kernel_set)
+    g_gath = capture(gather_set) if comm is not None else None
+    barrier()
+    with ClockSampler(local) as clk:
+        t_w = time.perf_counter()
+        i = 0
+        while i < W or time.perf_counter() - t_w < 1.0:
+            g_step.replay()
+            i += 1
+            if i % 8 == 0:
+                torch.cuda.synchronize()
+        barrier()
+        t_step = timed(g_step.replay, K_steps) / LMHEAD_SETS
+    W = max(W, i)
+    n_k = max(1, min(K_steps, 20))
+    t_kern = timed(g_kern.replay, n_k) / LMHEAD_SETS
+    t_gath = timed(g_gath.replay, n_k) / LMHEAD_SETS if g_gath is not None else 0.0
+    if comm is not None:
+        comm.check()
+
+    # end to end: the hidden states from pinned host memory, the gathered logits read back (what the sampler takes)
+    e2e = None
+    if not args.no_e2e:
+        h_x = x.cpu().pin_memory()
+        o_l = torch.empty(M, VOCAB, dtype=torch.bfloat16).pin_memory()
+        g1 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g1):
+            step_set(heads[0])
+
+        def e2e_step():
+            x.copy_(h_x, non_blocking=True)
+            g1.replay()
+            o_l.copy_(heads[0][2], non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        t_e2e = timed(e2e_step, n_k)
+        e2e = {"value": t_e2e * 1e6, "unit": "us", "h2d_bytes_per_step": int(h_x.numel() * 2),
+               "d2h_bytes_per_step": int(o_l.numel() * 2),
+               "api": "lmhead.logits_gathered (vt_w8a16_mm + vt_all_gather_rows), captured; host copies"}
+        del g1
+
+    # roofline: the W8A16 kernel streams this rank's head once per call (HBM bound at decode M)
+    alg = Vs * K + Vs * 4 + M * K * 2 + M * Vs * 2   # weights, row scales, activations, logits
+    hbm_peak, pk = peaks()
+    ach = alg / t_kern / 1e9
+    tr = read_traffic().get(f"w8a16_tp{world}_m{M}")
+    roof = {"bound": "hbm", "kernel": "w8a16_tc_kernel", "achieved": ach, "peak": hbm_peak, "unit": "GB/s",
+            "frac": ach / hbm_peak, "traffic": tr, "alg_bytes": alg, "peak_kind": pk}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dt, n, rows = time_oracle_lmhead(M, cpu_cores())
+        cpu = {"value": dt * 1e6, "unit": "us", "cores": cpu_cores(), "kind": "port",
+               "sample": f"{n} W8A16 calls on {rows} of the {VOCAB} head rows (M={M}), C oracle, scaled by rows"}
+    line = {
+        "metric": "int8 LM head (W8A16) + logits all-gather, us per step", "value": t_step * 1e6, "unit": "us",
+        "n_gpus": world, "steps": K_steps, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 x int8 -> fp32", "data": "synthetic",
+        "mode": "lmhead", "weight_gbs": Vs * K / t_kern / 1e9,
+        "config": {"workload": f"LM head int8 [5120 -> {VOCAB}] W8A16, vocabulary-parallel, logits all-gathered "
+                               f"(BASELINE config 4), M={M}", "tokens": M, "tp": world, "rows_per_rank": Vs,
+                   "l2": "inputs larger than L2 (three head buffer sets cycled)", "launch": "CUDA graph",
+                   "parallelism": f"tp{world}"},
+        "kernel_us": {"w8a16": t_kern * 1e6, "all_gather_rows": t_gath * 1e6},
+        "roofline": roof, "clocks": clk.summary(),
+        "gpu_launches": LMHEAD_SETS * K_steps * (2 if world > 1 else 1), "e2e": e2e, "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del g_step, g_kern, g_gath
+    if comm is not None:
+        comm.close()
+    dist.destroy_process_group()
+
+
 def run_allreduce(args, world, rank, local, dev, gloo):
     """Config 4's all-reduce sweep: bf16 messages of 1 KB .. 256 MB through TPComm.all_reduce (one-shot LL up to the
     LL capacity, two-shot above) and through NCCL (torch.distributed, the library baseline) on the same ranks. Each
@@ -556,6 +757,8 @@ def main():
         return run_prefill(args, world, rank, local, dev, gloo)
     if args.mode == "allreduce":
         return run_allreduce(args, world, rank, local, dev, gloo)
+    if args.mode == "lmhead":
+        return run_lmhead(args, world, rank, local, dev, gloo)
     _build.load()
     M = args.tokens
     NL = args.layers

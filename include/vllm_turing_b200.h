@@ -170,6 +170,16 @@ unsigned vt_comm_status(void *comm, int clear);
 /* Number of completed calls on this communicator (device counter); synchronises the device. */
 unsigned vt_comm_seq(void *comm);
 
+/* AR8, the optional lossy all-reduce (VLLM_TURING_AR8=1): x fp16 [n] -> packed [n int8 | n / 128 fp16 scales], one
+ * scale per 128 values (amax / 127 rounded to fp16), q = clamp(rint(x / scale), -127, 127); n % 128 == 0, x 16-byte and
+ * packed 8-byte aligned. Replaces ar8_quant (host_ar.cu:182-188). */
+int ar8_quant(const void *x, void *packed, int n, void *stream);
+/* out fp16 [n] = the rank-ordered float32 sum of the dequantised packed blocks of two ranks (gathered = 2 blocks of
+ * n + n / 64 bytes); n % 512 == 0. Replaces ar8_dequant_sum (host_ar.cu:190-201). */
+int ar8_dequant_sum(const void *gathered, void *out, int n, void *stream);
+/* The same for 1..8 ranks. New entry. */
+int vt_ar8_dequant_sum(const void *gathered, void *out, long long n, int world, void *stream);
+
 /* out[n] = sum over ranks of in[n], float32 accumulation in rank order, one rounding (the arithmetic of
  * host_ar.cu:90-101). algo 0 auto, 1 one-shot LL (n % 4 == 0, up to ll_data), 2 two-shot (n % 8 == 0).
  * in may equal out; 16-byte aligned. One rank: no kernel (a device-to-device copy when in != out). Replaces

@@ -44,6 +44,8 @@ def lib():
             "orc_all_gather": [_P, _I, _P, _L],
             "orc_lmhead_quant": [_P, _P, _P, _I, _I, _I],
             "orc_w8a16": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I],
+            "orc_ar8_quant": [_P, _P, _L],
+            "orc_ar8_dequant_sum": [_P, _P, _L, _I],
             "orc_set_threads": [_I],
             "orc_num_threads": [],
         }
@@ -246,3 +248,24 @@ def w8a16_close(got_bits, want_bits, mag, s, dtype=1, rel_sum=2.0 ** -16):
     ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(w), 1e-30))) - (mant - 1))
     tol = ulp + rel_sum * np.abs(np.asarray(s, np.float64).reshape(1, -1)) * mag
     return float(np.max(np.abs(g - w) / np.maximum(tol, 1e-30))) if g.size else 0.0
+
+
+def ar8_quant(x_bits):
+    """uint8 packed block [n + n / 64] of fp16 bits x [n] (n % 128 == 0): int8 values, then fp16 scales per 128
+    (vllm_turing/csrc/host_ar.cu:138-160)."""
+    x_bits = np.ascontiguousarray(x_bits, np.uint16).reshape(-1)
+    n = x_bits.size
+    packed = np.empty(n + n // 64, np.uint8)
+    lib().orc_ar8_quant(_p(x_bits), _p(packed), n)
+    return packed
+
+
+def ar8_dequant_sum(blocks):
+    """fp16 bits [n] = rank-ordered float32 sum of the dequantised packed blocks (host_ar.cu:163-180)."""
+    blocks = [np.ascontiguousarray(b, np.uint8) for b in blocks]
+    blk = blocks[0].size
+    n = blk * 64 // 65
+    g = np.ascontiguousarray(np.concatenate(blocks))
+    out = np.empty(n, np.uint16)
+    lib().orc_ar8_dequant_sum(_p(g), _p(out), n, len(blocks))
+    return out

@@ -351,3 +351,48 @@ void orc_w8a16(const uint16_t *x, const int8_t *w, const float *s, const uint16_
         }
     }
 }
+
+/* ---- AR8: the compressed all-reduce (optional, lossy) -------------------------------------------------------------
+ * Reference: vllm_turing/csrc/host_ar.cu:133-201. Packed block of n fp16 values (n % 128 == 0): n int8, then n / 128
+ * fp16 scales. Per 128-element group: amax = max |x|; sc = fp16(amax / 127) (float32 division, round to nearest
+ * even); inv = sc > 0 ? 1 / (float)sc : 0; q = clamp(rint(x * inv), -127, 127) (host_ar.cu:138-160). */
+void orc_ar8_quant(const uint16_t *x, uint8_t *packed, long n) {
+    int8_t *q = (int8_t *)packed;
+    uint16_t *sc = (uint16_t *)(packed + n);
+    const long ng = n / 128;
+#pragma omp parallel for schedule(static)
+    for (long g = 0; g < ng; ++g) {
+        float amax = 0.0f;
+        for (int j = 0; j < 128; ++j) {
+            const float v = fabsf(f16_to_f(x[g * 128 + j]));
+            amax = v > amax ? v : amax;
+        }
+        const uint16_t sh = f_to_f16(amax / 127.0f);
+        const float s = f16_to_f(sh);
+        const float inv = s > 0.0f ? 1.0f / s : 0.0f;
+        for (int j = 0; j < 128; ++j) {
+            float r = rintf(f16_to_f(x[g * 128 + j]) * inv);
+            r = r < -127.0f ? -127.0f : (r > 127.0f ? 127.0f : r);
+            q[g * 128 + j] = (int8_t)r;
+        }
+        sc[g] = sh;
+    }
+}
+
+/* out[i] = fp16(sum over ranks r = 0..world-1 in order of q_r[i] * sc_r[i / 128]) with float32 additions; gathered =
+ * world packed blocks of n + n / 64 bytes. Reference: ar8_dequant_sum_kernel (host_ar.cu:163-180), two ranks:
+ * `u * a0 + w * a1` -- both products are exact in float32, so its one rounding is the oracle's. */
+void orc_ar8_dequant_sum(const uint8_t *gathered, uint16_t *out, long n, int world) {
+    const long blk = n + n / 64;
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < n; ++i) {
+        float acc = 0.0f;
+        for (int r = 0; r < world; ++r) {
+            const int8_t *q = (const int8_t *)(gathered + r * blk);
+            const uint16_t *sc = (const uint16_t *)(gathered + r * blk + n);
+            const float p = (float)q[i] * f16_to_f(sc[i / 128]);
+            acc = r == 0 ? p : acc + p;
+        }
+        out[i] = f_to_f16(acc);
+    }
+}

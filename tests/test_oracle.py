@@ -168,3 +168,42 @@ def test_w8a16_matches_reference_large_m_path(golden):
     got = O.bits_to_float(out, 0).astype(np.float64)
     ref = O.bits_to_float(golden["lmbig_out"], 0).astype(np.float64)
     assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 2e-3
+
+
+def _ar8_torch(x):
+    """The reference's AR8 quantiser (vllm_turing/csrc/host_ar.cu:138-160) restated with torch CPU ops: an independent
+    check of the C oracle."""
+    g = x.float().view(-1, 128)
+    sh = (g.abs().amax(1) / 127.0).half()
+    sc = sh.float()
+    inv = torch.where(sc > 0, 1.0 / sc, torch.zeros_like(sc))
+    q = torch.round(g * inv[:, None]).clamp(-127, 127).to(torch.int8)
+    return q.view(-1), sh
+
+
+def test_ar8_quant_and_sum():
+    g = torch.Generator().manual_seed(8)
+    xs = [(torch.randn(2048, generator=g) * 3).half() for _ in range(4)]
+    xs[0][:128] = 0                                    # an all-zero group: scale 0, values 0
+    xs[1][128:256] *= 1e-4                             # tiny values: a subnormal fp16 scale
+    xs[2][256] = 6e4                                   # a near-overflow value
+    blocks = []
+    for x in xs:
+        b = O.ar8_quant(O.to_bits(x))
+        q, sh = _ar8_torch(x)
+        assert np.array_equal(b[:2048].view(np.int8), q.numpy())
+        assert np.array_equal(b[2048:].view(np.uint16), O.to_bits(sh))
+        blocks.append(b)
+    for w in (1, 2, 4):
+        out = O.from_bits(O.ar8_dequant_sum(blocks[:w]), torch.float16).float()
+        deq = [torch.from_numpy(b[:2048].view(np.int8).copy()).float().view(-1, 128) *
+               O.from_bits(b[2048:].view(np.uint16).copy(), torch.float16).float()[:, None] for b in blocks[:w]]
+        acc = deq[0]
+        for d in deq[1:]:
+            acc = acc + d                              # float32, rank order
+        assert torch.equal(out, acc.view(-1).half().float())
+        # error bound of the lossy format: half a scale step per rank
+        ref = sum(x.float() for x in xs[:w])
+        step = sum(O.from_bits(b[2048:].view(np.uint16).copy(), torch.float16).float().repeat_interleave(128)
+                   for b in blocks[:w])
+        assert ((out - ref).abs() <= step / 2 + ref.abs() * 2e-3 + 1e-6).all()

@@ -100,6 +100,16 @@ def test_allreduce_algorithm_choice():
     assert hostar.choose_algo(c, torch.empty(5 * 5120, dtype=torch.bfloat16)) == 1       # 51 KB: one-shot
     assert hostar.choose_algo(c, torch.empty(8192 * 5120, dtype=torch.bfloat16)) == 2    # 84 MB: two-shot
     assert hostar.choose_algo(c, torch.empty(5121, dtype=torch.bfloat16)) == 0           # odd: vLLM's path
+    # AR8 (VLLM_TURING_AR8=1): large fp16 messages only, above the one-shot size
+    c.ar8_ok = lambda t: t.dtype == torch.float16 and t.numel() % 1024 == 0
+    old = hostar.AR8
+    try:
+        hostar.AR8 = True
+        assert hostar.choose_algo(c, torch.empty(8192 * 5120, dtype=torch.float16)) == 3
+        assert hostar.choose_algo(c, torch.empty(8192 * 5120, dtype=torch.bfloat16)) == 2
+        assert hostar.choose_algo(c, torch.empty(5 * 5120, dtype=torch.float16)) == 1
+    finally:
+        hostar.AR8 = old
 
 
 def test_synthetic_inputs_are_deterministic():

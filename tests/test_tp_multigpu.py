@@ -3,6 +3,7 @@ torch.multiprocessing.spawn, a gloo group for set-up, tests/test_hostar.py:13-20
   - one-shot and two-shot all-reduce bit-exact to the rank-ordered float32 sum (tests/bench_devll.py:28-36 for 2 ranks)
     at decode / odd / prefill sizes, fp16 and bf16, identical on every rank;
   - all-gather (LL and bulk, contiguous slots and row-strided along the last dimension) exact;
+  - AR8 (int8 + fp16 scale per 128 values, all-gathered, rank-ordered sum) bit-exact to the oracle;
   - the int8 LM head's vocabulary-parallel logits at config 4's TP8 shard (151936 / 8 rows x 5120) gathered in place
     on every rank, within the W8A16 tolerance of the oracle;
   - the fused GEMV + all-reduce + residual + RMSNorm + quant at BASELINE config 0 (M=16, K_local=8704, N=5120) and
@@ -79,6 +80,14 @@ def _worker(rank, world, port, q):
             for r in range(world):
                 exp = (r * 37 + torch.arange(m) % 251).to(torch.uint8)
                 check(torch.equal(g[r * m:(r + 1) * m].cpu(), exp), f"all_gather m={m} slot {r}")
+
+        # ---- AR8 (the optional lossy all-reduce): bit-exact to the oracle's rank-ordered sum, same on every rank ----
+        for n in (8192 * 5120 // 8, 1024 * 40):
+            xs8 = [(torch.randn(n, generator=torch.Generator().manual_seed(900 + r)) * 2).half() for r in range(world)]
+            y = comm.all_reduce_ar8(xs8[rank].to(dev))
+            torch.cuda.synchronize()
+            want = O.ar8_dequant_sum([O.ar8_quant(O.to_bits(x)) for x in xs8])
+            check(np.array_equal(O.to_bits(y.cpu()), want), f"ar8 all-reduce n={n}")
 
         # ---- row-strided all-gather, and the int8 LM head's vocabulary-parallel logits gathered in place ----
         from vllm_turing_b200 import dmaag, lmhead

@@ -20,7 +20,7 @@ _csrc = os.path.join(_here, "csrc")
 _include = os.path.join(os.path.dirname(_here), "include")
 LIB_NAME = "libvllm_turing_b200.so"
 LIB_PATH = os.path.join(_here, LIB_NAME)
-SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "w8a16_tc.cu", "norm_quant.cu", "tp_comm.cu",
+SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "w8a16_tc.cu", "norm_quant.cu", "ar8.cu", "tp_comm.cu",
            "tp_fused.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 _lib = None
@@ -126,6 +126,9 @@ SIGNATURES = {
     "vt_scaled_int8_quant": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_rms_norm_quant": (_I, [_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _P]),
     "silu_mul_quant": (_I, [_P, _P, _P, _I, _I, _P]),
+    "ar8_quant": (_I, [_P, _P, _I, _P]),
+    "ar8_dequant_sum": (_I, [_P, _P, _I, _P]),
+    "vt_ar8_dequant_sum": (_I, [_P, _P, _LL, _I, _P]),
     "vt_silu_mul_quant": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "ce_alloc": (_I, [_SZ, ctypes.POINTER(ctypes.c_void_p), _P]),
     "ce_open": (_I, [_P, ctypes.POINTER(ctypes.c_void_p)]),

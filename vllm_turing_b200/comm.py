@@ -160,6 +160,37 @@ class TPComm:
             raise CommError(f"vt_all_gather failed: {rc}")
         return gathered
 
+    def ar8_ok(self, t):
+        """AR8 applies to fp16 messages of n % 1024 == 0 elements (each packed block n + n / 64 bytes, a multiple of
+        16, so the gather takes whole 16-byte words)."""
+        return t.is_cuda and t.dtype == torch.float16 and t.is_contiguous() and t.numel() % 1024 == 0 and \
+            t.data_ptr() % 16 == 0
+
+    def all_reduce_ar8(self, t, out=None):
+        """The reference's optional lossy all-reduce (AR8, vllm_turing/hostar.py:40-96, csrc/host_ar.cu:133-201) for
+        any rank count: int8 + an fp16 scale per 128 values, all-gathered over the P2P kernels, every rank summing the
+        dequantised blocks of all ranks in rank order (identical results on every rank). The packed blocks live in a
+        persistent per-communicator buffer, grown outside graph capture only."""
+        n = t.numel()
+        m = n + n // 64
+        need = self.world * m
+        buf = getattr(self, "_ar8_buf", None)
+        if buf is None or buf.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise CommError("vllm_turing_b200: AR8 scratch must grow before graph capture")
+            buf = self._ar8_buf = torch.empty(need, dtype=torch.uint8, device=t.device)
+        if out is None:
+            out = torch.empty_like(t)
+        st = torch.cuda.current_stream().cuda_stream
+        rc = self.L.ar8_quant(t.data_ptr(), buf.data_ptr() + self.rank * m, n, st)
+        if rc != 0:
+            raise CommError(f"ar8_quant failed: {rc}")
+        self.all_gather(buf, m)
+        rc = self.L.vt_ar8_dequant_sum(buf.data_ptr(), out.data_ptr(), n, self.world, st)
+        if rc != 0:
+            raise CommError(f"vt_ar8_dequant_sum failed: {rc}")
+        return out
+
     def all_gather_rows(self, gathered, rows, row_bytes, ld_bytes):
         """gathered: [rows, ld_bytes] device buffer holding world column blocks of row_bytes per row, this rank's
         block pre-written; fills the peers' blocks (one-shot LL; rows * row_bytes within ll_capacity)."""

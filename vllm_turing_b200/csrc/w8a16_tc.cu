@@ -47,10 +47,13 @@
 
 namespace vt {
 
-constexpr int WH_THREADS = 320;             // 10 warps: producer, MMA, 4 epilogue, 4 converter
-constexpr int WH_AS = 4;                    // A stages in TMEM, one K block (128 elements = 64 columns) each
+// warps: 0 producer, 1 MMA, 2..5 epilogue, 6.. converters: NW per TMEM lane quarter, taking whole K blocks in turn
+// (converter slot i of a quarter converts blocks i, i + NW, ...), so the per-block latency chain of one warp (shared
+// loads, conversion, tcgen05.st, tcgen05.wait::st, the arrival) overlaps with the other slots' blocks
+__host__ __device__ constexpr int wh_threads(int nw) { return 32 * (6 + 4 * nw); }
+constexpr int WH_AS = 6;                    // A stages in TMEM, one K block (128 elements = 64 columns) each
 constexpr int WH_ACOL = 128;                // first TMEM column of the A stages (the accumulators use columns < 128)
-constexpr int WH_TMEM_COLS = 512;           // WH_ACOL + WH_AS * 64 = 384, rounded up to a power of two
+constexpr int WH_TMEM_COLS = 512;           // WH_ACOL + WH_AS * 64 = 512
 constexpr int WH_W_BYTES = TC_BM * TC_BK;   // int8 weights of one K block: 128 rows x 128 bytes
 constexpr int WH_BAR_BYTES = 512;
 constexpr int WH_MAX_M = 64;
@@ -122,8 +125,8 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, uint64
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, deadline)) != 0;
 }
 
-template <typename T, int BN>
-__global__ void __launch_bounds__(WH_THREADS, 1)
+template <typename T, int BN, int NW>
+__global__ void __launch_bounds__(wh_threads(NW), 1)
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const WhArgs A) {
     using Lay = WhLayout<BN>;
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(WH_THREADS, 1)
     const int S = P.stages;
     uint64_t *full = reinterpret_cast<uint64_t *>(tiles + (size_t)S * Lay::STAGE);
     uint64_t *empty = full + S;
-    uint64_t *afull = empty + S;        // [WH_AS] converted K block in TMEM (4 converter warps arrive)
+    uint64_t *afull = empty + S;        // [WH_AS] converted K block in TMEM (one converter warp per quarter arrives)
     uint64_t *aempty = afull + WH_AS;   // [WH_AS] the MMAs reading it completed (commit)
     uint64_t *tfull = aempty + WH_AS;   // [2]
     uint64_t *tempty = tfull + 2;       // [2]
@@ -234,6 +237,7 @@ __global__ void __launch_bounds__(WH_THREADS, 1)
                     flags[0] = 1;
                 }
                 tc_fence_after();
+                static_assert(2 * BN <= WH_ACOL, "accumulators overlap the A stages");
                 const uint32_t d = tmem_base + (uint32_t)(buf * BN);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     if (flags[0]) break;   // aborted: issue nothing more
@@ -265,6 +269,7 @@ __global__ void __launch_bounds__(WH_THREADS, 1)
     } else if (warp >= 6) {
         // ---------------- converters: int8 rows (shared memory) -> 16-bit rows (TMEM) ----------------
         const int q = warp & 3;
+        const int slot = (warp - 6) >> 2;   // this warp converts the blocks it with it % NW == slot
         const int row = q * 32 + lane;
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)WH_ACOL;
         int it = 0;
@@ -272,6 +277,7 @@ __global__ void __launch_bounds__(WH_THREADS, 1)
         TcPieces pc(P);
         while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
             for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                if (it % NW != slot) continue;
                 const int s = it % S, a = it % WH_AS;
                 // warp-uniform decisions only: tcgen05.st below is a whole-warp instruction
                 const bool aborted = __any_sync(0xffffffffu, flags[0] != 0);
@@ -286,17 +292,20 @@ __global__ void __launch_bounds__(WH_THREADS, 1)
                 }
                 tc_fence_after();   // the MMAs that read this A stage before have completed
                 const unsigned char *src = tiles + (size_t)s * Lay::STAGE + row * TC_BK;
+                uint4 v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)   // the row's 128 bytes; 16-byte chunk j sits at chunk j ^ (row % 8)
+                    v[j] = *reinterpret_cast<const uint4 *>(src + ((j ^ (row & 7)) << 4));
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     uint32_t o[32];
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        const int j = h * 4 + c;   // 16-byte chunk j of the row sits at chunk j ^ (row % 8)
-                        const uint4 v = *reinterpret_cast<const uint4 *>(src + ((j ^ (row & 7)) << 4));
-                        cvt_word<T>(v.x, o[8 * c + 0], o[8 * c + 1]);
-                        cvt_word<T>(v.y, o[8 * c + 2], o[8 * c + 3]);
-                        cvt_word<T>(v.z, o[8 * c + 4], o[8 * c + 5]);
-                        cvt_word<T>(v.w, o[8 * c + 6], o[8 * c + 7]);
+                        const uint4 w = v[h * 4 + c];
+                        cvt_word<T>(w.x, o[8 * c + 0], o[8 * c + 1]);
+                        cvt_word<T>(w.y, o[8 * c + 2], o[8 * c + 3]);
+                        cvt_word<T>(w.z, o[8 * c + 4], o[8 * c + 5]);
+                        cvt_word<T>(w.w, o[8 * c + 6], o[8 * c + 7]);
                     }
                     tmem_st32(lane_base + (uint32_t)(a * 64 + h * 32), o);
                 }
@@ -462,8 +471,8 @@ template <int BN> inline int wh_stages(int dev) {
 }
 template <int BN> inline int wh_smem_bytes(int stages) { return stages * WhLayout<BN>::STAGE + 1024 + WH_BAR_BYTES; }
 
-template <typename T, int BN>
-static int launch_wh(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cudaStream_t s) {
+template <typename T, int BN, int NW>
+static int launch_wh_nw(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cudaStream_t s) {
     const int dev = cur_device();
     if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
     const int stages = wh_stages<BN>(dev);
@@ -472,14 +481,34 @@ static int launch_wh(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cud
     const int smem = wh_smem_bytes<BN>(stages);
     static bool attr[VT_MAX_DEV] = {false};
     if (!attr[dev]) {
-        if (cudaFuncSetAttribute(w8a16_tc_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        if (cudaFuncSetAttribute(w8a16_tc_kernel<T, BN, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return (int)cudaGetLastError();
         attr[dev] = true;
     }
     int g = num_sms(dev);
     if (g > A.t.units) g = A.t.units;
-    return launch_k(w8a16_tc_kernel<T, BN>, dim3(g), dim3(WH_THREADS), smem, s, true, mw, mx, A);
+    return launch_k(w8a16_tc_kernel<T, BN, NW>, dim3(g), dim3(wh_threads(NW)), smem, s, true, mw, mx, A);
+}
+
+// Converter warps per TMEM lane quarter: VLLM_TURING_W8A16_NW = 1, 2 or 3 (default 2; 3 only up to 32 token rows).
+inline int w8a16_nw() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_W8A16_NW");
+        const int x = e ? atoi(e) : 2;
+        v = (x == 1 || x == 3) ? x : 2;
+    }
+    return v;
+}
+
+template <typename T, int BN>
+static int launch_wh(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cudaStream_t s) {
+    const int nw = w8a16_nw();
+    if (nw == 1) return launch_wh_nw<T, BN, 1>(mw, mx, A, s);
+    if constexpr (BN <= 32)   // 64 token rows: the epilogue's registers leave room for 14 warps, not 18
+        if (nw == 3) return launch_wh_nw<T, BN, 3>(mw, mx, A, s);
+    return launch_wh_nw<T, BN, 2>(mw, mx, A, s);
 }
 
 // split-K slot bytes for M token rows on this device (one fp32 contribution of 128 x M per CTA, grid <= SMs)

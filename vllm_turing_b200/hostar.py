@@ -6,7 +6,8 @@ custom all-reduce / NCCL. On B200 every TP size 2..8 with full NVLink peer acces
 whose kernels serve every size: one-shot LL up to VLLM_TURING_LL_KB, two-shot reduce-scatter + all-gather above it,
 both CUDA-graph capturable (device-resident call counter). Other messages (odd sizes, other dtypes) and failed set-ups
 keep vLLM's path. Switches: VLLM_TURING_HAR=0 disables the module; VLLM_TURING_LL=0 disables the one-shot path;
-VLLM_TURING_CE_AR=0 disables the two-shot path. all_gather / gather (vocabulary-parallel logits, column-parallel
+VLLM_TURING_CE_AR=0 disables the two-shot path; VLLM_TURING_AR8=1 sends large fp16 messages through the lossy int8
+all-reduce (comm.all_reduce_ar8). all_gather / gather (vocabulary-parallel logits, column-parallel
 outputs) go to the communicator's P2P all-gather (dmaag.all_gather_dim; VLLM_TURING_DAG=0 keeps vLLM's).
 """
 import logging
@@ -18,6 +19,9 @@ logger = logging.getLogger("vllm.turing")
 ENABLED = os.environ.get("VLLM_TURING_HAR", "1") != "0"
 LL_ENABLED = os.environ.get("VLLM_TURING_LL", "1") != "0"
 CE_ENABLED = os.environ.get("VLLM_TURING_CE_AR", "1") != "0"
+# lossy int8 all-reduce for large messages (the reference's VLLM_TURING_AR8=1, hostar.py:40-44; off by default). On
+# NVLink it moves fewer bytes than the two-shot only at two ranks: (w - 1) (1 + 1/64) n vs 2 (w - 1) / w * 2n bytes.
+AR8 = os.environ.get("VLLM_TURING_AR8", "0") == "1"
 
 
 def peer_ok(n=None):
@@ -26,12 +30,14 @@ def peer_ok(n=None):
 
 
 def choose_algo(comm, t):
-    """0: not ours (vLLM's path), 1: one-shot, 2: two-shot."""
+    """0: not ours (vLLM's path), 1: one-shot, 2: two-shot, 3: AR8 (lossy, opt-in)."""
     if comm is None or not comm.should_use(t):
         return 0
     nbytes = t.numel() * t.element_size()
     if LL_ENABLED and nbytes <= comm.ll_bytes:
         return 1
+    if AR8 and comm.ar8_ok(t):   # above the one-shot size, as the reference (ar8_ok: numel * 2 > SLOT_BYTES)
+        return 3
     if CE_ENABLED:
         return 2
     return 0
@@ -67,6 +73,8 @@ def install():
     def all_reduce(self, input_):
         comm = getattr(self, "turing_comm", None)
         algo = choose_algo(comm, input_)
+        if algo == 3:
+            return comm.all_reduce_ar8(input_)
         if algo:
             return comm.all_reduce(input_, algo=algo)
         return orig_ar(self, input_)
