@@ -47,22 +47,27 @@
 
 namespace vt {
 
-// warps: 0 producer, 1 MMA, 2..5 epilogue, 6.. converters: NW per TMEM lane quarter, taking whole K blocks in turn
-// (converter slot i of a quarter converts blocks i, i + NW, ...), so the per-block latency chain of one warp (shared
-// loads, conversion, tcgen05.st, tcgen05.wait::st, the arrival) overlaps with the other slots' blocks
-__host__ __device__ constexpr int wh_threads(int nw) { return 32 * (6 + 4 * nw); }
+// warps: 0 weight producer, 1 MMA, 2..5 epilogue, 6 activation producer, 7.. converters: NW per TMEM lane quarter,
+// taking whole K blocks in turn (converter slot i of a quarter converts blocks i, i + NW, ...), so the per-block
+// latency chain of one warp (shared loads, conversion, tcgen05.st, tcgen05.wait::st, the arrival) overlaps with the
+// other slots' blocks
+constexpr int WH_CONV0 = 7;                 // first converter warp
+__host__ __device__ constexpr int wh_threads(int nw) { return 32 * (WH_CONV0 + 4 * nw); }
 constexpr int WH_AS = 6;                    // A stages in TMEM, one K block (128 elements = 64 columns) each
 constexpr int WH_ACOL = 128;                // first TMEM column of the A stages (the accumulators use columns < 128)
 constexpr int WH_TMEM_COLS = 512;           // WH_ACOL + WH_AS * 64 = 512
 constexpr int WH_W_BYTES = TC_BM * TC_BK;   // int8 weights of one K block: 128 rows x 128 bytes
-constexpr int WH_BAR_BYTES = 512;
-constexpr int WH_AS_SMEM = 3;               // A stages in shared memory (the ASMEM form), 32 KB each
-constexpr int WH_A_BYTES = TC_BM * 256;     // one K block of 16-bit weights: 128 rows x 128 elements, two atoms
+constexpr int WH_BAR_BYTES = 1024;
 constexpr int WH_MAX_M = 64;
 
+// Shared memory: a ring of weight stages (16 KB each) and a separate ring of activation stages (the K block's two
+// 64-element swizzle atoms of BN rows). The weight stage is released as soon as the converters have read it, so the
+// bytes in flight from HBM are limited by the ring alone -- with weights and activations in one stage, a stage stayed
+// occupied through the conversion and the MMAs as well, and at HBM latency under load that halved the stream.
 template <int BN> struct WhLayout {
-    static constexpr int X_ATOM = BN * 128;   // one 64-element, BN-row swizzle atom of the activations
-    static constexpr int STAGE = WH_W_BYTES + 2 * X_ATOM;
+    static constexpr int X_ATOM = BN * 128;            // one 64-element, BN-row swizzle atom of the activations
+    static constexpr int X_STAGE = 2 * X_ATOM;
+    static constexpr int XS = X_STAGE * 8 <= 32768 ? 8 : 4;   // activation stages: 32 KB (64 KB at BN = 64)
 };
 
 struct WhArgs {
@@ -80,19 +85,6 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// D (TMEM, fp32) (+)= A (shared-memory descriptor) . B (shared-memory descriptor)^T, kind::f16
-__device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                            uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-// generic-proxy shared-memory writes made visible to the tensor core (async proxy)
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
 // Instruction descriptor, kind::f16: fp32 accumulator (bits 4-5 = 1), A and B both bf16 (bits 7-9, 10-12 = 1) or
 // both fp16 (0), both K-major, MMA M x N.
 template <typename T> __host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
@@ -140,26 +132,24 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, uint64
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, deadline)) != 0;
 }
 
-// ASMEM: the converted weights go to a ring of shared-memory A stages (128-byte-swizzled K-major, the layout TMA
-// writes for the int8 kernels) and the MMA reads both operands through descriptors; otherwise they go to TMEM and the
-// MMA reads A from there.
-template <typename T, int BN, int NW, bool ASMEM>
+template <typename T, int BN, int NW>
 __global__ void __launch_bounds__(wh_threads(NW), 1)
     w8a16_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                     const WhArgs A) {
     using Lay = WhLayout<BN>;
-    constexpr int NAS = ASMEM ? WH_AS_SMEM : WH_AS;   // A stages
-    constexpr int TCOLS = ASMEM ? (2 * BN < 32 ? 32 : 2 * BN) : WH_TMEM_COLS;
+    constexpr int XS = Lay::XS;
     const TcArgs &P = A.t;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *tiles = tc_align1024(smem_raw);
-    const int S = P.stages;
-    unsigned char *astages = tiles + (size_t)S * Lay::STAGE;   // ASMEM: NAS x 32 KB, 1024-byte aligned
-    uint64_t *full = reinterpret_cast<uint64_t *>(astages + (ASMEM ? (size_t)NAS * WH_A_BYTES : 0));
-    uint64_t *empty = full + S;
-    uint64_t *afull = empty + S;        // [NAS] converted K block ready (one converter warp per quarter arrives)
-    uint64_t *aempty = afull + NAS;     // [NAS] the MMAs reading it completed (commit)
-    uint64_t *tfull = aempty + NAS;     // [2]
+    unsigned char *wring = tc_align1024(smem_raw);
+    const int S = P.stages;                                              // weight stages
+    unsigned char *xring = wring + (size_t)S * WH_W_BYTES;               // XS activation stages, 1024-aligned
+    uint64_t *wfull = reinterpret_cast<uint64_t *>(xring + (size_t)XS * Lay::X_STAGE);
+    uint64_t *wempty = wfull + S;       // [S] the 4 converter warps of the block read it
+    uint64_t *xfull = wempty + S;       // [XS]
+    uint64_t *xempty = xfull + XS;      // [XS] the MMAs reading it completed (commit)
+    uint64_t *afull = xempty + XS;      // [WH_AS] converted K block in TMEM (one converter warp per quarter arrives)
+    uint64_t *aempty = afull + WH_AS;   // [WH_AS] the MMAs reading it completed (commit)
+    uint64_t *tfull = aempty + WH_AS;   // [2]
     uint64_t *tempty = tfull + 2;       // [2]
     uint64_t *drain = tempty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
@@ -169,10 +159,14 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], 4);
         }
-        for (int a = 0; a < NAS; ++a) {
+        for (int t = 0; t < XS; ++t) {
+            mbar_init(&xfull[t], 1);
+            mbar_init(&xempty[t], 1);
+        }
+        for (int a = 0; a < WH_AS; ++a) {
             mbar_init(&afull[a], 4);
             mbar_init(&aempty[a], 1);
         }
@@ -187,66 +181,81 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
         tma_prefetch_desc(&tmap_x);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TCOLS);
+        tmem_alloc(tmem_slot, WH_TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
-    // only the producer runs ahead of the previous kernel: the weights and scales are no kernel's output
-    const bool producer = (warp == 0 && lane == 0);
-    if (!producer) pdl_wait();
+    // only the weight producer runs ahead of the previous kernel: the weights and scales are no kernel's output
+    const bool wproducer = (warp == 0 && lane == 0);
+    if (!wproducer) pdl_wait();
     uint64_t deadline = globaltimer() + P.timeout_ns;
 
     int ta, tb, kb0, kb1;
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- weight producer (TMA) ----------------
         if (lane == 0) {
             const uint64_t pol = policy_evict_first();   // the head is read once per call
-            int pre = 0;
-            {
-                TcPieces pp(P);
-                while (pre < S && pp.next(P, ta, tb, kb0, kb1))
-                    for (int kb = kb0; kb < kb1 && pre < S; ++kb, ++pre) {
-                        mbar_arrive_expect_tx(&full[pre], (uint32_t)Lay::STAGE);
-                        tma_load_2d_hint(tiles + (size_t)pre * Lay::STAGE, &tmap_w, kb * TC_BK, ta * TC_BM, &full[pre],
-                                         pol);
-                    }
-            }
-            pdl_wait();
-            deadline = globaltimer() + P.timeout_ns;
             int it = 0;
             bool dead = false;
             TcPieces pc(P);
             while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S;
-                    const uint32_t r = (uint32_t)(it / S);
-                    unsigned char *st = tiles + (size_t)s * Lay::STAGE;
-                    if (it >= pre) {
-                        if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
-                            if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x110u);
-                            flags[0] = 1;
-                            dead = true;
-                            break;
-                        }
-                        mbar_arrive_expect_tx(&full[s], (uint32_t)Lay::STAGE);
-                        tma_load_2d_hint(st, &tmap_w, kb * TC_BK, ta * TC_BM, &full[s], pol);
+                    if (it == S) {   // the first S stages went out before the wait on the previous kernel
+                        pdl_wait();
+                        deadline = globaltimer() + P.timeout_ns;
                     }
-                    tma_load_2d(st + WH_W_BYTES, &tmap_x, kb * TC_BK, 0, &full[s]);
-                    tma_load_2d(st + WH_W_BYTES + Lay::X_ATOM, &tmap_x, kb * TC_BK + 64, 0, &full[s]);
+                    if (it >= S && (flags[0] || !mbar_wait(&wempty[s], ((uint32_t)(it / S) & 1u) ^ 1u, deadline))) {
+                        if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x110u);
+                        flags[0] = 1;
+                        dead = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&wfull[s], (uint32_t)WH_W_BYTES);
+                    tma_load_2d_hint(wring + (size_t)s * WH_W_BYTES, &tmap_w, kb * TC_BK, ta * TC_BM, &wfull[s], pol);
                 }
             }
+            if (it < S) pdl_wait();   // (a short range never reached the wait above)
             if (dead) {   // let the copies already issued land before the shared memory is released
                 const uint64_t d2 = globaltimer() + P.timeout_ns;
-                for (int j = (it > S ? it - S : 0); j < it; ++j) mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, d2);
+                for (int j = (it > S ? it - S : 0); j < it; ++j) mbar_wait(&wfull[j % S], (uint32_t)(j / S) & 1u, d2);
+            }
+        }
+    } else if (warp == 6) {
+        // ---------------- activation producer (TMA; the K block's two atoms of the BN token rows) ----------------
+        if (lane == 0) {
+            int it = 0;
+            bool dead = false;
+            TcPieces pc(P);
+            while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int t = it % XS;
+                    if (it >= XS && (flags[0] || !mbar_wait(&xempty[t], ((uint32_t)(it / XS) & 1u) ^ 1u, deadline))) {
+                        if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x170u);
+                        flags[0] = 1;
+                        dead = true;
+                        break;
+                    }
+                    unsigned char *xs = xring + (size_t)t * Lay::X_STAGE;
+                    mbar_arrive_expect_tx(&xfull[t], (uint32_t)Lay::X_STAGE);
+                    tma_load_2d(xs, &tmap_x, kb * TC_BK, 0, &xfull[t]);
+                    tma_load_2d(xs + Lay::X_ATOM, &tmap_x, kb * TC_BK + 64, 0, &xfull[t]);
+                }
+            }
+            if (dead) {
+                const uint64_t d2 = globaltimer() + P.timeout_ns;
+                for (int j = (it > XS ? it - XS : 0); j < it; ++j)
+                    mbar_wait(&xfull[j % XS], (uint32_t)(j / XS) & 1u, d2);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16<T>(TC_BM, BN);
+            static_assert(2 * BN <= WH_ACOL, "accumulators overlap the A stages");
             int it = 0, ut = 0;
             TcPieces pc(P);
             while (pc.next(P, ta, tb, kb0, kb1)) {
@@ -258,34 +267,26 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
                     flags[0] = 1;
                 }
                 tc_fence_after();
-                static_assert(2 * BN <= WH_ACOL, "accumulators overlap the A stages");
                 const uint32_t d = tmem_base + (uint32_t)(buf * BN);
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     if (flags[0]) break;   // aborted: issue nothing more
-                    const int s = it % S, a = it % NAS;
-                    // full[s]: the activations landed (the converters saw it too); afull[a]: the weights are converted
-                    if (!mbar_wait(&full[s], (uint32_t)(it / S) & 1u, deadline) ||
-                        !mbar_wait(&afull[a], (uint32_t)(it / NAS) & 1u, deadline)) {
+                    const int t = it % XS, a = it % WH_AS;
+                    if (!mbar_wait(&xfull[t], (uint32_t)(it / XS) & 1u, deadline) ||
+                        !mbar_wait(&afull[a], (uint32_t)(it / WH_AS) & 1u, deadline)) {
                         report(P.status, ST_PIPE_TIMEOUT | 0x130u);
                         flags[0] = 1;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t xb = smem_u32(tiles + (size_t)s * Lay::STAGE + WH_W_BYTES);
+                    const uint32_t xb = smem_u32(xring + (size_t)t * Lay::X_STAGE);
+                    const uint32_t at = tmem_base + (uint32_t)(WH_ACOL + a * 64);
 #pragma unroll
-                    for (int k = 0; k < 8; ++k) {   // 16 elements (32 bytes: +2 in a descriptor, 8 TMEM columns) per MMA
+                    for (int k = 0; k < 8; ++k) {   // 16 elements (32 bytes: +2 in the descriptor, 8 TMEM columns)
                         const uint64_t bdesc = sw128_desc(xb + (uint32_t)((k >> 2) * Lay::X_ATOM)) + 2 * (k & 3);
-                        if constexpr (ASMEM) {
-                            const uint32_t ab = smem_u32(astages + (size_t)a * WH_A_BYTES);
-                            const uint64_t adesc = sw128_desc(ab + (uint32_t)((k >> 2) * (WH_A_BYTES / 2))) + 2 * (k & 3);
-                            umma_f16_ss(d, adesc, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-                        } else {
-                            const uint32_t at = tmem_base + (uint32_t)(WH_ACOL + a * 64);
-                            umma_f16_ts(d, at + 8 * k, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-                        }
+                        umma_f16_ts(d, at + 8 * k, bdesc, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
                     }
                     umma_commit(&aempty[a]);
-                    umma_commit(&empty[s]);
+                    umma_commit(&xempty[t]);
                 }
                 if (!flags[0]) umma_commit(&tfull[buf]);
             }
@@ -293,10 +294,10 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
             umma_commit(drain);
             mbar_wait(drain, 0u, globaltimer() + P.timeout_ns);
         }
-    } else if (warp >= 6) {
+    } else if (warp >= WH_CONV0) {
         // ---------------- converters: int8 rows (shared memory) -> 16-bit rows (TMEM) ----------------
         const int q = warp & 3;
-        const int slot = (warp - 6) >> 2;   // this warp converts the blocks it with it % NW == slot
+        const int slot = (warp - WH_CONV0) >> 2;   // this warp converts the blocks it with it % NW == slot
         const int row = q * 32 + lane;
         const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)WH_ACOL;
         int it = 0;
@@ -305,12 +306,22 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
         while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
             for (int kb = kb0; kb < kb1; ++kb, ++it) {
                 if (it % NW != slot) continue;
-                const int s = it % S, a = it % NAS;
+                const int s = it % S, a = it % WH_AS;
                 // warp-uniform decisions only: tcgen05.st below is a whole-warp instruction
                 const bool aborted = __any_sync(0xffffffffu, flags[0] != 0);
                 bool ok = !aborted;
-                if (ok) ok = warp_wait(&full[s], (uint32_t)(it / S) & 1u, deadline);
-                if (ok) ok = warp_wait(&aempty[a], ((uint32_t)(it / NAS) & 1u) ^ 1u, deadline);
+                if (ok) ok = warp_wait(&wfull[s], (uint32_t)(it / S) & 1u, deadline);
+                uint4 v[8];
+                if (ok) {
+                    const unsigned char *src = wring + (size_t)s * WH_W_BYTES + row * TC_BK;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)   // the row's 128 bytes; 16-byte chunk j sits at chunk j ^ (row % 8)
+                        v[j] = *reinterpret_cast<const uint4 *>(src + ((j ^ (row & 7)) << 4));
+                    // the weights are in registers: hand the stage back to the producer before converting
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&wempty[s]);
+                    ok = warp_wait(&aempty[a], ((uint32_t)(it / WH_AS) & 1u) ^ 1u, deadline);
+                }
                 if (!ok) {
                     if (lane == 0 && !aborted) report(P.status, ST_PIPE_TIMEOUT | 0x140u);
                     flags[0] = 1;
@@ -318,47 +329,21 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
                     break;
                 }
                 tc_fence_after();   // the MMAs that read this A stage before have completed
-                const unsigned char *src = tiles + (size_t)s * Lay::STAGE + row * TC_BK;
-                uint4 v[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)   // the row's 128 bytes; 16-byte chunk j sits at chunk j ^ (row % 8)
-                    v[j] = *reinterpret_cast<const uint4 *>(src + ((j ^ (row & 7)) << 4));
-                if constexpr (ASMEM) {
-                    // output chunk c (8 elements) of the row: atom c / 8, chunk (c % 8) ^ (row % 8) of the row's
-                    // 128 bytes in it -- the 128-byte swizzle, so a warp's 32 rows again cover all banks
-                    unsigned char *dst = astages + (size_t)a * WH_A_BYTES + row * 128;
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t o[32];
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        uint32_t o[8];
-                        cvt_word<T>(v[j].x, o[0], o[1]);
-                        cvt_word<T>(v[j].y, o[2], o[3]);
-                        cvt_word<T>(v[j].z, o[4], o[5]);
-                        cvt_word<T>(v[j].w, o[6], o[7]);
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const int c = 2 * j + e;
-                            *reinterpret_cast<uint4 *>(dst + (c >> 3) * (WH_A_BYTES / 2) + (((c & 7) ^ (row & 7)) << 4)) =
-                                make_uint4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
-                        }
+                    for (int c = 0; c < 4; ++c) {
+                        const uint4 w = v[h * 4 + c];
+                        cvt_word<T>(w.x, o[8 * c + 0], o[8 * c + 1]);
+                        cvt_word<T>(w.y, o[8 * c + 2], o[8 * c + 3]);
+                        cvt_word<T>(w.z, o[8 * c + 4], o[8 * c + 5]);
+                        cvt_word<T>(w.w, o[8 * c + 6], o[8 * c + 7]);
                     }
-                    fence_proxy_async_smem();
-                } else {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        uint32_t o[32];
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const uint4 w = v[h * 4 + c];
-                            cvt_word<T>(w.x, o[8 * c + 0], o[8 * c + 1]);
-                            cvt_word<T>(w.y, o[8 * c + 2], o[8 * c + 3]);
-                            cvt_word<T>(w.z, o[8 * c + 4], o[8 * c + 5]);
-                            cvt_word<T>(w.w, o[8 * c + 6], o[8 * c + 7]);
-                        }
-                        tmem_st32(lane_base + (uint32_t)(a * 64 + h * 32), o);
-                    }
-                    tmem_st_wait();
-                    tc_fence_before();
+                    tmem_st32(lane_base + (uint32_t)(a * 64 + h * 32), o);
                 }
+                tmem_st_wait();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&afull[a]);
             }
@@ -451,7 +436,7 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TCOLS);
+        tmem_dealloc(tmem_base, WH_TMEM_COLS);
     }
 }
 
@@ -513,43 +498,33 @@ __global__ void __launch_bounds__(256) w8a16_rows_kernel(const T *__restrict__ x
 }
 
 // ---- host side -------------------------------------------------------------------------------------------------------
-template <int BN, bool ASMEM> inline int wh_stages(int dev) {
-    const int fixed = 1024 + WH_BAR_BYTES + 1024 + (ASMEM ? WH_AS_SMEM * WH_A_BYTES : 0);
-    const int s = (max_smem_optin(dev) - fixed) / WhLayout<BN>::STAGE;
+template <int BN> inline int wh_stages(int dev) {   // weight stages
+    const int fixed = 1024 + WH_BAR_BYTES + 1024 + WhLayout<BN>::XS * WhLayout<BN>::X_STAGE;
+    const int s = (max_smem_optin(dev) - fixed) / WH_W_BYTES;
     return s > 16 ? 16 : s;
 }
-template <int BN, bool ASMEM> inline int wh_smem_bytes(int stages) {
-    return stages * WhLayout<BN>::STAGE + (ASMEM ? WH_AS_SMEM * WH_A_BYTES : 0) + 1024 + WH_BAR_BYTES;
+template <int BN> inline int wh_smem_bytes(int stages) {
+    return stages * WH_W_BYTES + WhLayout<BN>::XS * WhLayout<BN>::X_STAGE + 1024 + WH_BAR_BYTES;
 }
 
-template <typename T, int BN, int NW, bool ASMEM>
+template <typename T, int BN, int NW>
 static int launch_wh_nw(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cudaStream_t s) {
     const int dev = cur_device();
     if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
-    const int stages = wh_stages<BN, ASMEM>(dev);
+    const int stages = wh_stages<BN>(dev);
     if (stages < 2) return VT_EARG;
     A.t.stages = stages;
-    const int smem = wh_smem_bytes<BN, ASMEM>(stages);
+    const int smem = wh_smem_bytes<BN>(stages);
     static bool attr[VT_MAX_DEV] = {false};
     if (!attr[dev]) {
-        if (cudaFuncSetAttribute(w8a16_tc_kernel<T, BN, NW, ASMEM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 smem) != cudaSuccess)
+        if (cudaFuncSetAttribute(w8a16_tc_kernel<T, BN, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
             return (int)cudaGetLastError();
         attr[dev] = true;
     }
     int g = num_sms(dev);
     if (g > A.t.units) g = A.t.units;
-    return launch_k(w8a16_tc_kernel<T, BN, NW, ASMEM>, dim3(g), dim3(wh_threads(NW)), smem, s, true, mw, mx, A);
-}
-
-// Where the converted weights go: VLLM_TURING_W8A16_ASMEM = 1 shared memory, 0 tensor memory (default 0).
-inline bool w8a16_asmem() {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = getenv("VLLM_TURING_W8A16_ASMEM");
-        v = (e && atoi(e) == 1) ? 1 : 0;
-    }
-    return v != 0;
+    return launch_k(w8a16_tc_kernel<T, BN, NW>, dim3(g), dim3(wh_threads(NW)), smem, s, true, mw, mx, A);
 }
 
 // Converter warps per TMEM lane quarter: VLLM_TURING_W8A16_NW = 1, 2 or 3 (default 2; 3 only up to 32 token rows).
@@ -566,11 +541,10 @@ inline int w8a16_nw() {
 template <typename T, int BN>
 static int launch_wh(const CUtensorMap &mw, const CUtensorMap &mx, WhArgs A, cudaStream_t s) {
     const int nw = w8a16_nw();
-    if (w8a16_asmem()) return launch_wh_nw<T, BN, 2, true>(mw, mx, A, s);
-    if (nw == 1) return launch_wh_nw<T, BN, 1, false>(mw, mx, A, s);
-    if constexpr (BN <= 32)   // 64 token rows: the epilogue's registers leave room for 14 warps, not 18
-        if (nw == 3) return launch_wh_nw<T, BN, 3, false>(mw, mx, A, s);
-    return launch_wh_nw<T, BN, 2, false>(mw, mx, A, s);
+    if (nw == 1) return launch_wh_nw<T, BN, 1>(mw, mx, A, s);
+    if constexpr (BN <= 32)   // 64 token rows: the epilogue's registers leave room for 15 warps, not 19
+        if (nw == 3) return launch_wh_nw<T, BN, 3>(mw, mx, A, s);
+    return launch_wh_nw<T, BN, 2>(mw, mx, A, s);
 }
 
 // split-K slot bytes for M token rows on this device (one fp32 contribution of 128 x M per CTA, grid <= SMs)
