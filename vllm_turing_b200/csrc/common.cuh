@@ -64,6 +64,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint64
     return true;
 }
 
+// The same for a waiter off the critical path (e.g. an epilogue waiting out a whole tile's K range): it sleeps
+// between polls, leaving the issue slots and the integer pipe of its SM sub-partition to the warps doing the work.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, uint64_t deadline, uint32_t ns) {
+    uint32_t it = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        __nanosleep(ns);
+        if ((++it & 63u) == 0 && globaltimer() > deadline) return false;
+    }
+    return true;
+}
+
 // ---- 1-D bulk copy global -> shared (TMA engine), completion counted in bytes on an mbarrier -------------------------
 // dst and src 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -396,7 +396,8 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
                     }
                 }
             }
-            if (!__any_sync(0xffffffffu, flags[0] != 0) && !warp_wait(&tfull[buf], use & 1u, deadline)) {
+            if (!__any_sync(0xffffffffu, flags[0] != 0) &&
+                !__all_sync(0xffffffffu, mbar_wait_sleep(&tfull[buf], use & 1u, deadline, 256))) {
                 if (lane == 0) report(P.status, ST_PIPE_TIMEOUT | 0x160u);
                 flags[0] = 1;
             }
