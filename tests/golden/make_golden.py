@@ -15,6 +15,8 @@ exact formulas the reference's tests compute where the reference is CUDA:
              heads; the W8A16 GEMM as the reference's kernel computes it (vllm_turing/csrc/w8a16_gemv.cu:64-106:
              products exact in fp32, the sum, then acc * s + b in one fp32 rounding), with the sum in float64; and
              the reference's large-M path (lmhead.py:104-110: dequantise to the activation dtype, matmul), run on CPU
+  convert    the reference's scripts/w8a8_convert.py itself (run on the CPU) on a tiny seeded bf16 checkpoint, W8A8,
+             --w8a16 64 and --mixed: every stored tensor and the quantization_config
   config 0   the whole chain at BASELINE config 0 (M=16, K_local=8704, N=5120, 2 ranks, seed 0): digests of the
              exact parts plus the int8 / scales arrays
 Inputs come from seeded torch CPU generators (vllm_turing_b200.synthetic for config 0) and are stored (small cases)
@@ -52,6 +54,47 @@ def mm_case_inputs(M, N, K):
     sa = torch.rand(M, generator=g) * 1e-2
     sw = torch.rand(N, generator=g) * 1e-3
     return a, w, sa, sw
+
+
+# a tiny synthetic checkpoint for the converter (scripts/w8a8_convert.py): names from its quantised and kept sets
+CKPT_SHARDS = {
+    "model-00001-of-00002.safetensors": {
+        "model.language_model.layers.0.mlp.gate_proj.weight": (48, 256),
+        "model.language_model.layers.0.mlp.down_proj.weight": (64, 128),
+        "model.language_model.layers.0.self_attn.o_proj.weight": (32, 128),
+        "model.language_model.layers.0.linear_attn.in_proj_a.weight": (16, 64),   # kept (ignore list)
+        "model.language_model.norm.weight": (64,),
+    },
+    "model-00002-of-00002.safetensors": {
+        "mtp.layers.0.mlp.up_proj.weight": (32, 128),
+        "lm_head.weight": (100, 64),                                              # kept (ignore list)
+    },
+}
+CKPT_MODES = {"w8a8": [], "w8a16": ["--w8a16", "64"], "mixed": ["--mixed"]}
+
+
+def tiny_checkpoint(path):
+    """Writes the synthetic bf16 checkpoint (seeded) into `path`."""
+    import json as _json
+    from safetensors.torch import save_file
+    os.makedirs(path, exist_ok=True)
+    g = torch.Generator().manual_seed(77)
+    wmap = {}
+    for shard, tensors in CKPT_SHARDS.items():
+        out = {}
+        for name, shape in tensors.items():
+            t = (torch.randn(*shape, generator=g) * 0.05).to(torch.bfloat16)
+            if len(shape) == 2 and shape[0] > 5:
+                t[5] = 0                       # an all-zero output channel: scale clamps at 1e-12 / 127
+            out[name] = t
+            wmap[name] = shard
+        save_file(out, os.path.join(path, shard), metadata={"format": "pt"})
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        _json.dump({"metadata": {"total_size": 0}, "weight_map": wmap}, f)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        _json.dump({"architectures": ["Qwen3_5ForConditionalGeneration"], "text_config": {"hidden_size": 64}}, f)
+    with open(os.path.join(path, "tokenizer_config.json"), "w") as f:
+        f.write("{}")
 
 
 def main():
@@ -166,6 +209,26 @@ def main():
     out["cfg0_residual_sha"] = np.array(sha(bits(h)))
     out["cfg0_q"] = q.numpy()
     out["cfg0_s"] = s.reshape(-1).numpy()
+
+    # ---- checkpoint conversion: the reference's own script on the tiny checkpoint, on the CPU -----------------------
+    import json as _json
+    import subprocess
+    import tempfile
+    from safetensors import safe_open
+    with tempfile.TemporaryDirectory() as tmp:
+        src = os.path.join(tmp, "src")
+        tiny_checkpoint(src)
+        for mode, flags in CKPT_MODES.items():
+            dst = os.path.join(tmp, mode)
+            subprocess.run([sys.executable, os.path.join(args.ref, "scripts", "w8a8_convert.py"), src, dst, "cpu",
+                            *flags], check=True, capture_output=True)
+            for shard in CKPT_SHARDS:
+                with safe_open(os.path.join(dst, shard), framework="pt") as f:
+                    for name in f.keys():
+                        t = f.get_tensor(name)
+                        out[f"cv_{mode}_{name}"] = bits(t) if t.dtype == torch.bfloat16 else t.numpy()
+            cfg = _json.load(open(os.path.join(dst, "config.json")))
+            out[f"cv_{mode}_quantization_config"] = np.array(_json.dumps(cfg["quantization_config"], sort_keys=True))
 
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays, {os.path.getsize(args.out) / 1024:.0f} KiB")

@@ -121,7 +121,8 @@ def test_synthetic_inputs_are_deterministic():
     assert torch.equal(a.residual, c.residual) and torch.equal(a.norm_w, c.norm_w)   # shared across ranks
 
 
-@pytest.mark.parametrize("mod", ["w8a8", "hostar", "quantfuse", "customar", "dmaag", "tailoverlap", "comm", "lmhead"])
+@pytest.mark.parametrize("mod", ["w8a8", "hostar", "quantfuse", "customar", "dmaag", "tailoverlap", "comm", "lmhead",
+                                 "convert"])
 def test_modules_import_without_gpu(mod):
     __import__(f"vllm_turing_b200.{mod}")
 
