@@ -1,6 +1,7 @@
 """AR8, the optional lossy all-reduce format (csrc/ar8.cu), against the CPU oracle (oracle/w8a8_oracle.c
 orc_ar8_quant / orc_ar8_dequant_sum, the arithmetic of vllm_turing/csrc/host_ar.cu:133-201) and against the
-reference's own AR8 kernels rebuilt for sm_100a (oracle/_ref/libref_host_ar.so): bit-exact."""
+reference's own AR8 kernels rebuilt for sm_100a (oracle/_ref/libref_host_ar.so): bit-exact. Plus the communicator glue
+at one rank (TPComm.all_reduce_ar8, dmaag.all_gather_dim)."""
 import ctypes
 import os
 
@@ -83,3 +84,37 @@ def test_against_reference_ar8_kernels():
     torch.cuda.synchronize()
     assert torch.equal(g_ref.cpu(), g_us.cpu()), "packed blocks differ from the reference's"
     assert torch.equal(o_ref.cpu().view(torch.int16), o_us.cpu().view(torch.int16)), "sums differ"
+
+
+@pytest.fixture(scope="module")
+def comm1():
+    import torch.distributed as dist
+    from vllm_turing_b200.comm import TPComm
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29673")
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    torch.cuda.set_device(0)
+    c = TPComm(dist.group.WORLD, torch.device("cuda", 0))
+    yield c
+    c.close()
+
+
+def test_comm_ar8_single_rank(comm1):
+    """TPComm.all_reduce_ar8 at one rank: the packed block of the rank, gathered (nothing to fetch), summed: the
+    oracle's dequantised quantisation of the input, bit for bit."""
+    n = 8 * 5120
+    x = _x(n, 5)
+    y = comm1.all_reduce_ar8(x.cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(O.to_bits(y.cpu()), O.ar8_dequant_sum([O.ar8_quant(O.to_bits(x))]))
+    assert comm1.status(clear=True) == 0
+
+
+def test_all_gather_dim_single_rank(comm1):
+    from vllm_turing_b200 import dmaag
+    x = torch.randn(5, 24).to(torch.bfloat16).cuda()
+    for dim in (-1, 0):
+        got = dmaag.all_gather_dim(comm1, x, dim)
+        torch.cuda.synchronize()
+        assert got is not None and torch.equal(got.cpu(), x.cpu())
