@@ -15,16 +15,18 @@
 // of the weights. A split tile is finished by its head CTA from the other CTAs' fp32 partial sums (LL slot words).
 //
 // The int8 -> 16-bit conversion runs between shared memory and the tensor core, into TMEM:
-//   - warp 0 (one thread) TMA-loads each K block (128 weight rows x 128 bytes, 128-byte swizzle) and the activations
-//     of that K block (two 64-element swizzle atoms of BN rows) into a ring of shared-memory stages;
-//   - warps 6..9 convert: a thread owns one weight row of its warp's TMEM lane quarter, reads that row's 128 bytes (the
-//     swizzle spreads the 32 row reads of a warp over all banks), converts them exactly to 16-bit floats and stores
-//     them with tcgen05.st into a ring of A stages in TMEM (64 columns of two elements per row and K block);
+//   - warp 0 (one thread) TMA-loads each K block of weights (128 rows x 128 bytes, 128-byte swizzle) into a ring of
+//     16 KB shared-memory stages; warp 6 (one thread) loads the K block's activations (two 64-element swizzle atoms
+//     of BN rows) into a separate, smaller ring;
+//   - warps 7.. convert, two per TMEM lane quarter taking whole K blocks in turn: a thread owns one weight row, reads
+//     that row's 128 bytes (the swizzle spreads the 32 row reads of a warp over all banks), hands the weight stage
+//     back to the producer at once, converts the bytes exactly to 16-bit floats and stores them with tcgen05.st into
+//     a ring of A stages in TMEM (64 columns of two elements per row and K block);
 //   - warp 1 (one thread) issues 8 MMAs (K = 16 each) per K block, A from TMEM, B from shared memory;
 //   - warps 2..5 drain the accumulators (tcgen05.ld), apply the row scale and the bias and store the logits.
-// Shared memory carries the weights once in and once out as int8, plus the small activation tiles. Converting into
-// shared memory instead would add the 16-bit copy's write and the tensor core's read of it: about three times the
-// shared-memory traffic per weight byte.
+// Because the weight stage is free as soon as it is read, the bytes in flight from HBM are the whole weight ring,
+// whatever the conversion and the MMAs take. (A variant with the 16-bit weights in shared memory and the MMA reading
+// both operands by descriptor measured no faster.)
 //
 // Every wait is bounded (globaltimer); on a timeout the CTA records the status, stops issuing, waits (bounded) for the
 // copies and MMAs it issued, frees its TMEM and returns.
