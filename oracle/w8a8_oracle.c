@@ -1,5 +1,6 @@
 /*
- * w8a8_oracle.c -- CPU restatement of vllm-turing's tensor-parallel W8A8 linear hot path.
+ * w8a8_oracle.c -- CPU restatement of vllm-turing's tensor-parallel W8A8 linear hot path, its int8 LM head (W8A16)
+ * and its optional int8-compressed all-reduce (AR8).
  *
  * TEST INFRASTRUCTURE ONLY. This file is the checker: it is called by tests/, by __graft_entry__.smoke() and by
  * bench.py's cpu_baseline / `--impl reference` legs. The product path (vllm_turing_b200) never links, loads or calls
@@ -8,7 +9,9 @@
  * Parity pins: the quantisers, the dequant epilogue and the two-rank reduction are checked against golden vectors made
  * by the reference's own Python (vllm_turing/quantfuse.py quant_torch, imported from the reference tree) and by the
  * formulas its tests compute (tests/test_w8a8_mma.py:42-45, tests/test_quantfuse.py:45-48, tests/bench_devll.py:28-36);
- * see tests/golden/make_golden.py and tests/test_oracle.py.
+ * the LM head's row quantiser and W8A16 arithmetic against the reference's vllm_turing/lmhead.py quantize_rows and its
+ * large-M path run on the CPU; the AR8 format against the reference's own AR8 kernels rebuilt for the GPU (no golden
+ * file: the GPU tests compare both bit for bit); see tests/golden/make_golden.py and tests/test_oracle.py.
  *
  * Every function names the reference file:line whose arithmetic it restates. Floating point follows the reference's
  * rounding points exactly (compile with -ffp-contract=off; fused multiply-adds are written out as fmaf where the
