@@ -127,6 +127,8 @@ struct TcArgs {
     int group_m;                // prefill raster: A tiles per group (each group covers all B tiles)
     int blocked_a;              // decode: A (the weight) in the tile-blocked layout (tc_a_coords)
     int l2_prefetch_blocks;     // decode: weight K blocks past the ring prefetched into L2 before pdl_wait
+    int l2_runahead;            // decode: with each weight K block loaded, the one this many blocks later is
+                                // prefetched into L2 (0: off)
     const float *sa, *sw;       // per token, per output feature (NULL in int32 mode)
     const void *bias;           // [N] output dtype or NULL
     int sa_rows, sw_rows;       // 1: per row / feature, 0: one value
@@ -427,6 +429,17 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                                 tma_load_2d(st + j * Lay::A_BYTES, tmap_a, ax, ay, &full[s]);
                         }
                     }
+                    if (SWAP && P.l2_runahead > 0) {
+                        // L2 run-ahead: the weight block l2_runahead units later in this CTA's range, so that its
+                        // stage load finds it in L2 and the bytes in flight are not bounded by the ring alone
+                        for (int j = 0; j < nb; ++j) {
+                            const int v = ta * P.nkb + kb + j + P.l2_runahead;
+                            if (v >= pc.hi) break;
+                            int ax, ay;
+                            tc_a_coords(P, v / P.nkb, v % P.nkb, ax, ay);
+                            tma_prefetch_l2_2d(tmap_a, ax, ay);
+                        }
+                    }
                     for (int j = 0; j < nb; ++j)
                         tma_load_2d(st + KBS * Lay::A_BYTES + j * Lay::B_BYTES, tmap_b, (kb + j) * TC_BK, tb * BN,
                                     &full[s]);
@@ -645,6 +658,17 @@ inline int l2_prefetch_blocks() {
     return v;
 }
 
+// L2 run-ahead of the decode weight stream, in K blocks of 16 KB: VLLM_TURING_L2_RUNAHEAD (default 0 = off)
+inline int l2_runahead() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_L2_RUNAHEAD");
+        const int x = e ? atoi(e) : 0;
+        v = x > 0 ? (x > 4096 ? 4096 : x) : 0;
+    }
+    return v;
+}
+
 inline void tc_decode_args(TcArgs &P, int M, int N, int K) {  // (the launch grid is min(SMs, units))
     P.n_tiles_a = (N + TC_BM - 1) / TC_BM;
     P.n_tiles_b = 1;
@@ -652,6 +676,7 @@ inline void tc_decode_args(TcArgs &P, int M, int N, int K) {  // (the launch gri
     P.units = P.n_tiles_a * P.nkb;
     P.stream_k = 1;
     P.l2_prefetch_blocks = pdl_enabled() ? l2_prefetch_blocks() : 0;
+    P.l2_runahead = l2_runahead();
     P.M = M;
     P.N = N;
 }

@@ -219,6 +219,10 @@ __global__ void __launch_bounds__(wh_threads(NW), 1)
                     }
                     mbar_arrive_expect_tx(&wfull[s], (uint32_t)WH_W_BYTES);
                     tma_load_2d_hint(wring + (size_t)s * WH_W_BYTES, &tmap_w, kb * TC_BK, ta * TC_BM, &wfull[s], pol);
+                    if (P.l2_runahead > 0) {   // the block l2_runahead units later in this CTA's range, into L2
+                        const int v = ta * P.nkb + kb + P.l2_runahead;
+                        if (v < pc.hi) tma_prefetch_l2_2d(&tmap_w, (v % P.nkb) * TC_BK, (v / P.nkb) * TC_BM);
+                    }
                 }
             }
             if (!waited) pdl_wait();   // (a range of at most S blocks never reached the wait above)
