@@ -521,7 +521,9 @@ def run_lmhead(args, world, rank, local, dev, gloo):
         w = torch.randint(-128, 128, (Vs, K), generator=g, dtype=torch.int8).to(dev)
         sc = (torch.rand(Vs, generator=g) * 1e-3 + 1e-5).to(dev)
         heads.append((w, sc, torch.empty(M, VOCAB, dtype=torch.bfloat16, device=dev)))
-    comm = TPComm(gloo, dev) if world > 1 else None
+    # one-shot capacity for this rank's logits (TP2 at M = 5: 760 KB, above the 512 KB default)
+    ll = max(512 << 10, ((M * Vs * 2 + 4095) // 4096) * 4096)
+    comm = TPComm(gloo, dev, ll_bytes=ll) if world > 1 else None
     stream = torch.cuda.current_stream()
 
     def step_set(h):

@@ -191,7 +191,8 @@ int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype,
 int vt_all_gather(void *comm, void *gathered, long long m, void *stream);
 /* gathered [rows, ld_bytes]: world column blocks of row_bytes per row, this rank's block (offset rank * row_bytes)
  * pre-written; fills the peers' blocks (vLLM's all_gather along the last dimension, e.g. vocabulary-parallel logits,
- * with no transpose). row_bytes, ld_bytes % 8 == 0, rows * row_bytes within the one-shot LL capacity. New entry. */
+ * with no transpose). row_bytes, ld_bytes % 8 == 0, rows * row_bytes within the communicator's one-shot LL capacity
+ * (vt_comm_ll_bytes). New entry. */
 int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row_bytes, long long ld_bytes,
                        void *stream);
 

@@ -426,7 +426,8 @@ int vt_all_gather(void *comm, void *gathered, long long m, void *stream) {
 // (byte offset rank * row_bytes of every row) is pre-written, the call fills the peers' blocks. The concatenation
 // along the last dimension that vLLM's all_gather(dim=-1) builds (logits [M, world * V / world]) without a separate
 // transpose. row_bytes % 8 == 0, ld_bytes % 8 == 0, ld_bytes >= world * row_bytes, rows * row_bytes at most the LL
-// capacity (one-shot LL words); larger payloads: VT_EARG (use vt_all_gather on contiguous slots).
+// capacity of the communicator (one-shot LL words; size it with ll_data at creation); larger payloads: VT_EARG (use
+// vt_all_gather on contiguous slots).
 int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row_bytes, long long ld_bytes,
                        void *stream) {
     Comm *c = reinterpret_cast<Comm *>(comm);
@@ -435,7 +436,7 @@ int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row
         return VT_EARG;
     if (rows == 0 || row_bytes == 0 || c->v.world == 1) return 0;
     const long long m = rows * row_bytes;
-    if (m > (long long)(c->v.L.ll_slot / 2) || m > (1 << 20)) return VT_EARG;
+    if (m > (long long)(c->v.L.ll_slot / 2)) return VT_EARG;
     const long long nw = m >> 3;
     long long g = (nw + AR_THREADS - 1) / AR_THREADS;
     const int sms = num_sms(c->dev);
