@@ -206,3 +206,36 @@ def test_all_gather_dim_large_last_dim_uses_slots():
     fc = _FakeComm(xs, 1, ll=128)                                     # payload 384 B > the one-shot capacity
     got = dmaag.all_gather_dim(fc, xs[1], -1)
     assert torch.equal(got, torch.cat(xs, -1)) and fc.calls == ["slots"]
+
+
+@pytest.mark.parametrize("M,ll", [(5, 1 << 20), (5, 256), (70, 1 << 20)])
+def test_logits_gathered_paths(monkeypatch, M, ll):
+    """lmhead.logits_gathered on CPU with the kernel and the communicator faked: in place + row-strided gather when the
+    payload fits the one-shot capacity and M <= 64, else the shard through the op + contiguous slots + transpose;
+    both give the ranks' logits concatenated along the vocabulary."""
+    from vllm_turing_b200 import lmhead
+    world, Vs, K = 3, 40, 32
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    heads = [torch.randn(Vs, K, generator=g) for _ in range(world)]
+    logits = [(x.float() @ h.t()).to(torch.bfloat16) for h in heads]
+    want = torch.cat(logits, dim=1)
+    calls = []
+
+    def fake_mm_into(out, x_, w, s, bias=None, ldo=None):
+        calls.append("kernel")
+        r = int(w[0, 0].item())
+        out[:, :Vs] = logits[r]          # the view starts at this rank's columns; the row stride is out's
+        return out
+
+    monkeypatch.setattr(lmhead, "mm_into", fake_mm_into)
+    monkeypatch.setattr(lmhead, "kernel_ok", lambda x_, w: True)
+    monkeypatch.setattr(lmhead, "shard_logits", lambda x_, w, s, b=None: (calls.append("op"), logits[int(w[0, 0])])[1])
+    for rank in range(world):
+        fc = _FakeComm([lg for lg in logits], rank, ll=ll)
+        w_tag = torch.full((Vs, K), float(rank))   # the fakes read the rank from the weight
+        got = lmhead.logits_gathered(x, w_tag, None, comm=fc)
+        assert torch.equal(got, want)
+        fits = M <= 64 and M * Vs * 2 <= ll
+        assert fc.calls == (["rows"] if fits else ["slots"])
+    assert set(calls) == ({"kernel"} if M <= 64 and M * Vs * 2 <= ll else {"op"})

@@ -115,6 +115,11 @@ def _w8a16_mm_fake(x, w, s, bias):
     return x.new_empty(x.shape[0], w.shape[0])
 
 
+def shard_logits(x, w, s, bias=None):
+    """This rank's logits [M, Vs] through the op (any M)."""
+    return torch.ops.vllm_turing.w8a16_mm(x, w, s, bias)
+
+
 def logits_gathered(x, w, s, bias=None, comm=None, out=None):
     """Vocabulary-parallel logits gathered on every rank: out [M, world * Vs] (Vs = this rank's rows of the head).
     The kernel writes this rank's columns in place (row stride world * Vs); the row-strided P2P all-gather fills
@@ -132,7 +137,7 @@ def logits_gathered(x, w, s, bias=None, comm=None, out=None):
         if world > 1:
             comm.all_gather_rows(out, M, Vs * esz, world * Vs * esz)
         return out
-    shard = torch.ops.vllm_turing.w8a16_mm(x, w, s, bias)
+    shard = shard_logits(x, w, s, bias)
     if world == 1:
         out.copy_(shard)
         return out
