@@ -52,11 +52,14 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="tokens per step (decode default 5, prefill 8192)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce", "lmhead"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce", "lmhead", "p2p", "gemv"],
                     help="decode: the 64-layer MLP stack (the headline, config 1/2); prefill: the row-parallel layer "
                          "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant); "
                          "allreduce: config 4's size sweep, 1 KB .. 256 MB, against NCCL on the same ranks")
     ap.add_argument("--proj", default="down", choices=["down", "o_proj"], help="prefill: K = 17408 or 6144 (per TP)")
+    ap.add_argument("--tail", default="fused", choices=["fused", "chain"],
+                    help="prefill: the fused tail (TPComm.row_linear: GEMM with the reduce-scatter in its epilogue, then "
+                         "reduce + all-gather + RMSNorm + quant; default) or the unfused chain of three kernels")
     ap.add_argument("--blocked", action="store_true",
                     help="decode gate_up on the tile-blocked weight layout (w8a8.block_weight / mma_blocked)")
     ap.add_argument("--mlp", default="unfused", choices=["fused", "unfused"],
@@ -78,6 +81,23 @@ def peaks():
         return float(p["hbm_gbs"]), "measured"
     except Exception:   # noqa: BLE001
         return FALLBACK_HBM_GBS, "fallback"
+
+
+FALLBACK_NVLINK_GBS = 770.0   # the pool's earlier peer-copy measurement per direction (nominal 900)
+
+
+def nvlink_peak():
+    """(GB/s per direction, kind): the peer-copy bandwidth measured by `bench.py --mode p2p` on this pool and committed
+    in profiles/nvlink_peak.txt (`peer_copy_gbs <value>`), else the pool's earlier figure."""
+    try:
+        with open(os.path.join(HERE, "profiles", "nvlink_peak.txt")) as f:
+            for ln in f:
+                p = ln.split()
+                if len(p) >= 2 and p[0] == "peer_copy_gbs":
+                    return float(p[1]), "measured peer copy per direction (profiles/nvlink_peak.txt)"
+    except (OSError, ValueError):
+        pass
+    return FALLBACK_NVLINK_GBS, "fallback: the pool's earlier peer-copy figure per direction"
 
 
 class ClockSampler:
@@ -317,6 +337,74 @@ def dist_setup(args):
     return world, rank, local, dev, gloo
 
 
+def torch_tail_reference(parts, residual, norm_w, eps):
+    """A plain torch float32 restatement of the row-parallel tail from every rank's bf16 partial (all-gathered, exact):
+    reduced = the float32 sum in rank order rounded once; residual' = bf16(reduced + residual); y = bf16(h * rsqrt(
+    mean(h^2) + eps) * w); (q, scale) = per-token int8 quantisation of y (vllm_turing/quantfuse.py:18-24)."""
+    import torch
+    s = parts[0].float()
+    for p in parts[1:]:
+        s = s + p.float()
+    red = s.to(residual.dtype)
+    h = (red.float() + residual.float()).to(residual.dtype)
+    hf = h.float()
+    v = hf.pow(2).mean(-1, keepdim=True)
+    y = (hf * torch.rsqrt(v + eps) * norm_w.float()).to(residual.dtype).float()
+    amax = y.abs().amax(-1, keepdim=True)
+    q = torch.round(y * (amax.reciprocal() * 127.0)).clamp(-128, 127).to(torch.int8)
+    return red, h, q, amax / 127.0
+
+
+def tail_parity(world, gloo_pg, partial, fused, chain=None):
+    """Correctness of one row-parallel tail call, computed on the device and agreed over the ranks (NCCL).
+    partial: this rank's bf16 [M, N] GEMM partial (vllm_turing::scaled_mm_, oracle-pinned on one GPU);
+    fused / chain: dicts {reduced, residual, q} of the path under test and (optionally) of the unfused chain, both
+    started from the same residual. The reference is torch_tail_reference over the all-gathered partials.
+    Returns {reduced_bitexact, residual_bitexact, q_max_lsb, ranks_identical[, chain_*]} (worst over ranks)."""
+    import torch
+    import torch.distributed as dist
+    parts = [torch.empty_like(partial) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(parts, partial)
+    else:
+        parts[0].copy_(partial)
+    res0 = fused["residual0"]
+    red, h, q, _ = torch_tail_reference(parts, res0, fused["norm_w"], fused["eps"])
+
+    def cmp(d):
+        out = {"reduced_bitexact": bool(torch.equal(d["reduced"].view(torch.int16), red.view(torch.int16)))
+               if d.get("reduced") is not None else None,
+               "residual_bitexact": bool(torch.equal(d["residual"].view(torch.int16), h.view(torch.int16))),
+               "q_max_lsb": int((d["q"].int() - q.int()).abs().max().item())}
+        return out
+
+    res = cmp(fused)
+    # identical on every rank: compare rank 0's q and residual with this rank's
+    qq = fused["q"].clone()
+    rr = fused["residual"].clone()
+    if world > 1:
+        dist.broadcast(qq, src=0)
+        dist.broadcast(rr, src=0)
+    res["ranks_identical"] = bool(torch.equal(qq, fused["q"]) and torch.equal(rr, fused["residual"]))
+    if chain is not None:
+        for k, v in cmp(chain).items():
+            res["chain_" + k] = v
+    # worst over ranks: booleans by MIN, LSB counts by MAX
+    keys = sorted(res)
+    vals = torch.tensor([(-1.0 if res[k] is None else float(res[k])) for k in keys], dtype=torch.float64,
+                        device=partial.device)
+    neg = torch.tensor([0.0 if k.endswith("lsb") else 1.0 for k in keys], dtype=torch.float64, device=partial.device)
+    signed = torch.where(neg > 0, -vals, vals)   # MAX of -bool = -MIN(bool)
+    if world > 1:
+        dist.all_reduce(signed, op=dist.ReduceOp.MAX)
+    out = {}
+    for k, v, n in zip(keys, signed.tolist(), neg.tolist()):
+        x = -v if n > 0 else v
+        out[k] = None if res[k] is None else (int(x) if k.endswith("lsb") else bool(x >= 1.0))
+    out["reference"] = "torch float32 restatement over the all-gathered scaled_mm_ partials"
+    return out
+
+
 PREFILL_SETS = 3   # distinct layer buffers cycled by the captured step: every step's inputs are cold in L2
 
 
@@ -359,7 +447,11 @@ def run_prefill(args, world, rank, local, dev, gloo):
     def norm(st):
         rms_norm_dynamic_per_token_quant(st["out"], st["nw"], 1e-6, st["res"], q=st["q"], s=st["s"])
 
-    STEP = (gemm, allreduce, norm)
+    def fused(st):   # one call: GEMM with the reduce-scatter in its epilogue, then reduce + all-gather + row epilogue
+        comm.row_linear(st["a"], st["w"], st["sa"], st["sw"], residual=st["res"], norm_w=st["nw"], eps=1e-6,
+                        q=st["q"], scales=st["s"])
+
+    STEP = (fused,) if args.tail == "fused" else (gemm, allreduce, norm)
 
     def run(fns):
         for st in sets:
@@ -403,6 +495,23 @@ def run_prefill(args, world, rank, local, dev, gloo):
     barrier()
     comm.check()
 
+    # parity self-check (untimed) on set 0: the fused tail and the unfused chain (scaled_mm_ partial -> two-shot
+    # vt_all_reduce -> vt_rms_norm_quant) against a torch float32 restatement over all ranks' partials
+    st0 = sets[0]
+    partial = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+    torch.ops.vllm_turing.scaled_mm_(partial, st0["a"], st0["w"].t(), st0["sa"], st0["sw"], None)
+    fz = dict(residual=st0["res"].clone(), residual0=st0["res"].clone(), norm_w=st0["nw"], eps=1e-6,
+              reduced=torch.empty(M, N, dtype=torch.bfloat16, device=dev),
+              q=torch.empty(M, N, dtype=torch.int8, device=dev))
+    comm.row_linear(st0["a"], st0["w"], st0["sa"], st0["sw"], residual=fz["residual"], norm_w=st0["nw"], eps=1e-6,
+                    q=fz["q"], scales=torch.empty(M, 1, dtype=torch.float32, device=dev), reduced=fz["reduced"])
+    chk = dict(reduced=comm.all_reduce(partial.clone()), residual=st0["res"].clone())
+    chk["q"], _ = rms_norm_dynamic_per_token_quant(chk["reduced"], st0["nw"], 1e-6, chk["residual"])
+    barrier()
+    comm.check()
+    parity = tail_parity(world, gloo, partial, fz, chk)
+    del partial, chk, fz
+
     def capture(fns):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
@@ -411,6 +520,8 @@ def run_prefill(args, world, rank, local, dev, gloo):
 
     g_step = capture(STEP)
     g_k = {"gemm": capture((gemm,)), "allreduce": capture((allreduce,)), "norm": capture((norm,))}
+    if args.tail == "fused":
+        g_k["fused"] = capture((fused,))
     barrier()
     with ClockSampler(local) as clk:
         t_w = time.perf_counter()
@@ -455,39 +566,58 @@ def run_prefill(args, world, rank, local, dev, gloo):
         d2h = o_q.numel() + o_s.numel() * 4 + o_res.numel() * 2
         e2e = {"value": 2.0 * M * N * K_full / t_e2e / 1e12, "unit": "TOPS", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": int(d2h), "us_per_layer": t_e2e * 1e6,
-               "api": "scaled_mm_ + TPComm.all_reduce + rms_norm_dynamic_per_token_quant, captured; host copies"}
+               "api": ("TPComm.row_linear (fused prefill tail)" if args.tail == "fused" else
+                       "scaled_mm_ + TPComm.all_reduce + rms_norm_dynamic_per_token_quant") + ", captured; host copies"}
         del g1
 
-    # roofline of the dominant part: the GEMM on the tensor cores (int8 dense = 2x the measured bf16 GEMM rate), or
-    # the all-reduce on NVLink (measured 770 GB/s peer copy per direction)
+    # roofline. The GEMM alone: int8 dense on the tensor cores against 2x the measured bf16 GEMM rate. The fused tail:
+    # its floor is the slower of the GEMM and the NVLink bus bytes 2 (n - 1) / n x 2 M N (the reduce-scatter inside the
+    # GEMM plus the all-gather) at the measured peer-copy bandwidth per direction; achieved = floor / measured time.
     ops_rank = 2.0 * M * N * K
     S = 2 * M * N
-    bus = 2.0 * (world - 1) / world * S / t_k["allreduce"] / 1e9 if world > 1 else 0.0
+    bus_bytes = 2.0 * (world - 1) / world * S
+    nvl, nvl_kind = nvlink_peak()
     try:
         with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
             int8_peak, pk = 2.0 * float(json.load(f)["bf16_tflops"]), "2x measured bf16 GEMM"
     except Exception:   # noqa: BLE001
         int8_peak, pk = 2.0 * 1590.0, "2x fallback bf16"
-    if t_k["gemm"] >= t_k["allreduce"] or world == 1:
-        ach = ops_rank / t_k["gemm"] / 1e12
-        roof = {"bound": "tensor", "kernel": "tc_gemm_kernel (prefill, 128 x 256 tiles)", "achieved": ach,
-                "peak": int8_peak, "unit": "TOP/s", "frac": ach / int8_peak, "traffic": None, "peak_kind": pk}
+    t_tail = t_k["fused"] if args.tail == "fused" else t_k["gemm"] + t_k["allreduce"] + t_k["norm"]
+    bus = bus_bytes / t_tail / 1e9 if world > 1 else 0.0
+    floor = max(ops_rank / (int8_peak * 1e12), bus_bytes / (nvl * 1e9))
+    gemm_ach = ops_rank / t_k["gemm"] / 1e12
+    if args.tail == "fused":
+        roof = {"bound": "tensor" if ops_rank / (int8_peak * 1e12) >= bus_bytes / (nvl * 1e9) else "nvlink",
+                "kernel": "tp_prefill_gemm_kernel + tp_prefill_tail_kernel (fused prefill tail)",
+                "achieved": floor / t_tail, "peak": 1.0, "unit": "fraction of max(GEMM floor, NVLink floor)",
+                "frac": floor / t_tail, "traffic": None, "floor_us": floor * 1e6,
+                "gemm_floor_us": ops_rank / (int8_peak * 1e12) * 1e6, "nvlink_floor_us": bus_bytes / (nvl * 1e9) * 1e6,
+                "gemm_alone": {"achieved": gemm_ach, "peak": int8_peak, "unit": "TOP/s", "frac": gemm_ach / int8_peak,
+                               "peak_kind": pk},
+                "nvlink_peak_gbs": nvl, "nvlink_peak_kind": nvl_kind, "peak_kind": pk}
+    elif t_k["gemm"] >= t_k["allreduce"] or world == 1:
+        roof = {"bound": "tensor", "kernel": "tc_gemm_kernel (prefill, 128 x 256 tiles)", "achieved": gemm_ach,
+                "peak": int8_peak, "unit": "TOP/s", "frac": gemm_ach / int8_peak, "traffic": None, "peak_kind": pk}
     else:
-        roof = {"bound": "nvlink", "kernel": "ar_twoshot_kernel", "achieved": bus, "peak": 770.0, "unit": "GB/s",
-                "frac": bus / 770.0, "traffic": None, "peak_kind": "measured peer copy per direction"}
+        ar_bus = bus_bytes / t_k["allreduce"] / 1e9
+        roof = {"bound": "nvlink", "kernel": "ar_twoshot_kernel", "achieved": ar_bus, "peak": nvl, "unit": "GB/s",
+                "frac": ar_bus / nvl, "traffic": None, "peak_kind": nvl_kind}
     line = {
         "metric": METRIC, "value": 2.0 * M * N * K_full / t_layer / 1e12, "unit": "TOPS", "n_gpus": world,
         "steps": K_steps, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic", "mode": "prefill",
         "us_per_layer": t_layer * 1e6, "bus_gbs": bus,
         "config": {"workload": f"prefill row-parallel tail M={M}: {args.proj} GEMM {K_full}/{world} -> {N} + two-shot "
-                               f"all-reduce + residual add + RMSNorm + int8 quant (BASELINE config 3)",
-                   "tokens": M, "tp": world, "K_local": K, "N": N, "layers_cycled": PREFILL_SETS,
+                               f"all-reduce + residual add + RMSNorm + int8 quant (BASELINE config 3), "
+                               + ("fused: reduce-scatter in the GEMM epilogue, reduce + all-gather + norm in one kernel"
+                                  if args.tail == "fused" else "unfused chain of three kernels"),
+                   "tokens": M, "tp": world, "K_local": K, "N": N, "layers_cycled": PREFILL_SETS, "tail": args.tail,
                    "l2": "inputs larger than L2 (three layer buffer sets cycled)", "launch": "CUDA graph",
                    "parallelism": f"tp{world}"},
         "kernel_us": {k: v * 1e6 for k, v in t_k.items()},
-        "roofline": roof, "clocks": clk.summary(), "gpu_launches": 3 * PREFILL_SETS * K_steps, "e2e": e2e,
-        "cpu_baseline": None,
+        "roofline": roof, "clocks": clk.summary(),
+        "gpu_launches": len(STEP) * PREFILL_SETS * K_steps * (2 if args.tail == "fused" else 1), "e2e": e2e,
+        "cpu_baseline": None, "parity": parity,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -724,6 +854,7 @@ def run_allreduce(args, world, rank, local, dev, gloo):
                      "nccl_bus_gbs": bus(res["nccl"]) if "nccl" in res else None})
         del x
     top = rows[-1]
+    nvl, nvl_kind = nvlink_peak()
     line = {
         "metric": METRIC, "value": top["bus_gbs"], "unit": "GB/s", "n_gpus": world, "steps": 1, "warmup": 3,
         "ms_per_step": top["us"] / 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -732,9 +863,124 @@ def run_allreduce(args, world, rank, local, dev, gloo):
                    "tp": world, "launch": "CUDA graph of R calls per size", "parallelism": f"tp{world}"},
         "sweep": rows,
         "roofline": {"bound": "nvlink", "kernel": "ar_twoshot_kernel (256 MB)", "achieved": top["bus_gbs"],
-                     "peak": 770.0, "unit": "GB/s", "frac": top["bus_gbs"] / 770.0, "traffic": None,
-                     "peak_kind": "measured peer copy per direction"},
+                     "peak": nvl, "unit": "GB/s", "frac": top["bus_gbs"] / nvl, "traffic": None,
+                     "peak_kind": nvl_kind, "frac_of_nominal_900": top["bus_gbs"] / 900.0},
         "gpu_launches": None, "e2e": None, "cpu_baseline": None,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    comm.close()
+    dist.destroy_process_group()
+
+
+def run_gemv(args, world, rank, local, dev, gloo):
+    """The decode-shape W8A8 GEMVs on one GPU: the dp4a GEMV (w8a8_gemv, the reference's kernel shape) and the tcgen05
+    decode kernel (w8a8_mma) at M = 1, 5, 8 on config 1's two shapes, each over enough weight copies to exceed L2,
+    captured in a CUDA graph; GB/s = algorithmic bytes N K + M K + 4 (M + N) + 2 M N per call / CUDA-event time."""
+    import torch
+
+    from vllm_turing_b200 import _build, w8a8
+    from vllm_turing_b200.synthetic import make_layer_inputs
+
+    _build.load()
+    hbm, pk = peaks()
+    stream = torch.cuda.current_stream()
+    rows = []
+    for (N, K) in ((HIDDEN, INTER), (2 * INTER, HIDDEN)):
+        copies = max(2, int(4 * L2_BYTES // (N * K)) + 1)
+        base = make_layer_inputs(8, N, K, seed=11, with_norm=False)
+        ws_ = [base.w.to(dev) for _ in range(copies)]
+        sw = base.sw.to(dev)
+        for M in (1, 5, 8):
+            a, sa = base.a[:M].contiguous().to(dev), base.sa[:M].contiguous().to(dev)
+            out = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+            w8a8.workspace(dev, M, N)
+            res = {}
+            for name, fn in (("dp4a_gemv", w8a8.gemv), ("tcgen05_decode", w8a8.mma)):
+                for w in ws_:
+                    fn(out, a, w.t(), sa, sw, None)
+                torch.cuda.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    for w in ws_:
+                        fn(out, a, w.t(), sa, sw, None)
+                g.replay()
+                torch.cuda.synchronize()
+                reps = 5
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(reps):
+                    g.replay()
+                e1.record(stream)
+                torch.cuda.synchronize()
+                t = e0.elapsed_time(e1) / 1e3 / (reps * copies)
+                alg = N * K + M * K + 4 * (M + N) + 2 * M * N
+                res[name] = {"us": t * 1e6, "gbs": alg / t / 1e9, "frac": alg / t / 1e9 / hbm}
+                del g
+            rows.append({"N": N, "K": K, "M": M, **res})
+        del ws_
+    best = max(r["dp4a_gemv"]["gbs"] for r in rows)
+    line = {
+        "metric": "decode W8A8 GEMV achieved HBM GB/s", "value": best, "unit": "GB/s", "n_gpus": 1, "steps": 5,
+        "warmup": 1, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic", "mode": "gemv", "hbm_peak_gbs": hbm, "peak_kind": pk, "sweep": rows,
+        "config": {"workload": "config 1 shapes (5120 <- 17408, 34816 <- 5120) at M = 1, 5, 8",
+                   "l2": "inputs larger than L2 (weight copies cycled)", "launch": "CUDA graph"},
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    dist_close()
+
+
+def dist_close():
+    import torch.distributed as dist
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+def run_p2p(args, world, rank, local, dev, gloo):
+    """NVLink peak for the rooflines: every rank copies B bytes into the next rank's region (a ring, so every GPU
+    sends and receives at once), by SM stores (the way this package's kernels move data) and by the copy engines
+    (cudaMemcpyAsync to the IPC-mapped peer address); GB/s per direction = B / t, CUDA events, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from vllm_turing_b200 import _build
+    from vllm_turing_b200.comm import TPComm
+
+    L = _build.load()
+    assert world >= 2, "--mode p2p needs at least two ranks"
+    B = 256 << 20
+    comm = TPComm(gloo, dev, big_bytes=B * world)
+    stream = torch.cuda.current_stream()
+    peer = (rank + 1) % world
+    res = {}
+    with ClockSampler(local) as clk:
+        for name, engine, ctas in (("sm_push", 0, 0), ("copy_engine", 1, 0), ("sm_push_1cta_per_sm", 0,
+                                                                                  torch.cuda.get_device_properties(
+                                                                                      dev).multi_processor_count)):
+            reps = 10
+            for _ in range(3):
+                assert L.vt_comm_peer_copy(comm.handle, peer, B, engine, ctas, stream.cuda_stream) == 0
+            torch.cuda.synchronize()
+            dist.barrier(group=gloo)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(reps):
+                assert L.vt_comm_peer_copy(comm.handle, peer, B, engine, ctas, stream.cuda_stream) == 0
+            b.record(stream)
+            torch.cuda.synchronize()
+            dist.barrier(group=gloo)
+            t = torch.tensor([a.elapsed_time(b) / reps / 1e3], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            res[name] = B / t.item() / 1e9
+    best = max(res.values())
+    line = {
+        "metric": "NVLink peer copy GB/s per direction (ring, every GPU sending and receiving)", "value": best,
+        "unit": "GB/s", "n_gpus": world, "steps": 10, "warmup": 3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bytes", "data": "synthetic", "mode": "p2p", "bytes": B, "by_method": res,
+        "nominal_gbs": 900.0, "frac_of_nominal": best / 900.0, "clocks": clk.summary(),
+        "config": {"workload": f"{B >> 20} MiB from each rank to the next, 10 copies", "parallelism": f"tp{world}"},
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -761,6 +1007,10 @@ def main():
         return run_allreduce(args, world, rank, local, dev, gloo)
     if args.mode == "lmhead":
         return run_lmhead(args, world, rank, local, dev, gloo)
+    if args.mode == "p2p":
+        return run_p2p(args, world, rank, local, dev, gloo)
+    if args.mode == "gemv":
+        return run_gemv(args, world, rank, local, dev, gloo)
     _build.load()
     M = args.tokens
     NL = args.layers
@@ -850,6 +1100,26 @@ def main():
         run(LAYER, layers)
     barrier()
     comm.check()
+
+    # ---- parity self-check (untimed) on layer 0's down projection: the fused kernel and the unfused chain
+    # (scaled_mm_ partial -> vt_all_reduce -> vt_rms_norm_quant) against a torch float32 restatement over every rank's
+    # partial; the same calls in the same order on every rank ----
+    from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant
+    s0 = layers[0]
+    a_p, sa_p = h_q.clone(), h_s.clone()
+    partial = torch.empty(M, HIDDEN, dtype=torch.bfloat16, device=dev)
+    torch.ops.vllm_turing.scaled_mm_(partial, a_p, s0["dn_w"].t(), sa_p, s0["dn_sw"], None)
+    res_before = residual.clone()
+    fused = dict(residual=residual.clone(), reduced=torch.empty(M, HIDDEN, dtype=torch.bfloat16, device=dev),
+                 q=torch.empty(M, HIDDEN, dtype=torch.int8, device=dev), residual0=res_before, norm_w=norm_w, eps=1e-6)
+    comm.row_linear(a_p, s0["dn_w"], sa_p, s0["dn_sw"], residual=fused["residual"], norm_w=norm_w, eps=1e-6,
+                    q=fused["q"], scales=torch.empty(M, 1, dtype=torch.float32, device=dev), reduced=fused["reduced"])
+    chain = dict(reduced=comm.all_reduce(partial.clone()), residual=residual.clone())
+    chain["q"], _ = rms_norm_dynamic_per_token_quant(chain["reduced"], norm_w, 1e-6, chain["residual"])
+    barrier()
+    comm.check()
+    parity = tail_parity(world, gloo, partial, fused, chain)
+    del a_p, sa_p, partial, fused, chain
 
     def capture(fns):
         g = torch.cuda.CUDAGraph()
@@ -973,7 +1243,7 @@ def main():
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "bytes_per_launch": alg[dom],
                      "peak_kind": peak_kind},
-        "clocks": clocks, "gpu_launches": len(LAYER) * NL * K, "e2e": e2e, "cpu_baseline": cpu,
+        "clocks": clocks, "gpu_launches": len(LAYER) * NL * K, "e2e": e2e, "cpu_baseline": cpu, "parity": parity,
     }
     if rank == 0:
         print(json.dumps(line), flush=True)

@@ -40,10 +40,16 @@ int w8a8_gemv_ws(const void *a, const void *w, const void *sa, const void *sw, c
  * allocator, or after handing all device memory to a pool): same arguments and results, but the split-K scratch is a
  * fixed array compiled into the library (about 1 MiB per GPU that loads it, held until exit), so the call allocates
  * nothing. Limits: M * N <= 262144 and N <= 262144, else VT_EARG. The first call on a device resolves the array's
- * address and must come before any stream capture; calls sharing a device must not overlap on the GPU (they share
- * the array). No counterpart in the reference (its GEMV needs no scratch). */
+ * address and, with lazy module loading (CUDA_MODULE_LOADING=LAZY, the default), may load the library's module and
+ * with it the array: make it before any stream capture and before the window in which nothing may be allocated.
+ * Calls sharing a device must not overlap on the GPU (they share the array). A device-side timeout inside the call
+ * is reported through vt_noalloc_status, not through the return code. No counterpart in the reference (its GEMV
+ * needs no scratch). */
 int w8a8_gemv_noalloc(const void *a, const void *w, const void *sa, const void *sw, const void *bias, void *out,
                       int M, int N, int K, int sa_rows, int sw_rows, int dtype, void *stream);
+/* Status word of w8a8_gemv_noalloc on the current device: 0, or the first timeout code its kernels reported (see
+ * vt_status for the codes); clear != 0 resets it. Synchronises the device; allocates nothing. New entry. */
+unsigned vt_noalloc_status(int clear);
 
 /* int32 accumulators acc[M, N] = a . w^T (bit-exact parity checks), M 1..16. New entry. */
 int vt_gemv_s32(const void *a, const void *w, void *acc, int M, int N, int K, void *stream);
@@ -186,6 +192,11 @@ int vt_ar8_dequant_sum(const void *gathered, void *out, long long n, int world, 
  * har_all_reduce (host_ar.cu:114-131) and ce_all_reduce (ce_ar.cu:103-146) for any rank count. */
 int vt_all_reduce(void *comm, const void *in, void *out, long long n, int dtype, int algo, void *stream);
 
+/* NVLink bandwidth probe: copies `bytes` (% 16 == 0, at most the two-shot chunk capacity) from this rank's region to
+ * rank `peer`'s region, by SM stores (engine 0; ctas CTAs, 0 = 4 per SM) or the copy engines (engine 1). Not a
+ * collective and not ordered with the communicator's calls: bracket it with barriers. New entry (measurement only). */
+int vt_comm_peer_copy(void *comm, int peer, long long bytes, int engine, int ctas, void *stream);
+
 /* gathered [world * m bytes] with this rank's payload pre-written at [rank * m, (rank + 1) * m); fills the peers'
  * slots. m % 8 == 0 (LL) or m % 16 == 0 (bulk). Replaces dag_all_gather (dma_ag.cu:45-74) for N ranks over P2P. */
 int vt_all_gather(void *comm, void *gathered, long long m, void *stream);
@@ -205,8 +216,22 @@ int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row
 int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,
                      const void *norm_w, float eps, void *q, void *scales, void *reduced, int M, int N, int K,
                      int dtype, void *stream);
+/* The fused row-parallel layer tail for prefill shapes (vt_tp_row_linear forwards M > 32 here): the tcgen05 GEMM's
+ * epilogue writes each finished 128 x 256 tile into the receive buffer of the rank that owns its rows (rank o owns rows
+ * [o M / world, (o + 1) M / world)) and flags it; a second kernel sums each owned row over the ranks in rank order,
+ * publishes it, pulls the peers' reduced rows over NVLink and runs residual add + RMSNorm + int8 quant on every row.
+ * Same arguments and results as vt_tp_row_linear (partials dequantised in the prefill GEMM's order sa[m] * (sw[n] *
+ * acc)); M % (128 * world) == 0, N % 8 == 0 with N / 8 / v a multiple of 32 in [64, 256] for some v <= 8,
+ * K % 16 == 0, residual / norm_w / reduced 16-byte and q 8-byte aligned; rows beyond the communicator's two-shot
+ * buffers run as several calls. Replaces the reference's prefill tail: scaled_mm_ (w8a8.py:108-117, w8a8_big) ->
+ * all-reduce (cear.py:75-87) -> rms_norm_dynamic_per_token_quant (tailoverlap.py:200), chunk-overlapped across two
+ * streams in the reference (tailoverlap.py:165-204). */
+int vt_tp_row_linear_prefill(void *comm, const void *a, const void *w, const void *sa, const void *sw,
+                             void *residual, const void *norm_w, float eps, void *q, void *scales, void *reduced,
+                             int M, int N, int K, int dtype, void *stream);
 /* Loads the fused kernels now (a lazily loaded module may synchronise behind a kernel spinning on a peer). */
 int vt_tp_preload(void);
+int vt_tp_prefill_preload(void);
 
 #ifdef __cplusplus
 }

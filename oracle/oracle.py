@@ -175,6 +175,16 @@ def add_rms_norm_quant(x_bits, residual_bits, weight_bits, eps, dtype=1, want_no
     return res, q, s, normed
 
 
+def row_linear_tp_big(a_list, w_list, sa_list, sw_list, residual_bits, weight_bits, eps, dtype=1):
+    """The TP layer tail with the prefill GEMM's dequant order (sa * (sw * acc), vllm_turing/csrc/w8a8_big.cu:26-35,
+    the order the reference's scaled_mm takes for M > 32, vllm_turing/w8a8.py:108-117): per rank gemm_s32 then
+    dequant_big, the rank-ordered all-reduce, then add_rms_norm_quant -> (new residual, q, scales, reduced)."""
+    parts = [dequant_big(gemm_s32(a, w), sa, sw, dtype) for a, w, sa, sw in zip(a_list, w_list, sa_list, sw_list)]
+    red = all_reduce(parts, dtype)
+    res, q, s, _ = add_rms_norm_quant(red, residual_bits, weight_bits, eps, dtype)
+    return res, q, s, red
+
+
 def row_linear_tp(a_list, w_list, sa_list, sw_list, residual_bits, weight_bits, eps, dtype=1):
     """The whole TP layer tail -> (new residual, q, scales, reduced)."""
     n = len(a_list)

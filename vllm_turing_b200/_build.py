@@ -21,7 +21,7 @@ _include = os.path.join(os.path.dirname(_here), "include")
 LIB_NAME = "libvllm_turing_b200.so"
 LIB_PATH = os.path.join(_here, LIB_NAME)
 SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "w8a16_tc.cu", "norm_quant.cu", "ar8.cu", "tp_comm.cu",
-           "tp_fused.cu")
+           "tp_fused.cu", "tp_prefill.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 _lib = None
 
@@ -109,6 +109,7 @@ SIGNATURES = {
     "w8a8_gemv_noalloc": (_I, [_P] * 6 + [_I] * 6 + [_P]),
     "vt_gemv_s32": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_status": (_U, [_I]),
+    "vt_noalloc_status": (_U, [_I]),
     "vt_workspace_nonzero": (_LL, [_LL]),
     "w8a8_mma": (_I, [_P] * 6 + [_I] * 6 + [_P]),
     "w8a8_mma_ws_bytes": (_SZ, [_I, _I]),
@@ -144,9 +145,12 @@ SIGNATURES = {
     "vt_comm_seq": (_U, [_P]),
     "vt_all_reduce": (_I, [_P, _P, _P, _LL, _I, _I, _P]),
     "vt_all_gather": (_I, [_P, _P, _LL, _P]),
+    "vt_comm_peer_copy": (_I, [_P, _I, _LL, _I, _I, _P]),
     "vt_all_gather_rows": (_I, [_P, _P, _LL, _LL, _LL, _P]),
     "vt_tp_row_linear": (_I, [_P] * 5 + [_P, _P, _F, _P, _P, _P] + [_I] * 4 + [_P]),
     "vt_tp_preload": (_I, []),
+    "vt_tp_row_linear_prefill": (_I, [_P] * 5 + [_P, _P, _F, _P, _P, _P] + [_I] * 4 + [_P]),
+    "vt_tp_prefill_preload": (_I, []),
 }
 
 

@@ -11,6 +11,9 @@
 //   RS                   two-shot reduce-scatter receive buffers [parity 2][src rank][chunk_cap bytes]
 //   AG                   two-shot reduced own chunk [parity 2][chunk_cap bytes] (pulled by peers)
 //   FLAGS                u32 flags [parity 2][kind 2][src rank][256 CTAs] (kind 0: RS data landed, 1: AG chunk ready)
+//   PF                   fused prefill row-linear: tile flags [parity 2][src rank][PF_MAX_TILES] (a source's GEMM
+//                        tile of this rank's rows landed in RS) and reduced-rows flags [parity 2][PF_MAX_CTAS] (this
+//                        rank's CTA j published its reduced rows in AG; peers poll them)
 //
 // Call protocol (the same call order on every rank, stream-ordered calls on each rank; cf. vllm_turing/cear.py:79):
 //   each launch reads seq = ctrl.seq + 1 at its start; the last of its CTAs to finish stores ctrl.seq = seq, so seq
@@ -33,10 +36,11 @@ constexpr size_t COMM_MBOX_OFF = 4096;
 constexpr size_t COMM_TICKET_OFF = 16384;
 constexpr int COMM_TICKETS = 4096;
 constexpr int COMM_MBOX_ROWS = 32, COMM_MBOX_GROUPS = 16;
+constexpr int PF_MAX_TILES = 4096, PF_MAX_CTAS = 1024;
 
 struct CommLayout {
     size_t ll_slot;       // bytes of one LL slot (= 2 x the data bytes it carries)
-    size_t ll_off, scratch_off, scratch_bytes, rs_off, ag_off, flags_off, total;
+    size_t ll_off, scratch_off, scratch_bytes, rs_off, ag_off, flags_off, pf_off, total;
     size_t chunk_cap;     // two-shot: bytes of one rank's chunk per call
 };
 
@@ -54,7 +58,8 @@ __host__ __device__ inline CommLayout comm_layout(int world, size_t ll_data, siz
     L.rs_off = L.scratch_off + L.scratch_bytes;
     L.ag_off = L.rs_off + 2 * (size_t)world * L.chunk_cap;
     L.flags_off = L.ag_off + 2 * L.chunk_cap;
-    L.total = L.flags_off + comm_align(2 * 2 * (size_t)COMM_MAX_RANKS * COMM_MAX_CTAS * 4);
+    L.pf_off = L.flags_off + comm_align(2 * 2 * (size_t)COMM_MAX_RANKS * COMM_MAX_CTAS * 4);
+    L.total = L.pf_off + comm_align(2 * (size_t)COMM_MAX_RANKS * PF_MAX_TILES * 4 + 2 * (size_t)PF_MAX_CTAS * 4);
     return L;
 }
 
@@ -85,6 +90,16 @@ struct CommView {
     __device__ __forceinline__ unsigned *flag(int dst, unsigned p, int kind, int src, int cta) const {
         return reinterpret_cast<unsigned *>(base[dst] + L.flags_off) +
                (((size_t)p * 2 + kind) * COMM_MAX_RANKS + src) * COMM_MAX_CTAS + cta;
+    }
+    // fused prefill: tile `tile` (numbered within the owner's rows) from `src` landed in rank `dst`'s RS buffer
+    __device__ __forceinline__ unsigned *pf_tile_flag(int dst, unsigned p, int src, int tile) const {
+        return reinterpret_cast<unsigned *>(base[dst] + L.pf_off) + ((size_t)p * COMM_MAX_RANKS + src) * PF_MAX_TILES +
+               tile;
+    }
+    // fused prefill: CTA `cta` of rank `owner` published its reduced rows in owner's AG buffer
+    __device__ __forceinline__ unsigned *pf_ag_flag(int owner, unsigned p, int cta) const {
+        return reinterpret_cast<unsigned *>(base[owner] + L.pf_off) + 2 * (size_t)COMM_MAX_RANKS * PF_MAX_TILES +
+               (size_t)p * PF_MAX_CTAS + cta;
     }
 };
 

@@ -37,6 +37,8 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_util.h"
 #include "tma_host.h"
@@ -310,6 +312,12 @@ __device__ __forceinline__ void tc_prefill_epilogue(const TcArgs &P, int m, int 
     }
 }
 
+// A finisher with `static constexpr bool kPrefillHooks` takes over the prefill orientation's tiles: the epilogue warps
+// call fin.prefill_tile(P, m, ta, tb, taddr) (thread = A row m of tile (ta, tb), its BN accumulators from TMEM column
+// 0 of taddr) and, after releasing the TMEM buffer, fin.prefill_tile_done(P, ta, tb) (all four epilogue warps).
+template <class F, class = void> struct TcPrefillHooks : std::false_type {};
+template <class F> struct TcPrefillHooks<F, std::void_t<decltype(F::kPrefillHooks)>> : std::true_type {};
+
 // The GEMM phase: every thread of the CTA (TC_THREADS) calls it; it returns after the CTA's pieces are done and its
 // TMEM is freed (a __syncthreads is the last thing it does, so the caller may reuse the shared memory). `fin` is the
 // calling thread's own finisher object: state it keeps (in the epilogue threads) is there after the phase.
@@ -516,10 +524,14 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                     flags[0] = 1;
                 }
                 tc_fence_after();
-                tc_prefill_epilogue<T, BN>(P, arow, tb, taddr);
+                if constexpr (TcPrefillHooks<Fin>::value)
+                    fin.prefill_tile(P, arow, ta, tb, taddr);   // the finisher's own destination for the tile
+                else
+                    tc_prefill_epilogue<T, BN>(P, arow, tb, taddr);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
+                if constexpr (TcPrefillHooks<Fin>::value) fin.prefill_tile_done(P, ta, tb);
             } else {
                 const int n = arow;
                 const bool nok = n < P.N;

@@ -236,6 +236,22 @@ __global__ void __launch_bounds__(AR_THREADS) ag_bulk_kernel(CommView c, char *_
     comm_end(c, seq);
 }
 
+// NVLink bandwidth probe: this rank's AG buffer -> a peer's RS buffer (the slot of this rank), 16-byte stores with
+// TS_UNROLL loads in flight per thread over a grid-stride loop. Touches no flags and no call number.
+__global__ void __launch_bounds__(AR_THREADS) peer_push_kernel(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
+                                                               long long U) {
+    const long long nt = (long long)gridDim.x * blockDim.x;
+    for (long long u0 = (long long)blockIdx.x * blockDim.x + threadIdx.x; u0 < U; u0 += TS_UNROLL * nt) {
+        uint4 v[TS_UNROLL];
+#pragma unroll
+        for (int k = 0; k < TS_UNROLL; ++k)
+            if (u0 + k * nt < U) v[k] = src[u0 + k * nt];
+#pragma unroll
+        for (int k = 0; k < TS_UNROLL; ++k)
+            if (u0 + k * nt < U) dst[u0 + k * nt] = v[k];
+    }
+}
+
 template <typename K>
 static void preload(K k) {
     cudaFuncAttributes fa;
@@ -420,6 +436,24 @@ int vt_all_gather(void *comm, void *gathered, long long m, void *stream) {
         if (cudaError_t e = cudaGetLastError()) return (int)e;
     }
     return 0;
+}
+
+// NVLink bandwidth probe (bench.py --mode p2p): copies `bytes` (% 16 == 0, <= the two-shot chunk capacity) from this
+// rank's AG buffer into rank `peer`'s RS buffer, with SM stores (engine 0: grid of `ctas` CTAs, 0 = 4 per SM) or the
+// copy engines (engine 1: cudaMemcpyAsync to the IPC-mapped peer address). Not a collective: the caller brackets it
+// with barriers and runs no other call on the communicator meanwhile. The copied bytes are meaningless.
+int vt_comm_peer_copy(void *comm, int peer, long long bytes, int engine, int ctas, void *stream) {
+    Comm *c = reinterpret_cast<Comm *>(comm);
+    if (!c || peer < 0 || peer >= c->v.world || bytes <= 0 || (bytes & 15) ||
+        bytes > (long long)c->v.L.chunk_cap)
+        return VT_EARG;
+    const char *src = c->v.base[c->v.rank] + c->v.L.ag_off;
+    char *dst = c->v.base[peer] + c->v.L.rs_off + (size_t)c->v.rank * c->v.L.chunk_cap;
+    cudaStream_t s = (cudaStream_t)stream;
+    if (engine == 1) return (int)cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice, s);
+    const int g = ctas > 0 ? ctas : 4 * num_sms(c->dev);
+    peer_push_kernel<<<g, AR_THREADS, 0, s>>>((uint4 *)dst, (const uint4 *)src, bytes >> 4);
+    return (int)cudaGetLastError();
 }
 
 // Row-strided all-gather: gathered [rows, ld_bytes] holds world column blocks of row_bytes per row; this rank's block

@@ -507,15 +507,25 @@ using namespace vt;
 
 extern "C" {
 
+// tp_prefill.cu
+int vt_tp_row_linear_prefill(void *comm, const void *a, const void *w, const void *sa, const void *sw,
+                             void *residual, const void *norm_w, float eps, void *q, void *scales, void *reduced,
+                             int M, int N, int K, int dtype, void *stream);
+int vt_tp_prefill_preload(void);
+
 // The fused row-parallel layer tail on communicator `comm` (all ranks call it in the same order with the same M, N):
 //   a [M, K] int8 (this rank's activation slice), w [N, K] int8 (this rank's weight slice), sa [M], sw [N] float32;
 //   residual [M, N] (updated in place), norm_w [N], eps, q [M, N] int8, scales [M] float32 -- or residual = NULL for
 //   a plain row-linear + all-reduce; reduced [M, N] (optional; required without residual) receives the all-reduced
-//   sum. dtype 0 fp16 / 1 bf16. 1 <= M <= 32, N % 4 == 0, K % 16 == 0, M * N * 2 <= the communicator's LL capacity.
+//   sum. dtype 0 fp16 / 1 bf16. 1 <= M <= 32: this file's one-kernel decode tail (N % 4 == 0, K % 16 == 0,
+//   M * N * 2 <= the communicator's LL capacity); M > 32: the prefill tail of tp_prefill.cu (its requirements).
 int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,
                      const void *norm_w, float eps, void *q, void *scales, void *reduced, int M, int N, int K,
                      int dtype, void *stream) {
     Comm *ch = reinterpret_cast<Comm *>(comm);
+    if (ch && M > COMM_MBOX_ROWS)
+        return vt_tp_row_linear_prefill(comm, a, w, sa, sw, residual, norm_w, eps, q, scales, reduced, M, N, K, dtype,
+                                        stream);
     if (!ch || M < 1 || M > COMM_MBOX_ROWS || N < 4 || (N & 3) || K < 16 || (K & 15) || ((uintptr_t)a & 15) ||
         ((uintptr_t)w & 15))
         return VT_EARG;
@@ -545,6 +555,7 @@ int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, c
 int vt_tp_preload(void) {
     preload_fused<__half>();
     preload_fused<__nv_bfloat16>();
+    if (int rc = vt_tp_prefill_preload()) return rc;
     return (int)cudaGetLastError();
 }
 

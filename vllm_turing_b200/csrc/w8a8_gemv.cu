@@ -246,6 +246,24 @@ int w8a8_gemv_noalloc(const void *a, const void *w, const void *sa, const void *
     return gemv_dequant<__nv_bfloat16>(a, w, sa, sw, bias, out, M, N, K, sa_rows, sw_rows, partials, status, s);
 }
 
+// The status word of w8a8_gemv_noalloc on the current device (the first word of its fixed array): 0, or the first
+// timeout code one of its kernels reported (a pipeline wait that gave up leaves `out` wrong while the call itself
+// returned 0). clear != 0 resets it. Synchronises the device; allocates nothing. 0xffffffff if the array's address
+// cannot be resolved.
+unsigned vt_noalloc_status(int clear) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return 0xffffffffu;
+    int *base = noalloc_scratch_ptr(dev);
+    if (!base) return 0xffffffffu;
+    unsigned v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&v, base, 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return 0xffffffffu;
+    }
+    if (clear && cudaMemset(base, 0, 4) != cudaSuccess) cudaGetLastError();
+    return v;
+}
+
 // Number of non-zero 32-bit words in the first `bytes` of the current device's library workspace scratch (every
 // kernel that uses it leaves it zeroed; tests check that invariant). Synchronises the device; -1 on error.
 long long vt_workspace_nonzero(long long bytes) {
