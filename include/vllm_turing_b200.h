@@ -156,6 +156,45 @@ int ce_free(void *ptr);
 /* Single-process use: peer access from the current device to `peer`. 0 ok, 1 failed. (ce_ar.cu:95-99) */
 int ce_enable_peer(int peer);
 
+/* ---- the reference's two-rank transports, same names / signatures / return codes, B200 kernels ----------------
+ * Waits are bounded (VLLM_TURING_AR_TIMEOUT_MS); a wait that runs out reports into vt_status. */
+
+/* Loads the kernels below and creates the library workspace (call once per device, before any capture). 0 ok.
+ * Replaces vllm_turing/csrc/host_ar.cu:86-92. */
+int har_preload(void);
+/* Blocks of the LL all-reduce for nwords data words: the number of zeroed int32 call counters the caller keeps.
+ * Replaces vllm_turing/csrc/host_ar.cu:94-96 (the block size differs; callers size their counters with it). */
+int har_blocks(int nwords);
+/* cudaHostRegister (mapped, portable) of a host range; its device pointer or NULL. Replaces host_ar.cu:99-108. */
+void *har_register(void *ptr, size_t size);
+/* cudaHostUnregister; returns the cudaError. Replaces host_ar.cu:110-112. */
+int har_unregister(void *ptr);
+/* Two-rank LL all-reduce: out[nwords 32-bit words] = in + the peer's in (dtype 0 fp16 / 1 bf16, float32 sum rounded
+ * once). my_ll: where this rank's LL words go (the peer's region, or a mapped host segment); peer_ll: where the peer's
+ * arrive; each 2 * slot_words 8-byte words (two parity slots of {data word, call number}); counters: har_blocks(
+ * slot_words) zeroed ints of this rank. -1 if nwords > slot_words, else the launch's cudaError. CUDA-graph capturable.
+ * Replaces host_ar.cu:115-131. */
+int har_all_reduce(const void *in, void *out, int nwords, int dtype, void *my_ll, const void *peer_ll, void *counters,
+                   int slot_words, void *stream);
+/* 0: ce_all_reduce can run (it needs no driver entry points here). Replaces vllm_turing/csrc/ce_ar.cu:101. */
+int ce_driver_ok(void);
+/* Two-rank fp16 all-reduce over IPC-shared buffers my / peer (256 bytes of flags, then R1 and R2 of cap bytes, from
+ * ce_alloc / ce_open): out[n] = x + the peer's x, n % 16 == 0, 16-byte aligned; seq = 1, 2, ... in the same order on
+ * both ranks; blocks is accepted and unused. One SM kernel (two-shot over NVLink stores, a flag pair per slice).
+ * Returns 0, 2 bad arguments, 3 cap too small, 7 launch failed. Replaces ce_ar.cu:103-146 (copy engines and stream
+ * waits there). */
+int ce_all_reduce(const void *x, void *out, long n, int rank, void *my, void *peer, long cap, unsigned seq, int blocks,
+                  void *stream);
+/* cudaHostRegister of the staging segment; the device pointer of its start or NULL. Replaces vllm_turing/csrc/dma_ag.cu:26-41. */
+void *dag_register(void *host, size_t bytes);
+/* Two-rank all-gather through registered host staging: gathered (2 m bytes, this rank's half pre-written on main_);
+ * my_stage / peer_stage host pointers of m bytes; my_flag_dev / peer_flag_dev device pointers of P int32 piece flags;
+ * seq the call number (flags compared with >=). One kernel on main_; d2h_, h2d_ and the events are accepted and
+ * unused. 0 ok, 1 failure. Replaces dma_ag.cu:41-74. */
+int dag_all_gather(void *gathered, long long m, int rank, void *my_stage, const void *peer_stage, int *my_flag_dev,
+                   const int *peer_flag_dev, int seq, int P, void *main_, void *d2h_, void *h2d_, void *ev0, void *ev1,
+                   void *ev2);
+
 /* ---- tensor-parallel communicator (N = 1..8 ranks, one process per GPU, NVLink P2P) ---------------------------
  * Replaces the reference's two-rank transports (DevLLAllReduce over har_all_reduce, vllm_turing/hostar.py:152-188 /
  * host_ar.cu:114-131; CeAllReduce over ce_all_reduce, cear.py:52-87 / ce_ar.cu:103-146; DmaAllGather over

@@ -106,6 +106,7 @@ def test_all_reduce_world1(comm1, n, algo):
 # ---- prefill shapes (M > 32): GEMM with the reduce-scatter in its epilogue, then reduce + row epilogue ----
 @pytest.mark.parametrize("M,N,K", [(128, 5120, 4352), (256, 5120, 512), (384, 1024, 2176), (256, 2048, 1040)])
 def test_prefill_fused_tp1_vs_oracle_and_chain(comm1, M, N, K):
+    from vllm_turing_b200 import w8a8  # noqa: F401  (registers vllm_turing::scaled_mm_)
     from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant
     li = _inputs(M, N, K, seed=M + N + K)
     a, w, sa, sw, nw = li.a.cuda(), li.w.cuda(), li.sa.cuda(), li.sw.cuda(), li.norm_w.cuda()

@@ -21,7 +21,7 @@ _include = os.path.join(os.path.dirname(_here), "include")
 LIB_NAME = "libvllm_turing_b200.so"
 LIB_PATH = os.path.join(_here, LIB_NAME)
 SOURCES = ("w8a8_gemv.cu", "w8a8_tc.cu", "gate_up_silu.cu", "w8a16_tc.cu", "norm_quant.cu", "ar8.cu", "tp_comm.cu",
-           "tp_fused.cu", "tp_prefill.cu")
+           "tp_fused.cu", "tp_prefill.cu", "ref_abi.cu")
 ARCH = ("-gencode", "arch=compute_100a,code=sm_100a")
 _lib = None
 
@@ -136,6 +136,15 @@ SIGNATURES = {
     "ce_close": (_I, [_P]),
     "ce_free": (_I, [_P]),
     "ce_enable_peer": (_I, [_I]),
+    "ce_driver_ok": (_I, []),
+    "ce_all_reduce": (_I, [_P, _P, ctypes.c_long, _I, _P, _P, ctypes.c_long, _U, _I, _P]),
+    "har_preload": (_I, []),
+    "har_blocks": (_I, [_I]),
+    "har_register": (_P, [_P, _SZ]),
+    "har_unregister": (_I, [_P]),
+    "har_all_reduce": (_I, [_P, _P, _I, _I, _P, _P, _P, _I, _P]),
+    "dag_register": (_P, [_P, _SZ]),
+    "dag_all_gather": (_I, [_P, _LL, _I, _P, _P, _P, _P, _I, _I] + [_P] * 6),
     "vt_comm_region_bytes": (_SZ, [_I, _SZ, _SZ, _SZ]),
     "vt_comm_create": (_P, [_I, _I, ctypes.POINTER(ctypes.c_void_p), _SZ, _SZ, _SZ]),
     "vt_comm_destroy": (_I, [_P]),

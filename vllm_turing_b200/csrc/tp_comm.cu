@@ -266,7 +266,12 @@ extern "C" {
 
 // ---- IPC helpers (the reference's names and semantics, vllm_turing/csrc/ce_ar.cu:77-101) ----------------------------
 // A zeroed device buffer and its 64-byte CUDA IPC handle. 0 ok; 1 cudaMalloc, 2 memset, 3 sync, 4 handle failed.
+int har_preload(void);   // ref_abi.cu
+
 int ce_alloc(size_t bytes, void **ptr, void *handle) {
+    // load the two-rank kernels now (ce_ar.cu:79-81 preloads its add kernel for the same reason: a lazily loaded
+    // module's first launch synchronises, behind a peer that may already be spinning)
+    if (har_preload() != 0) return 5;
     if (cudaMalloc(ptr, bytes) != cudaSuccess) return 1;
     if (cudaMemset(*ptr, 0, bytes) != cudaSuccess) return 2;
     if (cudaDeviceSynchronize() != cudaSuccess) return 3;
