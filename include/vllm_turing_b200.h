@@ -201,6 +201,12 @@ int dag_all_gather(void *gathered, long long m, int rank, void *my_stage, const 
  * dag_all_gather, dmaag.py:107-119 / dma_ag.cu:45-74). All ranks must make the same calls in the same order; calls
  * on one communicator must be stream-ordered on each rank. Call counting is device-resident (CUDA-graph safe). */
 
+/* Bounds of the device-side waits of launches made from now on, in milliseconds (<= 0 keeps a bound): pipe_ms for
+ * waits inside one CTA, peer_ms for waits on other CTAs or GPUs; initially VLLM_TURING_PIPE_TIMEOUT_MS (2000) and
+ * VLLM_TURING_AR_TIMEOUT_MS (10000). A wait that runs out records its code in the status word and the kernel returns.
+ * Returns 0. New entry. */
+int vt_set_wait_bounds(double pipe_ms, double peer_ms);
+
 /* Bytes of the per-rank region: ll_data = largest one-shot / fused message (bytes), big_data = largest two-shot
  * message per launch (bytes; larger ones run in pieces), scratch_ints = split-K scratch of the fused row-linear in
  * int32 words (>= M * N for the GEMV phase, >= SMs * 128 * ceil(M / 2) * 4 for the tcgen05 phase). */

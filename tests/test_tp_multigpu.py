@@ -11,6 +11,7 @@ torch.multiprocessing.spawn, a gloo group for set-up, tests/test_hostar.py:13-20
   - 64 back-to-back calls without host syncs, and a captured CUDA graph of mixed calls replayed with fresh inputs
     (tests/test_hostar.py:33-54).
 Skipped with fewer than 2 GPUs."""
+import ctypes
 import os
 import socket
 import traceback
@@ -32,6 +33,91 @@ def _free_port():
 def _parts(n, world, seed, dtype):
     return [(torch.randn(n, generator=torch.Generator().manual_seed(seed * 100 + r)) * 4).to(dtype)
             for r in range(world)]
+
+
+def _ref_abi_two_ranks(L, rank, dev, check):
+    """The reference's two-rank entry points with a real peer (vllm_turing/hostar.py:152-188, cear.py:52-87,
+    dmaag.py:60-119 set them up the same way): har_all_reduce over IPC-shared device LL regions (push mode),
+    ce_all_reduce over IPC-shared flag + receive buffers, dag_all_gather through a shared host segment."""
+    import numpy as np
+    import torch.distributed as dist
+    from multiprocessing import shared_memory
+
+    from oracle import oracle as O
+
+    s = torch.cuda.current_stream().cuda_stream
+
+    def shared_region(nbytes):
+        p, h = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        assert L.ce_alloc(nbytes, ctypes.byref(p), h) == 0
+        hs = [None, None]
+        dist.all_gather_object(hs, h.raw)
+        qp = ctypes.c_void_p()
+        assert L.ce_open(ctypes.create_string_buffer(hs[1 - rank], 64), ctypes.byref(qp)) == 0
+        return p.value, qp.value
+
+    # har: LL words pushed into the peer's region, the peer's polled in the own one
+    slot_words = 32768
+    local, remote = shared_region(2 * slot_words * 8)
+    counters = torch.zeros(L.har_blocks(slot_words), dtype=torch.int32, device=dev)
+    for i, n in enumerate((5 * 5120, 24 * 5120, 2 * 777, 5 * 5120)):
+        xs = [(torch.randn(n, generator=torch.Generator().manual_seed(60 + 2 * i + r)) * 3).to(torch.bfloat16)
+              for r in range(2)]
+        out = torch.empty(n, dtype=torch.bfloat16, device=dev)
+        xd = xs[rank].to(dev)
+        check(L.har_all_reduce(xd.data_ptr(), out.data_ptr(), n // 2, 1, remote, local, counters.data_ptr(),
+                               slot_words, s) == 0, "har_all_reduce launch")
+        torch.cuda.synchronize()
+        want = O.all_reduce([O.to_bits(x) for x in xs], 1)
+        check(np.array_equal(O.to_bits(out.cpu()), want), f"har_all_reduce n={n}")
+    # ce: two-shot over the IPC buffers, host-side call numbers
+    cap = 8 << 20
+    my, peer = shared_region(256 + 2 * cap)
+    for seq, n in enumerate((2048 * 5120 // 4, 16 * 999, 5120 * 64), start=1):
+        xs = [(torch.randn(n, generator=torch.Generator().manual_seed(80 + 2 * seq + r)) * 2).half() for r in range(2)]
+        out = torch.empty(n, dtype=torch.float16, device=dev)
+        xd = xs[rank].to(dev)
+        check(L.ce_all_reduce(xd.data_ptr(), out.data_ptr(), n, rank, my, peer, cap, seq, 8, s) == 0, "ce launch")
+        torch.cuda.synchronize()
+        check(np.array_equal(O.to_bits(out.cpu()), O.all_reduce([O.to_bits(x) for x in xs], 0)),
+              f"ce_all_reduce n={n}")
+    # dag: per rank [2 parity buffers of CAP bytes][2 x 4096 bytes of flags] in one shared host segment
+    CAP, FB, P = 4 << 20, 4096, 8
+    region = 2 * CAP + 2 * FB
+    name = [None]
+    shm = shared_memory.SharedMemory(create=True, size=2 * region) if rank == 0 else None
+    if rank == 0:
+        name[0] = shm.name
+    dist.broadcast_object_list(name, src=0)
+    if rank != 0:
+        shm = shared_memory.SharedMemory(name=name[0])
+    try:
+        base = ctypes.addressof(ctypes.c_char.from_buffer(shm.buf))
+        if rank == 0:
+            ctypes.memset(base, 0, 2 * region)
+        dist.barrier()
+        dbase = L.dag_register(base, 2 * region)
+        check(bool(dbase), "dag_register")
+        for seq, m in enumerate((3 << 20, 5 * 1024 + 16, CAP), start=1):
+            b = seq & 1
+            payload = [torch.randint(0, 256, (m,), generator=torch.Generator().manual_seed(90 + 2 * seq + r),
+                                     dtype=torch.uint8) for r in range(2)]
+            g = torch.zeros(2 * m, dtype=torch.uint8, device=dev)
+            g[rank * m:(rank + 1) * m] = payload[rank].to(dev)
+            stage = lambda r: base + r * region + b * CAP   # noqa: E731
+            flags = lambda r: dbase + r * region + 2 * CAP + b * FB   # noqa: E731
+            check(L.dag_all_gather(g.data_ptr(), m, rank, stage(rank), stage(1 - rank), flags(rank),
+                                   flags(1 - rank), seq, P, s, None, None, None, None, None) == 0, "dag launch")
+            torch.cuda.synchronize()
+            check(torch.equal(g.cpu(), torch.cat(payload)), f"dag_all_gather m={m}")
+        dist.barrier()
+        L.har_unregister(base)
+    finally:
+        dist.barrier()
+        shm.close()
+        if rank == 0:
+            shm.unlink()
+    check(L.vt_status(1) == 0, "a wait of the two-rank transports timed out")
 
 
 def _worker(rank, world, port, q):
@@ -244,6 +330,8 @@ def _worker(rank, world, port, q):
         del g
         st = comm.status(clear=True)
         check(st == 0, f"device status {st:#x}")
+        if world == 2:
+            _ref_abi_two_ranks(comm.L, rank, dev, check)
         comm.close()
         dist.destroy_process_group()
     except Exception:   # noqa: BLE001

@@ -145,6 +145,7 @@ SIGNATURES = {
     "har_all_reduce": (_I, [_P, _P, _I, _I, _P, _P, _P, _I, _P]),
     "dag_register": (_P, [_P, _SZ]),
     "dag_all_gather": (_I, [_P, _LL, _I, _P, _P, _P, _P, _I, _I] + [_P] * 6),
+    "vt_set_wait_bounds": (_I, [ctypes.c_double, ctypes.c_double]),
     "vt_comm_region_bytes": (_SZ, [_I, _SZ, _SZ, _SZ]),
     "vt_comm_create": (_P, [_I, _I, ctypes.POINTER(ctypes.c_void_p), _SZ, _SZ, _SZ]),
     "vt_comm_destroy": (_I, [_P]),

@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include <stdlib.h>
 
+#include <atomic>
 #include <mutex>
 #include <utility>
 
@@ -59,15 +60,17 @@ inline uint64_t env_ns(const char *name, double default_ms) {
 }
 
 // Bound on waits inside one CTA (bulk copies, MMA completion): a healthy kernel waits microseconds.
-inline uint64_t pipe_timeout_ns() {
-    static uint64_t v = env_ns("VLLM_TURING_PIPE_TIMEOUT_MS", 2000.0);
+inline std::atomic<uint64_t> &pipe_timeout_slot() {
+    static std::atomic<uint64_t> v{env_ns("VLLM_TURING_PIPE_TIMEOUT_MS", 2000.0)};
     return v;
 }
+inline uint64_t pipe_timeout_ns() { return pipe_timeout_slot().load(std::memory_order_relaxed); }
 // Bound on waits for other CTAs or other GPUs (LL words of peers): ranks may enter a call far apart in time.
-inline uint64_t peer_timeout_ns() {
-    static uint64_t v = env_ns("VLLM_TURING_AR_TIMEOUT_MS", 10000.0);
+inline std::atomic<uint64_t> &peer_timeout_slot() {
+    static std::atomic<uint64_t> v{env_ns("VLLM_TURING_AR_TIMEOUT_MS", 10000.0)};
     return v;
 }
+inline uint64_t peer_timeout_ns() { return peer_timeout_slot().load(std::memory_order_relaxed); }
 
 // Programmatic dependent launch for the decode-chain kernels (tcgen05 GEMMs, fused row-linear, row-split SiLU-quant):
 // VLLM_TURING_PDL=0 turns it off.

@@ -298,6 +298,16 @@ int ce_enable_peer(int peer) {
     return e == cudaSuccess ? 0 : 1;
 }
 
+// The bounds of the device-side waits for launches from now on (milliseconds; <= 0 keeps a bound): pipe = waits inside
+// one CTA (bulk copies, MMA completion), peer = waits for other CTAs or GPUs. The environment variables
+// VLLM_TURING_PIPE_TIMEOUT_MS / VLLM_TURING_AR_TIMEOUT_MS set the initial values. A CUDA graph keeps the bounds its
+// kernels were captured with. Returns 0.
+int vt_set_wait_bounds(double pipe_ms, double peer_ms) {
+    if (pipe_ms > 0) pipe_timeout_slot().store((uint64_t)(pipe_ms * 1e6));
+    if (peer_ms > 0) peer_timeout_slot().store((uint64_t)(peer_ms * 1e6));
+    return 0;
+}
+
 // ---- communicator ------------------------------------------------------------------------------------------------------
 size_t vt_comm_region_bytes(int world, size_t ll_data, size_t big_data, size_t scratch_ints) {
     if (world < 1 || world > COMM_MAX_RANKS) return 0;

@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1) tp_prefill_tail_kernel(con
             for (int i = t; i < W * A.ntb; i += tpr) {
                 const int src = i / A.ntb, tb = i - src * A.ntb;
                 if (!dead && !flag_wait(c.pf_tile_flag(me, p, src, rb * A.ntb + tb), seq, deadline)) {
-                    report(c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)src);
+                    report(c.status(), ST_PEER_TIMEOUT | 0xb00u | (unsigned)src);
                     dead = true;
                 }
             }
@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1) tp_prefill_tail_kernel(con
         for (int k = 1; k < W; ++k) {
             const int src = (me + k) % W;
             if (threadIdx.x == 0 && !dead && !flag_wait(c.pf_ag_flag(src, p, blockIdx.x), seq, deadline)) {
-                report(c.status(), ST_PEER_TIMEOUT | 0x600u | (unsigned)src);
+                report(c.status(), ST_PEER_TIMEOUT | 0xc00u | (unsigned)src);
                 dead = true;
             }
             __syncthreads();
