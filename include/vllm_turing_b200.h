@@ -89,7 +89,7 @@ int vt_gemm_s32(const void *a, const void *w, void *acc, int M, int N, int K, vo
  * sa [M] (sa_rows = 1) or [1]. Bit-identical to w8a8_mma / scaled_mm_ with the plain weight followed by
  * silu_mul_quant. 1 <= M <= 32, I % 64 == 0, K % 16 == 0; a 256-byte aligned workspace of
  * vt_gate_up_silu_quant_ws_bytes(M, I) bytes, zeroed once before first use; calls sharing it must be stream-ordered.
- * dtype (0 fp16 / 1 bf16): the type of the gate / up / product values. Replaces the pair scaled_mm_ (w8a8.py:235-244)
+ * dtype (0 fp16 / 1 bf16): the type of the gate / up / product values. Replaces the pair scaled_mm_ (w8a8.py:108-117)
  * + silu_mul_quant (silu_quant.cu:71-77, tailoverlap.py:148-151). */
 size_t vt_gate_up_silu_quant_ws_bytes(int M, int I);
 int vt_gate_up_silu_quant(const void *a, const void *w, const void *sa, const void *sw, void *q, void *scales, int M,
@@ -256,7 +256,7 @@ int vt_all_gather_rows(void *comm, void *gathered, long long rows, long long row
  * with VLLM_TURING_FUSED_GEMV=1) -> all-reduce over the communicator -> residual add (in place) -> RMSNorm * norm_w
  * -> per-token int8 q / scales. residual = NULL: plain row-linear + all-reduce into `reduced`. 1 <= M <= 32,
  * N % 4 == 0, K % 16 == 0, M * N * 2 <= ll_data, M * N <= scratch_ints. Replaces the reference's
- * decode tail: scaled_mm_ (w8a8.py:235-244) -> tensor_model_parallel_all_reduce (hostar.py:260-278) ->
+ * decode tail: scaled_mm_ (w8a8.py:108-117) -> tensor_model_parallel_all_reduce (hostar.py:260-278) ->
  * rms_norm_dynamic_per_token_quant (tailoverlap.py:200). */
 int vt_tp_row_linear(void *comm, const void *a, const void *w, const void *sa, const void *sw, void *residual,
                      const void *norm_w, float eps, void *q, void *scales, void *reduced, int M, int N, int K,

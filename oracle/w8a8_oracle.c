@@ -96,7 +96,7 @@ void orc_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int M, int N, 
 /* ---- per-token x per-channel dequant epilogue ----------------------------------------------------------------------
  * out[m, n] = round_dtype(((float)acc * sa[m]) * sw[n] + bias[n]).
  * Reference: vllm_turing/csrc/w8a8_gemv.cu:87-91 (`(float) acc[r][m] * sa[sa_rows ? m : 0] * swn + b`, which nvcc
- * contracts to fma(acc * sa, sw, b)); sa_rows / sw_rows = 0 selects a per-tensor scale (w8a8.py:212-214). Without a
+ * contracts to fma(acc * sa, sw, b)); sa_rows / sw_rows = 0 selects a per-tensor scale (w8a8.py:45). Without a
  * bias the expression is the plain product (fma with +0 differs only in the sign of an exact zero, which acc * sa * sw
  * with positive scales never produces except as +0). */
 void orc_dequant(const int32_t *acc, const float *sa, const float *sw, const uint16_t *bias, uint16_t *out, int M,
@@ -127,7 +127,7 @@ void orc_dequant_big(const int32_t *acc, const float *sa, const float *sw, uint1
     }
 }
 
-/* cutlass_scaled_mm semantics as the reference plugin serves them (vllm_turing/w8a8.py:235-244 -> gemv / mma). */
+/* cutlass_scaled_mm semantics as the reference plugin serves them (vllm_turing/w8a8.py:108-117 -> gemv / mma). */
 void orc_scaled_mm(const int8_t *a, const int8_t *w, const float *sa, const float *sw, const uint16_t *bias,
                    uint16_t *out, int M, int N, int K, int sa_rows, int sw_rows, int dtype) {
     int32_t *acc = (int32_t *)malloc(sizeof(int32_t) * (size_t)M * (size_t)N);

@@ -2,7 +2,8 @@
 """Generate the committed golden vectors that pin the CPU oracle to the reference.
 
 Run in a container where the reference tree is present (it is NOT needed at test time):
-    python tests/golden/make_golden.py --ref /root/reference
+    python tests/golden/make_golden.py [--ref <reference tree>]
+(default: VLLM_TURING_REFERENCE, else the directory `reference` beside this repository)
 Writes tests/golden/golden.npz. Every output is produced by the reference's own code where it is Python, and by the
 exact formulas the reference's tests compute where the reference is CUDA:
 
@@ -99,7 +100,8 @@ def tiny_checkpoint(path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("VLLM_TURING_REFERENCE")
+                    or os.path.join(os.path.dirname(REPO), "reference"))
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = ap.parse_args()
     sys.path.insert(0, args.ref)

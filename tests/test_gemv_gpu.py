@@ -28,7 +28,7 @@ def test_s32_golden_cases(golden, case):
 @pytest.mark.parametrize("M", [1, 2, 3, 4, 5, 6, 7, 8, 10, 13, 16])
 @pytest.mark.parametrize("NK", [(5120, 3072), (1000, 5136), (300, 5168), (40, 256)])
 def test_s32_shapes(M, NK):
-    """M sweep x the reference's odd shapes (tests/test_w8a8_mma.py:113-114: K % 128 = 16, N % 16 = 8)."""
+    """M sweep x the reference's odd shapes (tests/test_w8a8_mma.py:65-66: K % 128 = 16, N % 16 = 8)."""
     from vllm_turing_b200 import w8a8
     N, K = NK
     a, w = rand_int8((M, K), M * 7 + K), rand_int8((N, K), N * 11 + K)
@@ -58,7 +58,7 @@ def test_scaled_mm_bit_exact(dtype, M, N, K):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_bias_and_per_tensor_scale(dtype):
-    """bias + per-tensor activation scale (tests/test_w8a8_mma.py:111-112) through the reference ABI entry."""
+    """bias + per-tensor activation scale (tests/test_w8a8_mma.py:63-64) through the reference ABI entry."""
     L = _lib()
     code = 0 if dtype == torch.float16 else 1
     M, N, K = 5, 8192, 5120

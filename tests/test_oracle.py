@@ -39,7 +39,7 @@ def test_gemm_and_dequant(golden, case):
 
 
 def test_dequant_bias_and_per_tensor_scale():
-    """bias and per-tensor scales (tests/test_w8a8_mma.py:111-112) against a float64 restatement."""
+    """bias and per-tensor scales (tests/test_w8a8_mma.py:63-64) against a float64 restatement."""
     g = torch.Generator().manual_seed(5)
     a = torch.randint(-128, 128, (3, 96), generator=g, dtype=torch.int8)
     w = torch.randint(-128, 128, (40, 96), generator=g, dtype=torch.int8)

@@ -28,7 +28,7 @@ def test_disable_switch():
 
 def test_register_idempotent_and_capability_gated():
     """On a non-B200 platform (here: no GPU) the GEMM and all-reduce hooks stay off, the capability-independent
-    quantfuse and custom-AR hooks go on (the reference gates the same way on cap 75, w8a8.py:257-261)."""
+    quantfuse and custom-AR hooks go on (the reference gates the same way on cap 75, w8a8.py:132-134)."""
     out = _py("import vllm_turing_b200 as v; v.register(); v.register(); from vllm import _custom_ops as o; "
               "from vllm.distributed.device_communicators.cuda_communicator import CudaCommunicator as C; "
               "from vllm.distributed.device_communicators.custom_all_reduce import CustomAllreduce as A; "
@@ -60,7 +60,7 @@ def test_scaled_mm_op_registered():
 
 
 def test_gemv_ok_predicates():
-    """The layout checks of vllm_turing/w8a8.py:165-193 on CPU tensors (no kernel call)."""
+    """The layout checks of vllm_turing/w8a8.py:38-66 on CPU tensors (no kernel call)."""
     from vllm_turing_b200 import w8a8
     M, N, K = 5, 64, 128
     a = torch.zeros(M, K, dtype=torch.int8)

@@ -1,7 +1,7 @@
 """The tcgen05 kind::i8 GEMMs (csrc/w8a8_tc.cu) against the oracle: int32 accumulators bit-exact, dequantised outputs
 bit-exact in each path's epilogue order -- w8a8_big: sa * (sw * acc) (vllm_turing/csrc/w8a8_big.cu:26-35); w8a8_mma:
 (acc * sa) * sw + bias (vllm_turing/csrc/w8a8_gemv.cu:288) -- at the reference's test shapes (tests/test_w8a8_mma.py:
-109-116, tests/test_w8a8_big.py:171-172) and the BASELINE prefill / decode shapes."""
+109-116, tests/test_w8a8_big.py:45-54) and the BASELINE prefill / decode shapes."""
 import numpy as np
 import pytest
 import torch
@@ -79,7 +79,7 @@ def test_big_dequant_bit_exact(dtype, M, N, K):
                                                 (27, 1000, 5136, False, True), (32, 300, 5168, True, True),
                                                 (9, 7168, 5120, False, True)])
 def test_mma_dequant_bit_exact(dtype, M, N, K, bias, per_row):
-    """the reference's w8a8_mma cases (tests/test_w8a8_mma.py:109-116): bias, per-tensor scale, odd K / N"""
+    """the reference's w8a8_mma cases (tests/test_w8a8_mma.py:61-68): bias, per-tensor scale, odd K / N"""
     code = 0 if dtype == torch.float16 else 1
     a, w = rand_int8((M, K), M + 17), rand_int8((N, K), N + 19)
     sa = rand_scales(M if per_row else 1, 3, 1e-2)
@@ -97,7 +97,7 @@ def test_mma_dequant_bit_exact(dtype, M, N, K, bias, per_row):
 
 def test_dispatch_through_scaled_mm_op():
     """vllm_turing::scaled_mm_ picks the GEMV (M <= VLLM_TURING_GEMV_MAX_M, off by default), the small-M tensor-core
-    kernel (M <= 32) and the prefill kernel (larger M), as vllm_turing/w8a8.py:235-244 does."""
+    kernel (M <= 32) and the prefill kernel (larger M), as vllm_turing/w8a8.py:108-117 does."""
     from vllm_turing_b200 import w8a8
     N, K = 5120, 8704
     w = rand_int8((N, K), 1)

@@ -1,5 +1,5 @@
 // The decode MLP's first half in one kernel on B200 (sm_100a): the column-parallel gate/up W8A8 GEMM, SiLU(gate) * up
-// and the per-token int8 quantisation of the product -- what the reference runs as scaled_mm_ (w8a8.py:235-244, the
+// and the per-token int8 quantisation of the product -- what the reference runs as scaled_mm_ (w8a8.py:108-117, the
 // GEMV / MMA kernels) followed by silu_mul_quant (csrc/silu_quant.cu:1-77, tailoverlap.py:148-151), here without the
 // [M, 2I] bf16 round trip through HBM and without the second launch.
 //

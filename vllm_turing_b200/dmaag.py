@@ -1,4 +1,4 @@
-"""The all-gather primitive (the reference's DmaAllGather API, vllm_turing/dmaag.py:205-267) on NVLink P2P.
+"""The all-gather primitive (the reference's DmaAllGather API, vllm_turing/dmaag.py:57-119) on NVLink P2P.
 
 The reference gathers two ranks' payloads through pinned host memory with copy engines (no peer access on its
 hosts). B200 nodes have NVSwitch, so the same contract -- `gathered` holds world slots of m bytes, the caller has

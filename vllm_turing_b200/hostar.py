@@ -1,6 +1,6 @@
 """The tensor-parallel all-reduce of vLLM's CudaCommunicator on the B200 P2P kernels (csrc/tp_comm.cu).
 
-The reference hooks CudaCommunicator.__init__ / all_reduce (vllm_turing/hostar.py:191-283) to route two-rank messages
+The reference hooks CudaCommunicator.__init__ / all_reduce (vllm_turing/hostar.py:191-282) to route two-rank messages
 to its LL kernel (<= 128 KiB), its copy-engine all-reduce (>= 8 MiB eager) or its host-memory kernel, else to vLLM's
 custom all-reduce / NCCL. On B200 every TP size 2..8 with full NVLink peer access gets one communicator (comm.TPComm)
 whose kernels serve every size: one-shot LL up to VLLM_TURING_LL_KB, two-shot reduce-scatter + all-gather above it,

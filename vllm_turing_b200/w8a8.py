@@ -37,7 +37,7 @@ def _dtype_code(dt):
 
 
 def gemv_ok(out, a, b, sa, sb, bias, max_m=None):
-    """The GEMV path's layout requirements (vllm_turing/w8a8.py:165-173, same checks)."""
+    """The GEMV path's layout requirements (vllm_turing/w8a8.py:38-46, same checks)."""
     M, K = a.shape
     return (1 <= M <= (MAX_M if max_m is None else max_m) and K % 16 == 0 and a.dtype == torch.int8
             and a.is_contiguous() and b.dtype == torch.int8 and b.stride(0) == 1 and b.stride(1) == K
@@ -170,7 +170,7 @@ def mma_blocked(out, a, wb, sa, sb, bias=None):
 
 
 def big_ok(out, a, b, sa, sb, bias):
-    """The prefill kernel's requirements (vllm_turing/w8a8.py:185-193, same checks)."""
+    """The prefill kernel's requirements (vllm_turing/w8a8.py:58-66, same checks)."""
     M, K = a.shape
     N = b.shape[1]
     return (BIG and _has("w8a8_big") and M > MMA_MAX_M and bias is None and K % 16 == 0 and N % 16 == 0
@@ -211,7 +211,7 @@ def _scaled_mm_fake(out, a, b, a_scales, b_scales, bias):
 
 
 def scaled_mm(a, b, scale_a, scale_b, out_dtype, bias=None):
-    """vLLM's cutlass_scaled_mm contract (vllm_turing/w8a8.py:263-274): a [..., K] int8, b [K, N] view."""
+    """vLLM's cutlass_scaled_mm contract (vllm_turing/w8a8.py:136-147): a [..., K] int8, b [K, N] view."""
     assert out_dtype is torch.bfloat16 or out_dtype is torch.float16
     assert bias is None or bias.numel() == b.shape[1] and bias.dtype == out_dtype
     target_shape = (*a.shape[:-1], b.shape[1])
