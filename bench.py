@@ -1168,6 +1168,22 @@ def main():
     t_k = {k: timed(g.replay, passes) / NL for k, g in g_k.items()}
     comm.check()
 
+    # the latency floor of the fused down kernel at N > 1: the one-shot all-reduce of its M x 5120 bf16 message alone
+    # (NL calls in a graph, as the step), next to its weight stream's HBM floor
+    t_ll = None
+    if world > 1:
+        msg = torch.zeros(M, HIDDEN, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            comm.all_reduce(msg, out=msg, algo=1)
+        barrier()
+        g_ll = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_ll):
+            for _ in range(NL):
+                comm.all_reduce(msg, out=msg, algo=1)
+        t_ll = timed(g_ll.replay, passes) / NL
+        comm.check()
+        del g_ll
+
     # the same step launched eagerly (no graph): host-side launch cost included
     t_eager = timed(lambda: run(LAYER, layers), max(1, min(K, 10))) / NL
     comm.check()
@@ -1243,6 +1259,14 @@ def main():
         "roofline": {"bound": "hbm", "kernel": names[dom], "achieved": achieved, "peak": hbm, "unit": "GB/s",
                      "frac": achieved / hbm, "traffic": traffic, "bytes_per_launch": alg[dom],
                      "peak_kind": peak_kind},
+        # the fused down kernel against its own floor: max(weight stream at the HBM peak, the one-shot all-reduce of
+        # its message measured alone); frac = floor / its measured time
+        "down_roofline": {"hbm_floor_us": alg["down"] / (hbm * 1e9) * 1e6,
+                          "oneshot_us": t_ll * 1e6 if t_ll is not None else None,
+                          "floor_us": max(alg["down"] / (hbm * 1e9), t_ll or 0.0) * 1e6,
+                          "measured_us": t_k["down"] * 1e6,
+                          "frac": max(alg["down"] / (hbm * 1e9), t_ll or 0.0) / t_k["down"],
+                          "hbm_gbs": alg["down"] / t_k["down"] / 1e9},
         "clocks": clocks, "gpu_launches": len(LAYER) * NL * K, "e2e": e2e, "cpu_baseline": cpu, "parity": parity,
     }
     if rank == 0:

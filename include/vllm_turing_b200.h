@@ -226,7 +226,8 @@ unsigned vt_comm_seq(void *comm);
  * packed 8-byte aligned. Replaces ar8_quant (host_ar.cu:182-188). */
 int ar8_quant(const void *x, void *packed, int n, void *stream);
 /* out fp16 [n] = the rank-ordered float32 sum of the dequantised packed blocks of two ranks (gathered = 2 blocks of
- * n + n / 64 bytes); n % 512 == 0. Replaces ar8_dequant_sum (host_ar.cu:190-201). */
+ * n + n / 64 bytes); n % 128 == 0 as there (vectorised when n % 512 == 0). Replaces ar8_dequant_sum
+ * (host_ar.cu:190-201). */
 int ar8_dequant_sum(const void *gathered, void *out, int n, void *stream);
 /* The same for 1..8 ranks. New entry. */
 int vt_ar8_dequant_sum(const void *gathered, void *out, long long n, int world, void *stream);

@@ -39,9 +39,11 @@ def test_ar8_quant_bitexact(n):
     assert np.array_equal(packed.cpu().numpy(), O.ar8_quant(O.to_bits(x)))
 
 
-@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
-def test_ar8_dequant_sum_bitexact(world):
-    n = 24 * 5120
+@pytest.mark.parametrize("world,n", [(1, 24 * 5120), (2, 24 * 5120), (3, 24 * 5120), (4, 24 * 5120),
+                                     (8, 24 * 5120), (2, 128), (3, 128 * 7), (2, 5120 + 128)])
+def test_ar8_dequant_sum_bitexact(world, n):
+    """n % 512 == 0: the vectorised kernel; n % 128 == 0 only (odd blocks not 8-byte aligned, as the reference allows,
+    host_ar.cu:190-201): the element-wise one. Same bits either way."""
     blocks = [O.ar8_quant(O.to_bits(_x(n, 100 + r))) for r in range(world)]
     g = torch.from_numpy(np.concatenate(blocks)).cuda()
     out = torch.empty(n, dtype=torch.float16, device="cuda")
@@ -56,7 +58,8 @@ def test_ar8_argument_checks():
     buf = torch.empty(4096, dtype=torch.uint8, device="cuda")
     st = torch.cuda.current_stream().cuda_stream
     assert L.ar8_quant(buf.data_ptr(), buf.data_ptr(), 100, st) == -1           # n % 128
-    assert L.vt_ar8_dequant_sum(buf.data_ptr(), buf.data_ptr(), 256, 2, st) == -1  # n % 512
+    assert L.vt_ar8_dequant_sum(buf.data_ptr(), buf.data_ptr(), 200, 2, st) == -1  # n % 128
+    assert L.ar8_dequant_sum(buf.data_ptr(), buf.data_ptr(), 200, st) == -1         # n % 128
     assert L.vt_ar8_dequant_sum(buf.data_ptr(), buf.data_ptr(), 512, 9, st) == -1  # > 8 ranks
 
 

@@ -239,3 +239,16 @@ def test_logits_gathered_paths(monkeypatch, M, ll):
         fits = M <= 64 and M * Vs * 2 <= ll
         assert fc.calls == (["rows"] if fits else ["slots"])
     assert set(calls) == ({"kernel"} if M <= 64 and M * Vs * 2 <= ll else {"op"})
+
+
+def test_logits_gathered_rejects_a_mismatched_out():
+    """A caller-supplied out is written through its pointer with row stride world * Vs: a wrong shape, dtype or a
+    non-contiguous view is refused instead of being mis-written."""
+    from vllm_turing_b200 import lmhead
+    M, Vs, K = 4, 40, 32
+    x = torch.randn(M, K).to(torch.bfloat16)
+    w = torch.zeros(Vs, K, dtype=torch.int8)
+    for bad in (torch.empty(M, Vs + 8, dtype=torch.bfloat16), torch.empty(M, Vs, dtype=torch.float16),
+                torch.empty(Vs, M, dtype=torch.bfloat16).t()):
+        with pytest.raises(ValueError):
+            lmhead.logits_gathered(x, w, None, out=bad)

@@ -106,6 +106,24 @@ __global__ void __launch_bounds__(AR8_THREADS) ar8_dequant_sum_kernel(const int8
     }
 }
 
+// One element per thread, byte and 2-byte accesses: for n % 512 != 0, where rank r's block (n + n / 64 bytes) does
+// not start 8-byte aligned. Same arithmetic and order as ar8_dequant_sum_kernel.
+__global__ void __launch_bounds__(AR8_THREADS) ar8_dequant_sum_scalar_kernel(const int8_t *__restrict__ gathered,
+                                                                             __half *__restrict__ out, long long n,
+                                                                             int world) {
+    const long long blk = n + n / 64;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float acc = 0.0f;
+        for (int r = 0; r < world; ++r) {
+            const int8_t *b = gathered + r * blk;
+            const float v = __fmul_rn((float)b[i], __half2float(reinterpret_cast<const __half *>(b + n)[i >> 7]));
+            acc = r == 0 ? v : __fadd_rn(acc, v);
+        }
+        out[i] = __float2half_rn(acc);
+    }
+}
+
 static int ar8_grid(long long threads) {
     const int sms = num_sms(cur_device());
     long long g = (threads + AR8_THREADS - 1) / AR8_THREADS;
@@ -131,18 +149,24 @@ int ar8_quant(const void *x, void *packed, int n, void *stream) {
 }
 
 // AR8 dequantise-and-sum over `world` packed blocks (n + n / 64 bytes each, rank order) into out fp16 [n]; 1..8 ranks,
-// n % 512 == 0 (every block then starts 8-byte aligned; prefill messages M x 5120 always are). New entry (the
+// n % 128 == 0. With n % 512 == 0 (every block then starts 8-byte aligned; prefill messages M x 5120 always are),
+// gathered 8-byte and out 16-byte aligned, the vectorised kernel; otherwise one element per thread. New entry (the
 // reference's two-rank form is ar8_dequant_sum).
 int vt_ar8_dequant_sum(const void *gathered, void *out, long long n, int world, void *stream) {
-    if (!gathered || !out || n <= 0 || (n % 512) || world < 1 || world > AR8_MAX_RANKS || ((uintptr_t)out & 15) ||
-        ((uintptr_t)gathered & 7))
+    if (!gathered || !out || n <= 0 || (n % 128) || world < 1 || world > AR8_MAX_RANKS || ((uintptr_t)out & 1) ||
+        ((uintptr_t)gathered & 1))
         return VT_EARG;
-    ar8_dequant_sum_kernel<<<ar8_grid(n / 8), AR8_THREADS, 0, (cudaStream_t)stream>>>((const int8_t *)gathered,
-                                                                                    (__half *)out, n, world);
+    if ((n % 512) == 0 && !((uintptr_t)out & 15) && !((uintptr_t)gathered & 7)) {
+        ar8_dequant_sum_kernel<<<ar8_grid(n / 8), AR8_THREADS, 0, (cudaStream_t)stream>>>((const int8_t *)gathered,
+                                                                                        (__half *)out, n, world);
+    } else {
+        ar8_dequant_sum_scalar_kernel<<<ar8_grid(n), AR8_THREADS, 0, (cudaStream_t)stream>>>(
+            (const int8_t *)gathered, (__half *)out, n, world);
+    }
     return (int)cudaGetLastError();
 }
 
-// The reference's two-rank AR8 sum (host_ar.cu:190-201), n % 512 == 0 here.
+// The reference's two-rank AR8 sum (host_ar.cu:190-201): n % 128 == 0, as there.
 int ar8_dequant_sum(const void *gathered, void *out, int n, void *stream) {
     return vt_ar8_dequant_sum(gathered, out, n, 2, stream);
 }

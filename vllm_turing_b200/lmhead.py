@@ -131,6 +131,11 @@ def logits_gathered(x, w, s, bias=None, comm=None, out=None):
     rank = comm.rank if comm is not None else 0
     if out is None:
         out = torch.empty(M, world * Vs, dtype=x.dtype, device=x.device)
+    elif (tuple(out.shape) != (M, world * Vs) or out.dtype != x.dtype or not out.is_contiguous()
+          or out.device != x.device):
+        # the kernel and the row-strided gather write through out's pointer with row stride world * Vs
+        raise ValueError(f"logits_gathered: out must be a contiguous {x.dtype} [{M}, {world * Vs}] tensor on "
+                         f"{x.device}, got {out.dtype} {tuple(out.shape)} contiguous={out.is_contiguous()}")
     esz = x.element_size()
     if M <= 64 and kernel_ok(x, w) and (world == 1 or M * Vs * esz <= comm.ll_capacity) and (Vs * esz) % 8 == 0:
         mm_into(out[:, rank * Vs:], x, w, s, bias, ldo=world * Vs)
