@@ -37,6 +37,9 @@
 #include "tc_core.cuh"
 #include "tma_host.h"
 
+extern "C" int vt_rms_norm_quant(const void *x, void *residual, const void *weight, float eps, void *q, void *scales,
+                                 void *normed, int M, int N, int dtype, void *stream);   // norm_quant.cu
+
 namespace vt {
 
 constexpr int PF_BN = 256;          // GEMM tile columns (output features)
@@ -67,7 +70,7 @@ struct PfRsEpi {
     unsigned seq, p;
     __device__ __forceinline__ void on_start(const TcArgs &, float *) {
         seq = *reinterpret_cast<volatile unsigned *>(A->c.seq_ptr()) + 1u;   // this call's number (after pdl_wait)
-        p = seq & 1u;
+        p = A->c.world == 1 ? 0u : (seq & 1u);   // one rank: no peer, no double buffering (the host reads parity 0)
     }
     __device__ __forceinline__ void post_start() {}
 
@@ -101,6 +104,7 @@ struct PfRsEpi {
     }
     // all four epilogue warps: the tile's stores are performed (system scope) before its flag is released
     __device__ __forceinline__ void prefill_tile_done(const TcArgs &, int ta, int tb) const {
+        if (A->c.world == 1) return;   // the next kernel in the stream reads the tiles; no flags
         __threadfence_system();
         named_sync(TC_EPI_BAR, 128);
         if (threadIdx.x == TC_EPI_LEAD) {
@@ -149,9 +153,10 @@ __device__ __forceinline__ float group_max(float v, float *red, int bar, int tpr
 // The row epilogue of one reduced row x (thread t holds elements 8 (t + k tpr) .. + 7 for k < VPT, rounded to T):
 // residual := rnd(x + residual); y = rnd((h * rsqrt(mean(h^2) + eps)) * w); q, scale = quant(y). The arithmetic and
 // summation order of rms_norm_quant_vec_kernel (norm_quant.cu) at the same VPT and threads per row.
-template <typename T, int VPT>
+// rv(k): the residual row's vector k of this thread (from registers or from a shared-memory slot).
+template <typename T, int VPT, class RV>
 __device__ __forceinline__ void pf_row_epilogue(const PfArgs<T> &A, size_t gr, int t, const float (&x)[VPT * 8],
-                                                const uint4 (&rv)[VPT], float *red, int bar) {
+                                                RV rv, float *red, int bar) {
     const int tpr = A.tpr, N = A.N;
     uint4 *rr = reinterpret_cast<uint4 *>(A.residual + gr * N);
     uint4 wv[VPT];   // the norm weight (L1 / L2 after the first row): issued now, used after the row's sum
@@ -161,7 +166,8 @@ __device__ __forceinline__ void pf_row_epilogue(const PfArgs<T> &A, size_t gr, i
     float ss = 0.0f;
 #pragma unroll
     for (int k = 0; k < VPT; ++k) {
-        const uint32_t rs_[4] = {rv[k].x, rv[k].y, rv[k].z, rv[k].w};
+        const uint4 r4 = rv(k);
+        const uint32_t rs_[4] = {r4.x, r4.y, r4.z, r4.w};
         uint32_t o[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -293,7 +299,7 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1) tp_prefill_tail_kernel(con
 #pragma unroll
             for (int k = 0; k < VPT; ++k) rv[k] = reinterpret_cast<const uint4 *>(A.residual + gr * N)[t + k * tpr];
             pf_unpack<T, VPT>(ov, x);   // the rounded sum
-            pf_row_epilogue<T, VPT>(A, gr, t, x, rv, red, bar);
+            pf_row_epilogue<T, VPT>(A, gr, t, x, [&](int k) { return rv[k]; }, red, bar);
         }
     }
 
@@ -327,12 +333,233 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1) tp_prefill_tail_kernel(con
                 if (A.residual) {
                     float x[VPT * 8];
                     pf_unpack<T, VPT>(v, x);
-                    pf_row_epilogue<T, VPT>(A, gr, t, x, rv, red, bar);
+                    pf_row_epilogue<T, VPT>(A, gr, t, x, [&](int k) { return rv[k]; }, red, bar);
                 }
             }
         }
     }
     comm_end(c, seq);
+}
+
+// ---- kernel 2, staged variant: rows land in shared memory by bulk copies ----------------------------------------------
+// The same two phases and arithmetic as tp_prefill_tail_kernel, but a row group does not load its rows into registers:
+// its first thread keeps PF_SLOTS whole rows (a source's partial row, a peer's reduced row, the residual row) in flight
+// as 1-D bulk copies (cp.async.bulk, the TMA engine) into a ring of shared-memory slots, completed on an mbarrier per
+// slot, so the bytes in flight per SM are set by shared memory (PF_SLOTS x N x 2 per group), not by registers. Each
+// slot is handed back after the group has read it (a named barrier), and the issuing thread fences the async proxy
+// before reusing it. Peer rows are read the same way over NVLink (a bulk load from a peer's memory, no multicast).
+constexpr int PF_SLOTS = 4;
+
+template <typename T>
+struct PfRing {   // one row group's ring
+    unsigned char *slot0;
+    uint64_t *full;
+    uint32_t rowb;
+    int issued, used;   // items issued / consumed (the same count in every thread of the group)
+};
+
+__device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(PF_TAIL_THREADS, 1)
+    tp_prefill_tail_bulk_kernel(const __grid_constant__ PfArgs<T> A) {
+    extern __shared__ __align__(128) unsigned char pf_smem[];
+    __shared__ unsigned s_seq;
+    __shared__ float red_all[PF_TAIL_THREADS / 64][8];
+    __shared__ __align__(8) uint64_t bars[PF_TAIL_THREADS / 64][PF_SLOTS];
+    pdl_wait();
+    const CommView &c = A.c;
+    const unsigned seq = comm_begin(c, &s_seq);
+    const unsigned p = seq & 1u;
+    const uint64_t deadline = globaltimer() + A.peer_timeout;
+    const int tpr = A.tpr, N = A.N, R = A.R, W = c.world, me = c.rank;
+    const int g = threadIdx.x / tpr, t = threadIdx.x - g * tpr;
+    const int RG = blockDim.x / tpr;
+    const long long S = (long long)gridDim.x * RG, slot = (long long)blockIdx.x * RG + g;
+    const int lr0 = (int)(R * slot / S), lr1 = (int)(R * (slot + 1) / S);
+    const int bar = 1 + g;
+    const uint32_t rowb = (uint32_t)N * sizeof(T);
+    float *red = red_all[g];
+    uint64_t *full = bars[g];
+    unsigned char *ring = pf_smem + (size_t)g * PF_SLOTS * rowb;
+    const bool lead = t == 0;
+    if (lead)
+        for (int s = 0; s < PF_SLOTS; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
+    __syncthreads();
+    bool dead = false;
+    // the source of item i of a row: partials 0..nsrc-1 (phase A) or the peer's reduced row (phase B), then residual
+    const int per_row_a = W + (A.residual ? 1 : 0);
+    int issued = 0, used = 0;
+
+    // ---- phase A ----
+    // every source's tiles of the row blocks of this group's rows have landed (one cooperative wait up front)
+    if (lr1 > lr0) {
+        for (int rb = lr0 / TC_BM; rb <= (lr1 - 1) / TC_BM; ++rb)
+            for (int i = t; i < W * A.ntb; i += tpr) {
+                const int src = i / A.ntb, tb = i - src * A.ntb;
+                if (!dead && !flag_wait(c.pf_tile_flag(me, p, src, rb * A.ntb + tb), seq, deadline)) {
+                    report(c.status(), ST_PEER_TIMEOUT | 0xb00u | (unsigned)src);
+                    dead = true;
+                }
+            }
+        named_sync(bar, tpr);
+    }
+    const int items_a = (lr1 - lr0) * per_row_a;
+    auto src_a = [&](int i) -> const void * {
+        const int lr = lr0 + i / per_row_a, k = i - (i / per_row_a) * per_row_a;
+        if (k < W) return c.rs_buf(me, p, k) + (size_t)lr * rowb;
+        return A.residual + ((size_t)me * R + lr) * N;
+    };
+    if (lead) {
+        fence_async_global();   // the flags were acquired by generic loads; the bulk copies read through the async proxy
+        for (; issued < items_a && issued < PF_SLOTS; ++issued) {
+            mbar_arrive_expect_tx(&full[issued % PF_SLOTS], rowb);
+            bulk_g2s(ring + (size_t)(issued % PF_SLOTS) * rowb, src_a(issued), rowb, &full[issued % PF_SLOTS]);
+        }
+    }
+    // wait for the slot of item `used`; its data as 16-byte vectors
+    auto take = [&](uint32_t code) -> const uint4 * {
+        const int s = used % PF_SLOTS;
+        if (!mbar_wait(&full[s], (uint32_t)(used / PF_SLOTS) & 1u, deadline) && !dead) {
+            report(c.status(), ST_PIPE_TIMEOUT | code);
+            dead = true;
+        }
+        return reinterpret_cast<const uint4 *>(ring + (size_t)s * rowb);
+    };
+    for (int lr = lr0; lr < lr1; ++lr) {
+        float x[VPT * 8];
+        for (int k = 0; k < W; ++k) {   // the sources' partial rows, summed in rank order
+            const uint4 *sv = take(0xd00u);
+#pragma unroll
+            for (int j = 0; j < VPT; ++j) {
+                const uint4 v = sv[t + j * tpr];
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = unpack2<T>(u[e]);
+                    x[8 * j + 2 * e] = k == 0 ? f.x : x[8 * j + 2 * e] + f.x;
+                    x[8 * j + 2 * e + 1] = k == 0 ? f.y : x[8 * j + 2 * e + 1] + f.y;
+                }
+            }
+            named_sync(bar, tpr);   // the slot is read: hand it back
+            ++used;
+            if (lead && issued < items_a) {
+                fence_async_shared();
+                const int s2 = issued % PF_SLOTS;
+                mbar_arrive_expect_tx(&full[s2], rowb);
+                bulk_g2s(ring + (size_t)s2 * rowb, src_a(issued), rowb, &full[s2]);
+                ++issued;
+            }
+        }
+        const size_t gr = (size_t)me * R + lr;
+        uint4 ov[VPT];
+#pragma unroll
+        for (int j = 0; j < VPT; ++j)
+            ov[j] = make_uint4(pack2<T>(x[8 * j], x[8 * j + 1]), pack2<T>(x[8 * j + 2], x[8 * j + 3]),
+                               pack2<T>(x[8 * j + 4], x[8 * j + 5]), pack2<T>(x[8 * j + 6], x[8 * j + 7]));
+        if (W > 1) {
+            uint4 *ag = reinterpret_cast<uint4 *>(c.ag_buf(me, p) + (size_t)lr * rowb);
+#pragma unroll
+            for (int j = 0; j < VPT; ++j) ag[t + j * tpr] = ov[j];
+        }
+        if (A.reduced) {
+#pragma unroll
+            for (int j = 0; j < VPT; ++j) reinterpret_cast<uint4 *>(A.reduced + gr * N)[t + j * tpr] = ov[j];
+        }
+        if (A.residual) {   // the residual row's slot is read inside the epilogue, then handed back
+            const uint4 *rs = take(0xd00u);
+            pf_unpack<T, VPT>(ov, x);
+            pf_row_epilogue<T, VPT>(A, gr, t, x, [&](int k) { return rs[t + k * tpr]; }, red, bar);
+            named_sync(bar, tpr);
+            ++used;
+            if (lead && issued < items_a) {
+                fence_async_shared();
+                const int s2 = issued % PF_SLOTS;
+                mbar_arrive_expect_tx(&full[s2], rowb);
+                bulk_g2s(ring + (size_t)s2 * rowb, src_a(issued), rowb, &full[s2]);
+                ++issued;
+            }
+        }
+    }
+
+    // ---- phase B ----
+    if (W > 1) {
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0) st_release_sys(c.pf_ag_flag(me, p, blockIdx.x), seq);
+        const int per_row_b = A.residual ? 2 : 1;
+        const int rows = lr1 - lr0;
+        const int items_b = (W - 1) * rows * per_row_b;
+        // item i: peer k = 1 + i / (rows per_row_b), row lr0 + (i / per_row_b) % rows; the peer's reduced row, then
+        // the residual row
+        auto src_b = [&](int i) -> const void * {
+            const int k = 1 + i / (rows * per_row_b), r = (i / per_row_b) % rows, e = i % per_row_b;
+            const int srk = (me + k) % W;
+            if (e == 0) return c.ag_buf(srk, p) + (size_t)(lr0 + r) * rowb;
+            return A.residual + ((size_t)srk * R + lr0 + r) * N;
+        };
+        int ib = 0;   // items of phase B issued (by the group's first thread); the ring continues from phase A
+        auto issue_b = [&]() {
+            // a peer's first item: its CTA blockIdx.x must have published its reduced rows
+            const int k = 1 + ib / (rows * per_row_b);
+            if (ib % (rows * per_row_b) == 0) {
+                const int srk = (me + k) % W;
+                if (!dead && !flag_wait(c.pf_ag_flag(srk, p, blockIdx.x), seq, deadline)) {
+                    report(c.status(), ST_PEER_TIMEOUT | 0xc00u | (unsigned)srk);
+                    dead = true;
+                }
+                fence_async_global();
+            }
+            fence_async_shared();
+            const int s2 = (issued + ib) % PF_SLOTS;
+            mbar_arrive_expect_tx(&full[s2], rowb);
+            bulk_g2s(ring + (size_t)s2 * rowb, src_b(ib), rowb, &full[s2]);
+            ++ib;
+        };
+        if (lead)
+            while (ib < items_b && ib < PF_SLOTS) issue_b();
+        for (int it = 0; it < items_b; it += per_row_b) {
+            const int k = 1 + it / (rows * per_row_b), r = (it / per_row_b) % rows;
+            const int srk = (me + k) % W;
+            const size_t gr = (size_t)srk * R + lr0 + r;
+            float x[VPT * 8];
+            {   // the peer's reduced row
+                const uint4 *sv = take(0xe00u);
+                uint4 v[VPT];
+#pragma unroll
+                for (int j = 0; j < VPT; ++j) v[j] = sv[t + j * tpr];
+                if (A.reduced) {
+#pragma unroll
+                    for (int j = 0; j < VPT; ++j) reinterpret_cast<uint4 *>(A.reduced + gr * N)[t + j * tpr] = v[j];
+                }
+                pf_unpack<T, VPT>(v, x);
+                named_sync(bar, tpr);
+                ++used;
+                if (lead && ib < items_b) issue_b();
+            }
+            if (A.residual) {   // the residual row's slot is read inside the epilogue, then handed back
+                const uint4 *rs = take(0xe00u);
+                pf_row_epilogue<T, VPT>(A, gr, t, x, [&](int k) { return rs[t + k * tpr]; }, red, bar);
+                named_sync(bar, tpr);
+                ++used;
+                if (lead && ib < items_b) issue_b();
+            }
+        }
+    }
+    comm_end(c, seq);
+}
+
+// Tail variant: rows staged through shared memory (tp_prefill_tail_bulk_kernel, the default; measured at TP1, M = 8192:
+// 70 us against 89 us for the register version) or, with VLLM_TURING_PF_TAIL=reg, tp_prefill_tail_kernel.
+inline bool pf_tail_bulk() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_PF_TAIL");
+        v = (e && e[0] == 'r') ? 0 : 1;
+    }
+    return v != 0;
 }
 
 // VPT (16-byte vectors per thread) and threads per row of the row epilogue: the choice vt_rms_norm_quant makes
@@ -351,9 +578,36 @@ inline bool pf_row_shape(int N, int &vpt, int &tpr) {
     return false;
 }
 
+template <typename T, int VPT>
+static int launch_tail_bulk_v(const PfArgs<T> &A, dim3 g, dim3 b, size_t smem, cudaStream_t s) {
+    static bool attr[VT_MAX_DEV] = {false};
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    if (!attr[dev]) {   // once, for the largest ring any N can ask for (launch_tail keeps smem within it)
+        if (cudaFuncSetAttribute(tp_prefill_tail_bulk_kernel<T, VPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 max_smem_optin(dev) - 4096) != cudaSuccess)
+            return (int)cudaGetLastError();
+        attr[dev] = true;
+    }
+    return launch_k(tp_prefill_tail_bulk_kernel<T, VPT>, g, b, smem, s, true, A);
+}
+
 template <typename T>
 static int launch_tail(const PfArgs<T> &A, int vpt, int grid, cudaStream_t s) {
     const dim3 g(grid), b((PF_TAIL_THREADS / A.tpr) * A.tpr);
+    const size_t bulk_smem = (size_t)(PF_TAIL_THREADS / A.tpr) * PF_SLOTS * A.N * sizeof(T);
+    if (pf_tail_bulk() && bulk_smem + 4096 <= (size_t)max_smem_optin(cur_device())) {
+        switch (vpt) {
+            case 8: return launch_tail_bulk_v<T, 8>(A, g, b, bulk_smem, s);
+            case 7: return launch_tail_bulk_v<T, 7>(A, g, b, bulk_smem, s);
+            case 6: return launch_tail_bulk_v<T, 6>(A, g, b, bulk_smem, s);
+            case 5: return launch_tail_bulk_v<T, 5>(A, g, b, bulk_smem, s);
+            case 4: return launch_tail_bulk_v<T, 4>(A, g, b, bulk_smem, s);
+            case 3: return launch_tail_bulk_v<T, 3>(A, g, b, bulk_smem, s);
+            case 2: return launch_tail_bulk_v<T, 2>(A, g, b, bulk_smem, s);
+            default: return launch_tail_bulk_v<T, 1>(A, g, b, bulk_smem, s);
+        }
+    }
     switch (vpt) {
         case 8: return launch_k(tp_prefill_tail_kernel<T, 8>, g, b, 0, s, true, A);
         case 7: return launch_k(tp_prefill_tail_kernel<T, 7>, g, b, 0, s, true, A);
@@ -434,6 +688,24 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
         int g1 = sms < P.units ? sms : P.units;
         if (int rc = launch_k(tp_prefill_gemm_kernel<T>, dim3(g1), dim3(TC_THREADS), smem, s, true, ma, mb, P, A))
             return rc;
+        if (W == 1) {
+            // one rank: nothing to reduce or gather, so the row epilogue is the standalone residual + RMSNorm + quant
+            // kernel over the GEMM's rows (same arithmetic as the tail kernel's, at higher occupancy). The GEMM wrote
+            // them to parity 0 (with one rank nothing is double-buffered) and published no flags.
+            const T *part = reinterpret_cast<const T *>(v.base[v.rank] + v.L.rs_off);
+            if (reduced) {
+                if (cudaError_t e = cudaMemcpyAsync(reduced + m0 * N, part, (size_t)Mp * N * sizeof(T),
+                                                    cudaMemcpyDeviceToDevice, s))
+                    return (int)e;
+            }
+            if (residual) {
+                const int dt = std::is_same<T, __half>::value ? 0 : 1;
+                if (int rc = vt_rms_norm_quant(part, residual + m0 * N, norm_w, eps, q + m0 * N, scales + m0, nullptr,
+                                               Mp, N, dt, s))
+                    return rc;
+            }
+            continue;
+        }
         int g2 = sms < PF_MAX_CTAS ? sms : PF_MAX_CTAS;
         if (int rc = launch_tail<T>(A, vpt, g2, s)) return rc;
     }
