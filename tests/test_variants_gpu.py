@@ -6,7 +6,8 @@ process against the oracle (int32 accumulators and the fused layer's reduced sum
   - several CTAs per token row in the fused row epilogue, with the mailbox combine that tensor parallelism above two
     ranks uses (VLLM_TURING_ROW_CTAS);
   - launches without programmatic dependent launch (VLLM_TURING_PDL=0), and the weight prefetch into L2 ahead of the
-    launch wait (VLLM_TURING_L2_PREFETCH_KB, off by default)."""
+    launch wait (VLLM_TURING_L2_PREFETCH_KB, off by default);
+  - the prefill GEMM on 128 x 256 tiles instead of 256 x 256 (VLLM_TURING_PREFILL_WIDE=0)."""
 import os
 import subprocess
 import sys
@@ -32,7 +33,8 @@ def child():
 
     L = _build.load()
     s = torch.cuda.current_stream().cuda_stream
-    for M, N, K in ((5, 34816, 5120), (16, 5120, 17408), (32, 1000, 5136), (1, 136, 128)):
+    for M, N, K in ((5, 34816, 5120), (16, 5120, 17408), (32, 1000, 5136), (1, 136, 128),   # decode orientation
+                    (33, 256, 128), (300, 1000, 5136), (2048, 5120, 2176)):                 # prefill orientation
         a, w = rand_int8((M, K), M + 1), rand_int8((N, K), N + 2)
         ac, wc = a.cuda(), w.cuda()   # kept alive until the kernel has run
         acc = torch.empty(M, N, dtype=torch.int32, device="cuda")
@@ -74,6 +76,19 @@ def child():
         assert_bits_equal(red, redo, f"reduced M={M}")
         assert_bits_equal(res, ro, f"residual M={M}")
         assert q_off(q.cpu().numpy(), qo) <= 1
+    for M, N, K in ((384, 5120, 2176),):   # the prefill tail (its GEMM's tiles follow VLLM_TURING_PREFILL_WIDE)
+        li = make_layer_inputs(M, N, K, seed=M + K, rank=0)
+        res = li.residual.cuda()
+        red = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        q, sc = comm.row_linear(li.a.cuda(), li.w.cuda(), li.sa.cuda(), li.sw.cuda(), residual=res,
+                                norm_w=li.norm_w.cuda(), eps=li.eps, reduced=red)
+        torch.cuda.synchronize()
+        comm.check()
+        ro, qo, so, redo = O.row_linear_tp_big([li.a.numpy()], [li.w.numpy()], [li.sa.numpy()], [li.sw.numpy()],
+                                               O.to_bits(li.residual), O.to_bits(li.norm_w), li.eps, 1)
+        assert_bits_equal(red, redo, f"prefill reduced M={M}")
+        assert_bits_equal(res, ro, f"prefill residual M={M}")
+        assert q_off(q.cpu().numpy(), qo) <= 1
     comm.close()
     dist.destroy_process_group()
     print("CHILD OK")
@@ -82,8 +97,10 @@ def child():
 @pytest.mark.parametrize("env", [{"VLLM_TURING_FUSED_GEMV": "1"}, {"VLLM_TURING_TC_KBS": "1"},
                                  {"VLLM_TURING_TC_KBS": "2"}, {"VLLM_TURING_ROW_CTAS": "4"},
                                  {"VLLM_TURING_FUSED_GEMV": "1", "VLLM_TURING_ROW_CTAS": "3"},
-                                 {"VLLM_TURING_PDL": "0"}, {"VLLM_TURING_L2_PREFETCH_KB": "256"}],
-                         ids=["fused_gemv", "kbs1", "kbs2", "row_ctas4", "gemv_row_ctas3", "no_pdl", "l2_prefetch"])
+                                 {"VLLM_TURING_PDL": "0"}, {"VLLM_TURING_L2_PREFETCH_KB": "256"},
+                                 {"VLLM_TURING_PREFILL_WIDE": "0"}],
+                         ids=["fused_gemv", "kbs1", "kbs2", "row_ctas4", "gemv_row_ctas3", "no_pdl", "l2_prefetch",
+                              "prefill_128x256"])
 def test_variant_in_child(env):
     e = dict(os.environ, **env)
     r = subprocess.run([sys.executable, "-c", "import tests.test_variants_gpu as t; t.child()"], cwd=ROOT, env=e,

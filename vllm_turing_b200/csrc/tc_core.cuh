@@ -237,8 +237,8 @@ struct TcOutEpi {
     float *sa_sm;   // the token scales, loaded once per CTA
     __device__ __forceinline__ void on_start(const TcArgs &P, float *sm) {
         sa_sm = sm;
-        const int t = threadIdx.x - 64;
-        if (!P.s32_out && t < P.M) sm[t] = P.sa[P.sa_rows ? t : 0];
+        const int t = threadIdx.x - 64;   // the decode finisher reads sa_sm[m] for m < BN <= 32
+        if (!P.s32_out && t < P.M && t < kSmemFloats) sm[t] = P.sa[P.sa_rows ? t : 0];
     }
     __device__ __forceinline__ void post_start() {}
     __device__ __forceinline__ Prep prep(const TcArgs &P, int n) const {
@@ -314,7 +314,8 @@ __device__ __forceinline__ void tc_prefill_epilogue(const TcArgs &P, int m, int 
 
 // A finisher with `static constexpr bool kPrefillHooks` takes over the prefill orientation's tiles: the epilogue warps
 // call fin.prefill_tile(P, m, ta, tb, taddr) (thread = A row m of tile (ta, tb), its BN accumulators from TMEM column
-// 0 of taddr) and, after releasing the TMEM buffer, fin.prefill_tile_done(P, ta, tb) (all four epilogue warps).
+// 0 of taddr) and, after releasing the TMEM buffer, fin.prefill_tile_done(P, ta, tb, bar, lead) (the four epilogue
+// warps that stored the tile: named barrier `bar`, first thread `lead`).
 template <class F, class = void> struct TcPrefillHooks : std::false_type {};
 template <class F> struct TcPrefillHooks<F, std::void_t<decltype(F::kPrefillHooks)>> : std::true_type {};
 
@@ -531,7 +532,7 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
-                if constexpr (TcPrefillHooks<Fin>::value) fin.prefill_tile_done(P, ta, tb);
+                if constexpr (TcPrefillHooks<Fin>::value) fin.prefill_tile_done(P, ta, tb, TC_EPI_BAR, TC_EPI_LEAD);
             } else {
                 const int n = arow;
                 const bool nok = n < P.N;
@@ -608,6 +609,200 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
         tmem_dealloc(tmem_base, Lay::TMEM_COLS);
     }
     __syncthreads();
+}
+
+// ---- prefill, wide tiles: 256 x 256 per CTA ------------------------------------------------------------------------
+// The prefill orientation with two 128-row A halves per tile sharing one 256-row B tile: per 128-byte K block a stage
+// holds A0 | A1 | B (16 + 16 + 32 KB) and feeds 2 x 4 MMAs (128 x 256 x 32) into two accumulators, a0 in TMEM
+// columns [0, 256) and a1 in [256, 512). Against 128 x 256 tiles this moves a third fewer bytes from L2 to the SM per
+// MMA (64 KB per two 128 x 256 x 128 blocks instead of 2 x 48 KB), and three 64 KB stages cover 3 x 1024 tensor cycles
+// of L2 latency instead of 4 x 512. TMEM holds one tile: two groups of four epilogue warps drain a0 and a1 at the same
+// time and hand each back on its own barrier (the block has 10 warps, TCW_THREADS). A 128-row half is the unit the
+// finisher sees: tile index ta2 = 2 ta + h (the prefill hooks' `ta`), rows 128 ta2 .. + 127; a half entirely past M is
+// skipped (the loads read zeros there).
+constexpr int TCW_BN = 256;
+constexpr int TCW_THREADS = 320;   // producer warp, MMA warp, two groups of four epilogue warps (one per half)
+struct TcWideLayout {
+    static constexpr int A_BYTES = TC_BM * TC_BK;                 // one 128-row half, one K block
+    static constexpr int B_BYTES = TCW_BN * TC_BK;
+    static constexpr int STAGE = 2 * A_BYTES + B_BYTES;           // 64 KB
+    static constexpr int TMEM_COLS = 512;
+    static constexpr int BAR_BYTES = 512;
+};
+
+template <typename T, class Fin>
+__device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const CUtensorMap *tmap_b, const TcArgs &P,
+                                              unsigned char *smem_raw, Fin &fin) {
+    using Lay = TcWideLayout;
+    unsigned char *tiles = tc_align1024(smem_raw);
+    const int S = P.stages;
+    uint64_t *full = reinterpret_cast<uint64_t *>(tiles + (size_t)S * Lay::STAGE);
+    uint64_t *empty = full + S;
+    uint64_t *tfull = empty + S;     // [1]: the tile's last MMAs completed
+    uint64_t *tempty = tfull + 1;    // [2]: a0 / a1 drained by the four epilogue warps
+    uint64_t *drain = tempty + 2;    // [1]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 4);
+    float *epi_sm = reinterpret_cast<float *>(reinterpret_cast<unsigned char *>(full) + Lay::BAR_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(tfull, 1);
+        mbar_init(&tempty[0], 4);
+        mbar_init(&tempty[1], 4);
+        mbar_init(drain, 1);
+        flags[0] = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(tmap_a);
+        tma_prefetch_desc(tmap_b);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Lay::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *reinterpret_cast<volatile uint32_t *>(tmem_slot);
+    pdl_wait();
+    const uint64_t deadline = globaltimer() + P.timeout_ns;
+
+    int ta, tb, kb0, kb1;
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int it = 0;
+            bool dead = false;
+            TcPieces pc(P);
+            while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t r = (uint32_t)(it / S);
+                    if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
+                        if (!flags[0]) report(P.status, ST_PIPE_TIMEOUT | 0x11u);
+                        flags[0] = 1;
+                        dead = true;
+                        break;
+                    }
+                    unsigned char *st = tiles + (size_t)s * Lay::STAGE;
+                    mbar_arrive_expect_tx(&full[s], (uint32_t)Lay::STAGE);
+                    tma_load_2d(st, tmap_a, kb * TC_BK, ta * 2 * TC_BM, &full[s]);
+                    tma_load_2d(st + Lay::A_BYTES, tmap_a, kb * TC_BK, ta * 2 * TC_BM + TC_BM, &full[s]);
+                    tma_load_2d(st + 2 * Lay::A_BYTES, tmap_b, kb * TC_BK, tb * TCW_BN, &full[s]);
+                }
+            }
+            if (dead) {
+                const uint64_t d2 = globaltimer() + P.timeout_ns;
+                for (int j = (it > S ? it - S : 0); j < it; ++j) mbar_wait(&full[j % S], (uint32_t)(j / S) & 1u, d2);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_i8(TC_BM, TCW_BN);
+            int it = 0, ut = 0;
+            TcPieces pc(P);
+            while (pc.next(P, ta, tb, kb0, kb1)) {
+                const uint32_t use = (uint32_t)ut++;
+                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t r = (uint32_t)(it / S);
+                    if (flags[0]) break;
+                    if (!mbar_wait(&full[s], r & 1u, deadline)) {
+                        report(P.status, ST_PIPE_TIMEOUT | 0x31u);
+                        flags[0] = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sbase = smem_u32(tiles + (size_t)s * Lay::STAGE);
+                    const uint64_t bdesc = sw128_desc(sbase + 2 * Lay::A_BYTES);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        if (kb == kb0 && use > 0) {   // accumulator h of the previous tile drained
+                            if (!flags[0] && !mbar_wait(&tempty[h], (use - 1) & 1u, deadline)) {
+                                report(P.status, ST_PIPE_TIMEOUT | 0x21u);
+                                flags[0] = 1;
+                            }
+                            tc_fence_after();
+                        }
+                        const uint64_t adesc = sw128_desc(sbase + h * Lay::A_BYTES);
+                        const uint32_t d = tmem_base + (uint32_t)(h * TCW_BN);
+#pragma unroll
+                        for (int k = 0; k < TC_BK / 32; ++k)
+                            umma_i8(d, adesc + 2 * k, bdesc + 2 * k, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (!flags[0]) umma_commit(tfull);
+            }
+            umma_commit(drain);
+            mbar_wait(drain, 0u, globaltimer() + P.timeout_ns);
+        }
+    } else {
+        // ---------------- epilogue: warps 2..5 drain a0, warps 6..9 drain a1, concurrently ----------------
+        const int q = warp & 3;          // the TMEM lane quarter this warp may access
+        const int h = (warp - 2) >> 2;   // the accumulator half it drains
+        const int row = q * 32 + lane;
+        const int bar = TC_EPI_BAR + h, lead = TC_EPI_LEAD + 128 * h;   // this half's four warps
+        fin.on_start(P, epi_sm);
+        named_sync(TC_EPI_BAR + 2, 256);   // all eight epilogue warps (barrier ids 1, 2: the halves; 3: all)
+        fin.post_start();
+        int ut = 0;
+        TcPieces pc(P);
+        while (pc.next(P, ta, tb, kb0, kb1)) {
+            const uint32_t use = (uint32_t)ut++;
+            if (!flags[0] && !mbar_wait_sleep(tfull, use & 1u, deadline, 256)) {
+                report(P.status, ST_PIPE_TIMEOUT | 0x41u);
+                flags[0] = 1;
+            }
+            tc_fence_after();
+            const int ta2 = ta * 2 + h;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * TCW_BN);
+            const bool live = ta2 * TC_BM < P.M;   // a half past M holds only zero rows: nothing to finish
+            if (live) {
+                if constexpr (TcPrefillHooks<Fin>::value)
+                    fin.prefill_tile(P, ta2 * TC_BM + row, ta2, tb, taddr);
+                else
+                    tc_prefill_epilogue<T, TCW_BN>(P, ta2 * TC_BM + row, tb, taddr);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[h]);
+            if constexpr (TcPrefillHooks<Fin>::value)
+                if (live) fin.prefill_tile_done(P, ta2, tb, bar, lead);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, Lay::TMEM_COLS);
+    }
+    __syncthreads();
+}
+
+inline int tc_wide_stages(int dev, int epi_floats = 64) {
+    const int cap = max_smem_optin(dev);
+    int s = (cap - 1024 - TcWideLayout::BAR_BYTES - 4 * epi_floats - 1024) / TcWideLayout::STAGE;
+    return s > 8 ? 8 : s;
+}
+inline int tc_wide_smem_bytes(int stages, int epi_floats = 64) {
+    return stages * TcWideLayout::STAGE + 1024 + TcWideLayout::BAR_BYTES + 4 * epi_floats;
+}
+
+// VLLM_TURING_PREFILL_WIDE=0 selects the 128 x 256 prefill tiles (tc_phase) instead of the 256 x 256 ones.
+inline bool prefill_wide() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_PREFILL_WIDE");
+        v = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    return v != 0;
 }
 
 // ---- host side -------------------------------------------------------------------------------------------------------

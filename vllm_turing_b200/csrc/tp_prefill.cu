@@ -11,7 +11,7 @@
 // and overlaps them only by chunking the token rows across two streams (vllm_turing/tailoverlap.py:165-204). Here the
 // rows are owned by ranks (rank o owns rows [o R, (o + 1) R), R = M / world) and two kernels run per call:
 //
-//  1. tp_prefill_gemm_kernel: the tcgen05 prefill GEMM (tc_core.cuh, 128 x 256 tiles). Its epilogue writes each
+//  1. tp_prefill_gemm_kernel: the tcgen05 prefill GEMM (tc_core.cuh, 256 x 256 tiles). Its epilogue writes each
 //     finished tile, dequantised, straight into the receive buffer of the rank owning the tile's rows (NVLink stores for
 //     a peer, HBM for itself) and then releases a per-tile flag there. The reduce-scatter's traffic thus leaves tile by
 //     tile while the tensor cores work on the next tiles; no partial is ever written to this rank's own memory first.
@@ -102,12 +102,13 @@ struct PfRsEpi {
             }
         }
     }
-    // all four epilogue warps: the tile's stores are performed (system scope) before its flag is released
-    __device__ __forceinline__ void prefill_tile_done(const TcArgs &, int ta, int tb) const {
+    // the four epilogue warps that stored the tile (named barrier `bar`, first thread `lead`): the stores are
+    // performed (system scope) before the tile's flag is released
+    __device__ __forceinline__ void prefill_tile_done(const TcArgs &, int ta, int tb, int bar, int lead) const {
         if (A->c.world == 1) return;   // the next kernel in the stream reads the tiles; no flags
         __threadfence_system();
-        named_sync(TC_EPI_BAR, 128);
-        if (threadIdx.x == TC_EPI_LEAD) {
+        named_sync(bar, 128);
+        if ((int)threadIdx.x == lead) {
             const int rbpr = A->R / TC_BM;   // 128-row blocks per rank
             const int owner = ta / rbpr;
             const int tile = (ta - owner * rbpr) * A->ntb + tb;
@@ -116,13 +117,17 @@ struct PfRsEpi {
     }
 };
 
-template <typename T>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+// WIDE: 256 x 256 tiles (tc_phase_wide, whose halves the finisher sees as 128-row tiles); else 128 x 256 (tc_phase).
+template <typename T, bool WIDE>
+__global__ void __launch_bounds__(WIDE ? TCW_THREADS : TC_THREADS, 1)
     tp_prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                            TcArgs P, const __grid_constant__ PfArgs<T> A) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     PfRsEpi<T> fin{&A, 0u, 0u};
-    tc_phase<T, PF_BN, false, 1>(&tmap_a, &tmap_b, P, smem_raw, fin);
+    if constexpr (WIDE)
+        tc_phase_wide<T>(&tmap_a, &tmap_b, P, smem_raw, fin);
+    else
+        tc_phase<T, PF_BN, false, 1>(&tmap_a, &tmap_b, P, smem_raw, fin);
 }
 
 // ---- kernel 2: reduce owned rows, all-gather by pulls, residual add + RMSNorm + quant ------------------------------------
@@ -636,16 +641,19 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
     if (Rmax > Rtiles) Rmax = Rtiles;
     Rmax = Rmax / TC_BM * TC_BM;
     if (Rmax < TC_BM) return VT_EARG;
-    const int stages = tc_stages<PF_BN, 1>(dev, PfRsEpi<T>::kSmemFloats);
+    const bool wide = prefill_wide();
+    const int stages = wide ? tc_wide_stages(dev, PfRsEpi<T>::kSmemFloats)
+                            : tc_stages<PF_BN, 1>(dev, PfRsEpi<T>::kSmemFloats);
     if (stages < 2) return VT_EARG;
-    const int smem = tc_smem_bytes<PF_BN, 1>(stages, PfRsEpi<T>::kSmemFloats);
-    static bool attr[2][VT_MAX_DEV] = {{false}};
-    const int ti = sizeof(T) == 2 && std::is_same<T, __half>::value ? 0 : 1;
-    if (!attr[ti][dev]) {
-        if (cudaFuncSetAttribute(tp_prefill_gemm_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
-            cudaSuccess)
+    const int smem = wide ? tc_wide_smem_bytes(stages, PfRsEpi<T>::kSmemFloats)
+                          : tc_smem_bytes<PF_BN, 1>(stages, PfRsEpi<T>::kSmemFloats);
+    auto gemm_kernel = wide ? tp_prefill_gemm_kernel<T, true> : tp_prefill_gemm_kernel<T, false>;
+    static bool attr[2][2][VT_MAX_DEV] = {{{false}}};
+    const int ti = std::is_same<T, __half>::value ? 0 : 1;
+    if (!attr[wide][ti][dev]) {
+        if (cudaFuncSetAttribute(gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
             return (int)cudaGetLastError();
-        attr[ti][dev] = true;
+        attr[wide][ti][dev] = true;
     }
     CUtensorMap mb;
     if (!tc_make_map(&mb, w, N, K, PF_BN)) return VT_EARG;
@@ -656,12 +664,13 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
         CUtensorMap ma;
         if (!tc_make_map(&ma, (const int8_t *)a + m0 * K, Mp, K, TC_BM)) return VT_EARG;
         TcArgs P{};
-        P.n_tiles_a = Mp / TC_BM;
+        P.n_tiles_a = wide ? (Mp + 2 * TC_BM - 1) / (2 * TC_BM) : Mp / TC_BM;
         P.n_tiles_b = ntb;
         P.nkb = (K + TC_BK - 1) / TC_BK;
         P.units = P.n_tiles_a * P.n_tiles_b;
         P.stream_k = 0;
-        P.group_m = P.n_tiles_a < 16 ? P.n_tiles_a : 16;
+        const int gm = wide ? 8 : 16;
+        P.group_m = P.n_tiles_a < gm ? P.n_tiles_a : gm;
         P.sa = sa + m0;
         P.sw = sw;
         P.sa_rows = 1;
@@ -686,7 +695,8 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
         A.reduced = reduced ? reduced + m0 * N : nullptr;
         A.peer_timeout = peer_timeout_ns();
         int g1 = sms < P.units ? sms : P.units;
-        if (int rc = launch_k(tp_prefill_gemm_kernel<T>, dim3(g1), dim3(TC_THREADS), smem, s, true, ma, mb, P, A))
+        if (int rc = launch_k(gemm_kernel, dim3(g1), dim3(wide ? TCW_THREADS : TC_THREADS), smem, s, true, ma, mb, P,
+                              A))
             return rc;
         if (W == 1) {
             // one rank: nothing to reduce or gather, so the row epilogue is the standalone residual + RMSNorm + quant
@@ -715,7 +725,8 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
 template <typename T>
 static void preload_prefill() {
     cudaFuncAttributes fa;
-    cudaFuncGetAttributes(&fa, tp_prefill_gemm_kernel<T>);
+    cudaFuncGetAttributes(&fa, tp_prefill_gemm_kernel<T, false>);
+    cudaFuncGetAttributes(&fa, tp_prefill_gemm_kernel<T, true>);
     cudaFuncGetAttributes(&fa, tp_prefill_tail_kernel<T, 1>);
     cudaFuncGetAttributes(&fa, tp_prefill_tail_kernel<T, 2>);
     cudaFuncGetAttributes(&fa, tp_prefill_tail_kernel<T, 3>);

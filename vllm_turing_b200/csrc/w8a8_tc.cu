@@ -3,7 +3,9 @@
 //
 //   D[rows, cols] = A[rows, K] . B[cols, K]^T   (both K-major int8), then out = dequant(D) in bf16 / fp16.
 //
-//   prefill (w8a8_big):  A = activations (128-row tiles of M), B = weights (256-row tiles of N); MMA 128 x 256 x 32.
+//   prefill (w8a8_big):  A = activations, B = weights (256-row tiles of N); 256 x 256 tiles per CTA, two 128-row A
+//                        halves sharing the B tile (tc_phase_wide; 128 x 256 tiles with VLLM_TURING_PREFILL_WIDE=0);
+//                        MMA 128 x 256 x 32.
 //                        Dequant order of the reference's CUTLASS epilogue, sa[m] * (sw[n] * acc)
 //                        (vllm_turing/csrc/w8a8_big.cu:26-35).
 //   decode (w8a8_mma):   A = weights (128-row tiles of N), B = activations (16 or 32 token rows); MMA 128 x 16|32 x 32
@@ -53,19 +55,53 @@ static int launch_tc(const CUtensorMap &ma, const CUtensorMap &mb, TcArgs P, cud
     return launch_k(tc_gemm_kernel<T, BN, SWAP, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, ma, mb, P);
 }
 
-// Prefill orientation: a [M, K] activations, w [N, K] weights, whole 128 x 256 tiles per CTA.
+// Prefill GEMM on 256 x 256 tiles (tc_phase_wide): two 128-row A halves share each 256-row B tile.
+template <typename T>
+__global__ void __launch_bounds__(TCW_THREADS, 1)
+    tc_gemm_wide_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                        TcArgs P) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    TcOutEpi<T, TCW_BN> fin{};
+    tc_phase_wide<T>(&tmap_a, &tmap_b, P, smem_raw, fin);
+}
+
+template <typename T>
+static int launch_tc_wide(const CUtensorMap &ma, const CUtensorMap &mb, TcArgs P, cudaStream_t s) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    const int stages = tc_wide_stages(dev);
+    if (stages < 2) return VT_EARG;
+    P.stages = stages;
+    const int smem = tc_wide_smem_bytes(stages);
+    static bool attr[VT_MAX_DEV] = {false};
+    if (!attr[dev]) {
+        if (cudaFuncSetAttribute(tc_gemm_wide_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return (int)cudaGetLastError();
+        attr[dev] = true;
+    }
+    int g = num_sms(dev);
+    if (g > P.units) g = P.units;
+    return launch_k(tc_gemm_wide_kernel<T>, dim3(g), dim3(TCW_THREADS), smem, s, true, ma, mb, P);
+}
+
+// Prefill orientation: a [M, K] activations, w [N, K] weights, whole tiles per CTA: 256 x 256 (default) or 128 x 256
+// (VLLM_TURING_PREFILL_WIDE=0).
 template <typename T>
 static int big_gemm(const void *a, const void *w, const float *sa, const float *sw, void *out, int M, int N, int K,
                     int s32, unsigned *status, cudaStream_t s) {
     CUtensorMap ma, mb;
     if (!tc_make_map(&ma, a, M, K, TC_BM) || !tc_make_map(&mb, w, N, K, 256)) return VT_EARG;
+    const bool wide = prefill_wide();
     TcArgs P{};
-    P.n_tiles_a = (M + TC_BM - 1) / TC_BM;
+    P.n_tiles_a = wide ? (M + 2 * TC_BM - 1) / (2 * TC_BM) : (M + TC_BM - 1) / TC_BM;
     P.n_tiles_b = (N + 255) / 256;
     P.nkb = (K + TC_BK - 1) / TC_BK;
     P.units = P.n_tiles_a * P.n_tiles_b;
     P.stream_k = 0;
-    P.group_m = P.n_tiles_a < 16 ? P.n_tiles_a : 16;   // a group's A tiles + all of B stay in L2 across a wave
+    // a group's A tiles + all of B stay in L2 across a wave (2048 activation rows per group either way)
+    const int gm = wide ? 8 : 16;
+    P.group_m = P.n_tiles_a < gm ? P.n_tiles_a : gm;
     P.sa = sa;
     P.sw = sw;
     P.sa_rows = 1;
@@ -76,6 +112,7 @@ static int big_gemm(const void *a, const void *w, const float *sa, const float *
     P.s32_out = s32;
     P.timeout_ns = pipe_timeout_ns();
     P.status = status;
+    if (wide) return launch_tc_wide<T>(ma, mb, P, s);
     return launch_tc<T, 256, false, 1>(ma, mb, P, s);
 }
 
