@@ -59,27 +59,50 @@ struct PfArgs {
     float *scales;               // [M]
     T *reduced;                  // [M, N] or NULL
     uint64_t peer_timeout;
+    int stage_rs;                // the GEMM epilogue stages its reduce-scatter stores through shared memory
 };
 
+// The reduce-scatter stores are staged (whole 64-byte row segments per store instruction) when peers are written;
+// VLLM_TURING_PF_STAGE=0 never stages, =2 stages at one rank too (a test of the staged path on one GPU).
+inline int pf_stage_rs(int world) {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_PF_STAGE");
+        v = e ? atoi(e) : 1;
+    }
+    return (v == 2 || (v == 1 && world > 1)) ? 1 : 0;
+}
+
 // ---- kernel 1: GEMM whose epilogue scatters the tiles to their owners --------------------------------------------------
+constexpr int PF_STAGE_ROWB = 80;   // bytes per row of a warp's staging chunk (64 data + 16 pad: conflict-free)
+
 template <typename T>
 struct PfRsEpi {
     static constexpr bool kPrefillHooks = true;
-    static constexpr int kSmemFloats = 64;
+    // 64 floats for the core, then a 32-row x 32-column staging chunk per epilogue warp (up to 8 warps)
+    static constexpr int kSmemFloats = 64 + 8 * 32 * PF_STAGE_ROWB / 4;
     const PfArgs<T> *A;
     unsigned seq, p;
-    __device__ __forceinline__ void on_start(const TcArgs &, float *) {
+    unsigned char *stage;   // this warp's staging chunk
+    __device__ __forceinline__ void on_start(const TcArgs &, float *sm) {
         seq = *reinterpret_cast<volatile unsigned *>(A->c.seq_ptr()) + 1u;   // this call's number (after pdl_wait)
         p = A->c.world == 1 ? 0u : (seq & 1u);   // one rank: no peer, no double buffering (the host reads parity 0)
+        stage = reinterpret_cast<unsigned char *>(sm + 64) + (size_t)((threadIdx.x >> 5) - 2) * 32 * PF_STAGE_ROWB;
     }
     __device__ __forceinline__ void post_start() {}
 
-    // thread = row m of tile (ta, tb): dequantise its 256 accumulators and store them into the owner's RS buffer
+    // thread = row m of tile (ta, tb): dequantise its 256 accumulators and store them into the owner's RS buffer.
+    // A warp holds 32 consecutive rows of one owner. Staged (A->stage_rs): each 32-column chunk goes through the warp's
+    // shared-memory chunk, so every store instruction writes 8 rows x 64 contiguous bytes (a peer's memory over NVLink
+    // takes whole segments); otherwise each thread stores its own row, 16 bytes per instruction and row.
     __device__ __forceinline__ void prefill_tile(const TcArgs &P, int m, int ta, int tb, uint32_t taddr) const {
         const int N = A->N, R = A->R;
         const int owner = m / R, lr = m - owner * R;
-        T *orow = reinterpret_cast<T *>(A->c.rs_buf(owner, p, A->c.rank) + (size_t)lr * N * sizeof(T));
+        char *rs = A->c.rs_buf(owner, p, A->c.rank);
+        T *orow = reinterpret_cast<T *>(rs + (size_t)lr * N * sizeof(T));
         const float sam = P.sa[m];
+        const int lane = threadIdx.x & 31;
+        const bool staged = A->stage_rs != 0;
 #pragma unroll 1
         for (int c = 0; c < PF_BN; c += 32) {
             uint32_t r[32];
@@ -88,17 +111,34 @@ struct PfRsEpi {
             const int n0 = tb * PF_BN + c;
 #pragma unroll
             for (int j = 0; j < 32; j += 8) {
-                if (n0 + j >= N) break;   // N % 8 == 0: a granule is whole or absent
                 uint32_t w4[4];
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
-                    const int n = n0 + j + 2 * h;
+                    const int n = min(n0 + j + 2 * h, N - 2);   // clamped past N: those granules are not stored
                     // the reference's CUTLASS epilogue order sa[m] * (sw[n] * acc) (vllm_turing/csrc/w8a8_big.cu:26-35)
                     const float v0 = __fmul_rn(sam, __fmul_rn(P.sw[n], (float)(int)r[j + 2 * h]));
                     const float v1 = __fmul_rn(sam, __fmul_rn(P.sw[n + 1], (float)(int)r[j + 2 * h + 1]));
                     w4[h] = pack2<T>(v0, v1);
                 }
-                *reinterpret_cast<uint4 *>(orow + n0 + j) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                if (staged)
+                    *reinterpret_cast<uint4 *>(stage + lane * PF_STAGE_ROWB + j * 2) = make_uint4(w4[0], w4[1], w4[2],
+                                                                                                  w4[3]);
+                else if (n0 + j < N)   // N % 8 == 0: a granule is whole or absent
+                    *reinterpret_cast<uint4 *>(orow + n0 + j) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+            if (staged) {
+                __syncwarp();
+                const int g = lane & 3;   // this lane's 16-byte granule of a row's 64 bytes
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int rw = i * 8 + (lane >> 2);   // the row (of the warp's 32) this lane stores
+                    if (n0 + g * 8 < N) {
+                        const uint4 v = *reinterpret_cast<const uint4 *>(stage + rw * PF_STAGE_ROWB + g * 16);
+                        *reinterpret_cast<uint4 *>(rs + (size_t)(lr - lane + rw) * N * sizeof(T) +
+                                                   (size_t)(n0 + g * 8) * sizeof(T)) = v;
+                    }
+                }
+                __syncwarp();   // the chunk is read: the next one may overwrite it
             }
         }
     }
@@ -694,6 +734,7 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
         A.scales = scales ? scales + m0 : nullptr;
         A.reduced = reduced ? reduced + m0 * N : nullptr;
         A.peer_timeout = peer_timeout_ns();
+        A.stage_rs = pf_stage_rs(W);
         int g1 = sms < P.units ? sms : P.units;
         if (int rc = launch_k(gemm_kernel, dim3(g1), dim3(wide ? TCW_THREADS : TC_THREADS), smem, s, true, ma, mb, P,
                               A))
