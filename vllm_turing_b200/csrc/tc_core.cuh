@@ -141,8 +141,6 @@ struct TcArgs {
     int stages;
     uint64_t timeout_ns;
     unsigned *status;
-    int light_ctas;             // stream-K: CTAs [0, light_ctas) take light_w / heavy_w of a share (0: uniform shares)
-    int light_w, heavy_w;
 };
 
 template <int BN, int KBS> struct TcLayout {
@@ -154,25 +152,13 @@ template <int BN, int KBS> struct TcLayout {
     static constexpr int BAR_BYTES = 512;           // mbarriers, TMEM slot and flags; the finisher's floats follow
 };
 
-// First K-block unit of CTA c in the stream-K partition. Uniform shares, or (light_ctas > 0) CTAs below light_ctas
-// weighted light_w against heavy_w for the others: CTA c starts at units x (weight of the CTAs before it) / (weight of
-// all), in 64-bit integer arithmetic, so every thread of every CTA computes the same bounds.
-__device__ __forceinline__ int tc_lo(const TcArgs &P, int c) {
-    const int G = gridDim.x;
-    if (P.light_ctas <= 0) return (int)((long long)P.units * c / G);
-    const long long L = P.light_ctas < G ? P.light_ctas : G;
-    const long long wc = c < L ? (long long)c * P.light_w : L * P.light_w + (long long)(c - L) * P.heavy_w;
-    const long long wt = L * P.light_w + (long long)(G - L) * P.heavy_w;
-    return (int)((long long)P.units * wc / wt);
-}
-
 // The CTA's pieces: (A tile, B tile, K-block range). Identical sequence in every role of the CTA.
 struct TcPieces {
     int idx, hi;
     __device__ __forceinline__ explicit TcPieces(const TcArgs &P) {
         if (P.stream_k) {
-            idx = tc_lo(P, blockIdx.x);
-            hi = tc_lo(P, blockIdx.x + 1);
+            idx = (int)((long long)P.units * blockIdx.x / gridDim.x);
+            hi = (int)((long long)P.units * (blockIdx.x + 1) / gridDim.x);
         } else {
             idx = blockIdx.x;
             hi = P.units;
@@ -219,21 +205,12 @@ __device__ __forceinline__ void tc_a_coords(const TcArgs &P, int ta, int kb, int
 }
 
 // First K-block unit of CTA c in the stream-K partition (the formula TcPieces uses), and the CTA holding unit u.
-__device__ __forceinline__ int tc_range_lo(const TcArgs &P, int c) { return tc_lo(P, c); }
+__device__ __forceinline__ int tc_range_lo(const TcArgs &P, int c) {
+    return (int)((long long)P.units * c / gridDim.x);
+}
 __device__ __forceinline__ int tc_owner(const TcArgs &P, int u) {
-    const int G = gridDim.x;
-    int c;
-    if (P.light_ctas <= 0) {
-        c = (int)((long long)u * G / P.units);
-    } else {   // invert the weighted bounds, then settle on lo(c) <= u < lo(c + 1)
-        const long long L = P.light_ctas < G ? P.light_ctas : G;
-        const long long wt = L * P.light_w + (long long)(G - L) * P.heavy_w;
-        const long long x = (long long)u * wt / P.units;
-        c = (int)(x < L * P.light_w ? x / P.light_w : L + (x - L * P.light_w) / P.heavy_w);
-        if (c > G - 1) c = G - 1;
-        while (c > 0 && tc_lo(P, c) > u) --c;
-    }
-    while (c + 1 < G && tc_lo(P, c + 1) <= u) ++c;
+    int c = (int)((long long)u * gridDim.x / P.units);
+    if (c + 1 < (int)gridDim.x && tc_range_lo(P, c + 1) <= u) ++c;
     return c;
 }
 // Split-K slot words: CTA c's contribution (its first piece, when that piece is not a tile's head), row r of the
@@ -575,7 +552,6 @@ __device__ __forceinline__ void tc_phase(const CUtensorMap *tmap_a, const CUtens
                     // it saves.)
                     const int clast = tc_owner(P, ta * P.nkb + P.nkb - 1);
                     for (int c = blockIdx.x + 1; c <= clast; ++c) {
-                        if (P.light_ctas > 0 && tc_lo(P, c) == tc_lo(P, c + 1)) continue;   // a CTA without units
                         uint4 v[BN / 2];
 #pragma unroll
                         for (int h = 0; h < BN / 2; ++h)

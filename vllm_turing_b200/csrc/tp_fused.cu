@@ -380,16 +380,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (!publish) comm_end(c, seq);
 }
 
-inline int row_share_pct() {
-    static int v = -1;
-    if (v < 0) {
-        const char *e = getenv("VLLM_TURING_ROW_SHARE");
-        const int x = e ? atoi(e) : 50;
-        v = x < 1 ? 1 : (x > 100 ? 100 : x);
-    }
-    return v;
-}
-
 template <typename T, int BN, int KBS>
 static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     const int dev = cur_device();
@@ -422,16 +412,6 @@ static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     if (P.M > g || tc_decode_slot_bytes(P.M, g) > P.c.L.scratch_bytes) return VT_EARG;
     const int E = row_ctas(P.c.world, P.M, g);
     P.E = E;
-    // the M x E row-epilogue CTAs take a lighter share of the weight stream, so they are already polling (and have
-    // summed most of their row) when the last tiles land (VLLM_TURING_ROW_SHARE: their share in percent, default 50)
-    const int share = row_share_pct();
-    // (only while every light CTA keeps at least one unit: weight x units >= total weight)
-    if (share < 100 && P.M * E < g &&
-        (long long)share * G.units >= (long long)P.M * E * share + (long long)(g - P.M * E) * 100) {
-        G.light_ctas = P.M * E;
-        G.light_w = share;
-        G.heavy_w = 100;
-    }
     // row epilogue buffers: ceil(N / 4 / E) words of 4 floats and a norm weight word each, in the (free) stage ring
     if ((size_t)((P.N / 4 + E - 1) / E) * 24 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
     return launch_k(tp_row_linear_tc_kernel<T, BN, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, mw, ma, G, P);
