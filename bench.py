@@ -408,8 +408,15 @@ def tail_parity(world, gloo_pg, partial, fused, chain=None):
 PREFILL_SETS = 3   # distinct layer buffers cycled by the captured step: every step's inputs are cold in L2
 
 
+def prefill_kernel_name():
+    """The prefill GEMM kernel the library picks (VLLM_TURING_PREFILL_WIDE=0: the 128 x 256 tiles)."""
+    if os.environ.get("VLLM_TURING_PREFILL_WIDE", "1") == "0":
+        return "tc_gemm_kernel (prefill, 128 x 256 tiles)"
+    return "tc_gemm_wide_kernel (prefill, 256 x 256 tiles, last round as 128-row halves)"
+
+
 def run_prefill(args, world, rank, local, dev, gloo):
-    """Config 3: the row-parallel tail of a prefill layer -- this rank's W8A8 GEMM (tcgen05, 128 x 256 tiles) ->
+    """Config 3: the row-parallel tail of a prefill layer -- this rank's W8A8 GEMM (tcgen05, 256 x 256 tiles) ->
     two-shot all-reduce over NVLink P2P -> residual add + RMSNorm + per-token int8 quant -- through the public API
     (vllm_turing::scaled_mm_, TPComm.all_reduce, quantfuse.rms_norm_dynamic_per_token_quant), captured in a CUDA graph.
     value = whole-job int8 TOPS of the GEMM part; us_per_layer, bus_gbs (the all-reduce's nccl-tests convention)."""
@@ -596,7 +603,7 @@ def run_prefill(args, world, rank, local, dev, gloo):
                                "peak_kind": pk},
                 "nvlink_peak_gbs": nvl, "nvlink_peak_kind": nvl_kind, "peak_kind": pk}
     elif t_k["gemm"] >= t_k["allreduce"] or world == 1:
-        roof = {"bound": "tensor", "kernel": "tc_gemm_kernel (prefill, 128 x 256 tiles)", "achieved": gemm_ach,
+        roof = {"bound": "tensor", "kernel": prefill_kernel_name(), "achieved": gemm_ach,
                 "peak": int8_peak, "unit": "TOP/s", "frac": gemm_ach / int8_peak, "traffic": None, "peak_kind": pk}
     else:
         ar_bus = bus_bytes / t_k["allreduce"] / 1e9

@@ -7,7 +7,8 @@ process against the oracle (int32 accumulators and the fused layer's reduced sum
     ranks uses (VLLM_TURING_ROW_CTAS);
   - launches without programmatic dependent launch (VLLM_TURING_PDL=0), and the weight prefetch into L2 ahead of the
     launch wait (VLLM_TURING_L2_PREFETCH_KB, off by default);
-  - the prefill GEMM on 128 x 256 tiles instead of 256 x 256 (VLLM_TURING_PREFILL_WIDE=0), and the fused prefill
+  - the prefill GEMM on 128 x 256 tiles instead of 256 x 256 (VLLM_TURING_PREFILL_WIDE=0), its last round as whole
+    256 x 256 tiles instead of 128-row halves (VLLM_TURING_PREFILL_SPLIT=0), and the fused prefill
     tail's reduce-scatter stores staged through shared memory at one rank too (VLLM_TURING_PF_STAGE=2)."""
 import os
 import subprocess
@@ -100,9 +101,10 @@ def child():
                                  {"VLLM_TURING_FUSED_GEMV": "1", "VLLM_TURING_ROW_CTAS": "3"},
                                  {"VLLM_TURING_PDL": "0"}, {"VLLM_TURING_L2_PREFETCH_KB": "256"},
                                  {"VLLM_TURING_PREFILL_WIDE": "0"}, {"VLLM_TURING_PF_STAGE": "2"},
-                                 {"VLLM_TURING_PF_STAGE": "2", "VLLM_TURING_PREFILL_WIDE": "0"}],
+                                 {"VLLM_TURING_PF_STAGE": "2", "VLLM_TURING_PREFILL_WIDE": "0"},
+                                 {"VLLM_TURING_PREFILL_SPLIT": "0"}],
                          ids=["fused_gemv", "kbs1", "kbs2", "row_ctas4", "gemv_row_ctas3", "no_pdl", "l2_prefetch",
-                              "prefill_128x256", "pf_staged", "pf_staged_128x256"])
+                              "prefill_128x256", "pf_staged", "pf_staged_128x256", "prefill_no_split"])
 def test_variant_in_child(env):
     e = dict(os.environ, **env)
     r = subprocess.run([sys.executable, "-c", "import tests.test_variants_gpu as t; t.child()"], cwd=ROOT, env=e,

@@ -127,6 +127,7 @@ struct TcArgs {
     int units;                  // prefill: tiles (n_tiles_a * n_tiles_b); decode: K blocks of all tiles (n_tiles_a * nkb)
     int stream_k;               // 1: decode stream-K ranges; 0: whole tiles round robin
     int group_m;                // prefill raster: A tiles per group (each group covers all B tiles)
+    int split_tail;             // wide prefill: a last round that fills at most half the grid goes as 128-row halves
     int blocked_a;              // decode: A (the weight) in the tile-blocked layout (tc_a_coords)
     int l2_prefetch_blocks;     // decode: weight K blocks past the ring prefetched into L2 before pdl_wait
     int l2_runahead;            // decode: with each weight K block loaded, the one this many blocks later is
@@ -630,6 +631,39 @@ struct TcWideLayout {
     static constexpr int BAR_BYTES = 512;
 };
 
+// The wide phase's pieces: whole 256 x 256 tiles dealt round robin over the grid (grouped raster, as TcPieces), except
+// that when the last round would keep at most half the CTAs busy, its tiles are dealt as 128-row halves instead (twice
+// the pieces, half the work each: that round ends in about half the time). A piece is (ta, tb, half): half = -1 for
+// a whole tile, 0 or 1 for one 128-row half (rows 256 ta + 128 half ..), which goes through accumulator a0 only.
+struct TcWidePieces {
+    int idx, total, whole;
+    __device__ __forceinline__ explicit TcWidePieces(const TcArgs &P) {
+        const int G = gridDim.x, U = P.units;
+        const int rounds = U / G, rem = U - rounds * G;
+        whole = (P.split_tail && rem > 0 && 2 * rem <= G) ? rounds * G : U;
+        total = whole + 2 * (U - whole);
+        idx = blockIdx.x;
+    }
+    __device__ __forceinline__ bool next(const TcArgs &P, int &ta, int &tb, int &half) {
+        if (idx >= total) return false;
+        int t;
+        if (idx < whole) {
+            t = idx;
+            half = -1;
+        } else {
+            t = whole + ((idx - whole) >> 1);
+            half = (idx - whole) & 1;
+        }
+        idx += gridDim.x;
+        const int per_group = P.group_m * P.n_tiles_b;
+        const int g = t / per_group, r = t - g * per_group;
+        const int gm = min(P.group_m, P.n_tiles_a - g * P.group_m);
+        ta = g * P.group_m + r % gm;
+        tb = r / gm;
+        return true;
+    }
+};
+
 template <typename T, class Fin>
 __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const CUtensorMap *tmap_b, const TcArgs &P,
                                               unsigned char *smem_raw, Fin &fin) {
@@ -676,11 +710,11 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            int it = 0;
+            int it = 0, half;
             bool dead = false;
-            TcPieces pc(P);
-            while (!dead && pc.next(P, ta, tb, kb0, kb1)) {
-                for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            TcWidePieces pc(P);
+            while (!dead && pc.next(P, ta, tb, half)) {
+                for (int kb = 0; kb < P.nkb; ++kb, ++it) {
                     const int s = it % S;
                     const uint32_t r = (uint32_t)(it / S);
                     if (flags[0] || !mbar_wait(&empty[s], (r & 1u) ^ 1u, deadline)) {
@@ -690,9 +724,14 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
                         break;
                     }
                     unsigned char *st = tiles + (size_t)s * Lay::STAGE;
-                    mbar_arrive_expect_tx(&full[s], (uint32_t)Lay::STAGE);
-                    tma_load_2d(st, tmap_a, kb * TC_BK, ta * 2 * TC_BM, &full[s]);
-                    tma_load_2d(st + Lay::A_BYTES, tmap_a, kb * TC_BK, ta * 2 * TC_BM + TC_BM, &full[s]);
+                    if (half < 0) {
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)Lay::STAGE);
+                        tma_load_2d(st, tmap_a, kb * TC_BK, ta * 2 * TC_BM, &full[s]);
+                        tma_load_2d(st + Lay::A_BYTES, tmap_a, kb * TC_BK, ta * 2 * TC_BM + TC_BM, &full[s]);
+                    } else {   // one 128-row half: its A rows into the first A slot
+                        mbar_arrive_expect_tx(&full[s], (uint32_t)(Lay::A_BYTES + Lay::B_BYTES));
+                        tma_load_2d(st, tmap_a, kb * TC_BK, ta * 2 * TC_BM + half * TC_BM, &full[s]);
+                    }
                     tma_load_2d(st + 2 * Lay::A_BYTES, tmap_b, kb * TC_BK, tb * TCW_BN, &full[s]);
                 }
             }
@@ -705,10 +744,13 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_i8(TC_BM, TCW_BN);
-            int it = 0, ut = 0;
-            TcPieces pc(P);
-            while (pc.next(P, ta, tb, kb0, kb1)) {
+            int it = 0, ut = 0, half;
+            TcWidePieces pc(P);
+            while (pc.next(P, ta, tb, half)) {
                 const uint32_t use = (uint32_t)ut++;
+                kb0 = 0;
+                kb1 = P.nkb;
+                const int nh = half < 0 ? 2 : 1;   // accumulators this piece writes (a half piece: a0 only)
                 for (int kb = kb0; kb < kb1; ++kb, ++it) {
                     const int s = it % S;
                     const uint32_t r = (uint32_t)(it / S);
@@ -723,7 +765,8 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
                     const uint64_t bdesc = sw128_desc(sbase + 2 * Lay::A_BYTES);
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        if (kb == kb0 && use > 0) {   // accumulator h of the previous tile drained
+                        if (h >= nh) break;
+                        if (kb == kb0 && use > 0) {   // accumulator h of the previous piece drained
                             if (!flags[0] && !mbar_wait(&tempty[h], (use - 1) & 1u, deadline)) {
                                 report(P.status, ST_PIPE_TIMEOUT | 0x21u);
                                 flags[0] = 1;
@@ -752,18 +795,20 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
         fin.on_start(P, epi_sm);
         named_sync(TC_EPI_BAR + 2, 256);   // all eight epilogue warps (barrier ids 1, 2: the halves; 3: all)
         fin.post_start();
-        int ut = 0;
-        TcPieces pc(P);
-        while (pc.next(P, ta, tb, kb0, kb1)) {
+        int ut = 0, half;
+        TcWidePieces pc(P);
+        while (pc.next(P, ta, tb, half)) {
             const uint32_t use = (uint32_t)ut++;
             if (!flags[0] && !mbar_wait_sleep(tfull, use & 1u, deadline, 256)) {
                 report(P.status, ST_PIPE_TIMEOUT | 0x41u);
                 flags[0] = 1;
             }
             tc_fence_after();
-            const int ta2 = ta * 2 + h;
+            // a whole tile: group h drains a_h (rows 128 (2 ta + h) ..); a half piece: group 0 drains a0 (its rows),
+            // group 1 has nothing to drain but still hands a1 back (the MMA side counts one hand-back per piece)
+            const int ta2 = half < 0 ? ta * 2 + h : ta * 2 + half;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * TCW_BN);
-            const bool live = ta2 * TC_BM < P.M;   // a half past M holds only zero rows: nothing to finish
+            const bool live = (half < 0 || h == 0) && ta2 * TC_BM < P.M;   // a half past M holds only zero rows
             if (live) {
                 if constexpr (TcPrefillHooks<Fin>::value)
                     fin.prefill_tile(P, ta2 * TC_BM + row, ta2, tb, taddr);
@@ -803,6 +848,16 @@ inline bool prefill_wide() {
         v = (e && atoi(e) == 0) ? 0 : 1;
     }
     return v != 0;
+}
+
+// VLLM_TURING_PREFILL_SPLIT=0 keeps the wide phase's last round as whole tiles (TcArgs::split_tail).
+inline int prefill_split_tail() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_PREFILL_SPLIT");
+        v = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    return v;
 }
 
 // ---- host side -------------------------------------------------------------------------------------------------------

@@ -711,6 +711,7 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
         P.stream_k = 0;
         const int gm = wide ? 8 : 16;
         P.group_m = P.n_tiles_a < gm ? P.n_tiles_a : gm;
+        P.split_tail = wide ? prefill_split_tail() : 0;
         P.sa = sa + m0;
         P.sw = sw;
         P.sa_rows = 1;

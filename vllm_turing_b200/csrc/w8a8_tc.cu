@@ -102,6 +102,7 @@ static int big_gemm(const void *a, const void *w, const float *sa, const float *
     // a group's A tiles + all of B stay in L2 across a wave (2048 activation rows per group either way)
     const int gm = wide ? 8 : 16;
     P.group_m = P.n_tiles_a < gm ? P.n_tiles_a : gm;
+    P.split_tail = wide ? prefill_split_tail() : 0;
     P.sa = sa;
     P.sw = sw;
     P.sa_rows = 1;
