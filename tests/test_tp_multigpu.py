@@ -200,9 +200,10 @@ def _worker(rank, world, port, q):
                                            want_acc=True)
                     err = O.w8a16_close(lb[:, r * Vs:(r + 1) * Vs], want, mag, heads[r][1].numpy(), 1)
                     check(err <= 1.0, f"lm head logits M={M} block {r}: error {err:.2f} of tolerance")
-            l0 = logits.cpu().view(torch.int16).clone()
+            lbits = logits.cpu().view(torch.int16).to(torch.int32)   # gloo has no 16-bit integer type
+            l0 = lbits.clone()
             dist.broadcast(l0, src=0)
-            check(torch.equal(l0, logits.cpu().view(torch.int16)), f"lm head logits differ from rank 0 (M={M})")
+            check(torch.equal(l0, lbits), f"lm head logits differ from rank 0 (M={M})")
 
         # ---- fused row-linear ----
         for (M, N, K) in ((16, 5120, 8704), (5, 5120, 17408 // world), (1, 5120, 17408 // world),

@@ -645,22 +645,27 @@ struct TcWidePieces {
         idx = blockIdx.x;
     }
     __device__ __forceinline__ bool next(const TcArgs &P, int &ta, int &tb, int &half) {
-        if (idx >= total) return false;
-        int t;
-        if (idx < whole) {
-            t = idx;
-            half = -1;
-        } else {
-            t = whole + ((idx - whole) >> 1);
-            half = (idx - whole) & 1;
+        for (;;) {
+            if (idx >= total) return false;
+            int t;
+            if (idx < whole) {
+                t = idx;
+                half = -1;
+            } else {
+                t = whole + ((idx - whole) >> 1);
+                half = (idx - whole) & 1;
+            }
+            idx += gridDim.x;
+            const int per_group = P.group_m * P.n_tiles_b;
+            const int g = t / per_group, r = t - g * per_group;
+            const int gm = min(P.group_m, P.n_tiles_a - g * P.group_m);
+            ta = g * P.group_m + r % gm;
+            tb = r / gm;
+            const bool dead1 = (2 * ta + 1) * TC_BM >= P.M;   // the tile's second half holds no rows of A
+            if (half < 0 && dead1) half = 0;                 // a whole tile over M's last 128 rows: its first half
+            if (half == 1 && dead1) continue;                // a half past M: nothing to compute
+            return true;
         }
-        idx += gridDim.x;
-        const int per_group = P.group_m * P.n_tiles_b;
-        const int g = t / per_group, r = t - g * per_group;
-        const int gm = min(P.group_m, P.n_tiles_a - g * P.group_m);
-        ta = g * P.group_m + r % gm;
-        tb = r / gm;
-        return true;
     }
 };
 
@@ -781,6 +786,14 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
                     }
                     umma_commit(&empty[s]);
                 }
+                // a half piece leaves a1 alone, but still takes a1's hand-back of the previous piece, so that every
+                // piece moves a1's barrier by one phase whatever the order of whole and half pieces
+                if (nh == 1 && use > 0 && !flags[0]) {
+                    if (!mbar_wait(&tempty[1], (use - 1) & 1u, deadline)) {
+                        report(P.status, ST_PIPE_TIMEOUT | 0x22u);
+                        flags[0] = 1;
+                    }
+                }
                 if (!flags[0]) umma_commit(tfull);
             }
             umma_commit(drain);
@@ -829,6 +842,14 @@ __device__ __forceinline__ void tc_phase_wide(const CUtensorMap *tmap_a, const C
         tmem_dealloc(tmem_base, Lay::TMEM_COLS);
     }
     __syncthreads();
+}
+
+// Grid of the wide phase: one CTA per SM, or per whole tile when there are fewer; with split_tail, at most half the
+// SMs' worth of tiles runs as 128-row halves on twice the CTAs (TcWidePieces: all pieces are then halves).
+inline int tc_wide_grid(int sms, const TcArgs &P) {
+    if (P.units >= sms) return sms;
+    if (P.split_tail && 2 * P.units <= sms) return 2 * P.units;
+    return P.units;
 }
 
 inline int tc_wide_stages(int dev, int epi_floats = 64) {

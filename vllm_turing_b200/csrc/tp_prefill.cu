@@ -736,7 +736,7 @@ static int prefill_fused(Comm *ch, const void *a, const void *w, const float *sa
         A.reduced = reduced ? reduced + m0 * N : nullptr;
         A.peer_timeout = peer_timeout_ns();
         A.stage_rs = pf_stage_rs(W);
-        int g1 = sms < P.units ? sms : P.units;
+        const int g1 = wide ? tc_wide_grid(sms, P) : (sms < P.units ? sms : P.units);
         if (int rc = launch_k(gemm_kernel, dim3(g1), dim3(wide ? TCW_THREADS : TC_THREADS), smem, s, true, ma, mb, P,
                               A))
             return rc;

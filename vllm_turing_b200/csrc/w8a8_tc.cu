@@ -80,8 +80,7 @@ static int launch_tc_wide(const CUtensorMap &ma, const CUtensorMap &mb, TcArgs P
             return (int)cudaGetLastError();
         attr[dev] = true;
     }
-    int g = num_sms(dev);
-    if (g > P.units) g = P.units;
+    const int g = tc_wide_grid(num_sms(dev), P);
     return launch_k(tc_gemm_wide_kernel<T>, dim3(g), dim3(TCW_THREADS), smem, s, true, ma, mb, P);
 }
 
