@@ -767,8 +767,10 @@ def run_lmhead(args, world, rank, local, dev, gloo):
     alg = Vs * K + Vs * 4 + M * K * 2 + M * Vs * 2   # weights, row scales, activations, logits
     hbm_peak, pk = peaks()
     ach = alg / t_kern / 1e9
-    tr = read_traffic().get(f"w8a16_tp{world}_m{M}")
-    roof = {"bound": "hbm", "kernel": "w8a16_tc_kernel", "achieved": ach, "peak": hbm_peak, "unit": "GB/s",
+    limbs = M <= 8 and os.environ.get("VLLM_TURING_W8A16_LIMBS", "1") != "0"   # csrc/w8a16_tc.cu's choice
+    kname = "w8a16_limb_kernel (int8 tcgen05 on exact activation limbs)" if limbs else "w8a16_tc_kernel"
+    tr = read_traffic().get(f"w8a16_limb_tp{world}_m{M}" if limbs else f"w8a16_tp{world}_m{M}")
+    roof = {"bound": "hbm", "kernel": kname, "achieved": ach, "peak": hbm_peak, "unit": "GB/s",
             "frac": ach / hbm_peak, "traffic": tr, "alg_bytes": alg, "peak_kind": pk}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

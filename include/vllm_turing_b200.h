@@ -111,9 +111,9 @@ int w8a16_gemv_rows(const void *x, const void *w, const void *s, const void *bia
 int w8a16_mma(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int cfg,
               void *stream);
 /* The same for M 1..64 in either dtype, output row stride ldo >= N (write one rank's columns of a [M, world * N]
- * logits buffer), caller-owned workspace of vt_w8a16_ws_bytes(M) bytes (256-byte aligned, zeroed once; the kernel
+ * logits buffer), caller-owned workspace of vt_w8a16_ws_bytes(M, K) bytes (256-byte aligned, zeroed once; the kernel
  * leaves it zeroed; calls sharing it must be stream-ordered). New entries. */
-size_t vt_w8a16_ws_bytes(int M);
+size_t vt_w8a16_ws_bytes(int M, int K);
 int vt_w8a16_mm(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int ldo,
                 int dtype, void *workspace, size_t ws_bytes, void *stream);
 

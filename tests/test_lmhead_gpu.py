@@ -143,7 +143,7 @@ def test_argument_checks():
     assert L.w8a16_gemv(*args, 5, 256, 60, 1, st) == -1           # K % 16
     assert L.w8a16_mma(*args, 5, 255, 64, 2, st) == -1            # N even (w8a16_mma.cu:163)
     assert L.w8a16_mma(*args, 65, 256, 64, 2, st) == -1           # M <= 64
-    ws = torch.zeros(int(L.vt_w8a16_ws_bytes(5)), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(int(L.vt_w8a16_ws_bytes(5, 64)), dtype=torch.uint8, device="cuda")
     assert L.vt_w8a16_mm(*args, 5, 256, 64, 255, 1, ws.data_ptr(), ws.numel(), st) == -1   # ldo < N
     assert L.vt_w8a16_mm(*args, 5, 256, 64, 256, 1, ws.data_ptr(), 64, st) == -1           # workspace too small
     assert L.w8a16_gemv(*args, 5, 256, 64, 1, st) == 0
@@ -151,16 +151,18 @@ def test_argument_checks():
 
 
 def test_workspace_left_zeroed_and_graph_replay():
-    """The caller's workspace is zero after the calls (split-K slots cleared by the head CTAs), and the kernel replays
-    in a CUDA graph with fresh activations."""
+    """The caller's workspace's split-K slots are zero after the calls (cleared by the head CTAs; they follow the
+    status word, the activation limbs [32, K] and their exponents), and the kernel replays in a CUDA graph with fresh
+    activations."""
     from vllm_turing_b200 import lmhead
     M, N, K = 5, 18992, 5120
+    slots = 256 + (32 * K + 255) // 256 * 256 + 256
     x, w, s, _ = _inputs(M, N, K, 5)
     dx, dw, ds = x.cuda(), w.cuda(), s.cuda()
     out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
     lmhead.mm_into(out, dx, dw, ds)
     torch.cuda.synchronize()
-    assert int(torch.count_nonzero(lmhead.workspace(dx.device)[256:])) == 0
+    assert int(torch.count_nonzero(lmhead.workspace(dx.device, K)[slots:])) == 0
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
         lmhead.mm_into(out, dx, dw, ds)
@@ -170,7 +172,7 @@ def test_workspace_left_zeroed_and_graph_replay():
         g.replay()
         torch.cuda.synchronize()
         _check(out, x2, w, s, None, 1, f"graph replay {it}")
-    assert int(torch.count_nonzero(lmhead.workspace(dx.device)[256:])) == 0
+    assert int(torch.count_nonzero(lmhead.workspace(dx.device, K)[slots:])) == 0
     del g
 
 

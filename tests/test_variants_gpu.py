@@ -3,8 +3,9 @@ process against the oracle (int32 accumulators and the fused layer's reduced sum
 1 LSB):
   - the fused row-linear's dp4a GEMV phase (VLLM_TURING_FUSED_GEMV=1);
   - the tcgen05 decode kernel's K blocks per pipeline stage (VLLM_TURING_TC_KBS = 1 or 2; 4 is the default);
-  - several CTAs per token row in the fused row epilogue, with the mailbox combine that tensor parallelism above two
-    ranks uses (VLLM_TURING_ROW_CTAS);
+  - the row-CTA epilogue of the fused row-linear instead of the tile owners (VLLM_TURING_DECODE_TAIL=rows), alone and
+    with several CTAs per token row and the mailbox combine that tensor parallelism above two ranks uses there
+    (VLLM_TURING_ROW_CTAS);
   - launches without programmatic dependent launch (VLLM_TURING_PDL=0), and the weight prefetch into L2 ahead of the
     launch wait (VLLM_TURING_L2_PREFETCH_KB, off by default);
   - the prefill GEMM on 128 x 256 tiles instead of 256 x 256 (VLLM_TURING_PREFILL_WIDE=0), its last round as whole
@@ -97,13 +98,15 @@ def child():
 
 
 @pytest.mark.parametrize("env", [{"VLLM_TURING_FUSED_GEMV": "1"}, {"VLLM_TURING_TC_KBS": "1"},
-                                 {"VLLM_TURING_TC_KBS": "2"}, {"VLLM_TURING_ROW_CTAS": "4"},
+                                 {"VLLM_TURING_TC_KBS": "2"}, {"VLLM_TURING_DECODE_TAIL": "rows"},
+                                 {"VLLM_TURING_DECODE_TAIL": "rows", "VLLM_TURING_ROW_CTAS": "4"},
                                  {"VLLM_TURING_FUSED_GEMV": "1", "VLLM_TURING_ROW_CTAS": "3"},
                                  {"VLLM_TURING_PDL": "0"}, {"VLLM_TURING_L2_PREFETCH_KB": "256"},
                                  {"VLLM_TURING_PREFILL_WIDE": "0"}, {"VLLM_TURING_PF_STAGE": "2"},
                                  {"VLLM_TURING_PF_STAGE": "2", "VLLM_TURING_PREFILL_WIDE": "0"},
                                  {"VLLM_TURING_PREFILL_SPLIT": "0"}],
-                         ids=["fused_gemv", "kbs1", "kbs2", "row_ctas4", "gemv_row_ctas3", "no_pdl", "l2_prefetch",
+                         ids=["fused_gemv", "kbs1", "kbs2", "rows_tail", "rows_tail_ctas4", "gemv_row_ctas3", "no_pdl",
+                              "l2_prefetch",
                               "prefill_128x256", "pf_staged", "pf_staged_128x256", "prefill_no_split"])
 def test_variant_in_child(env):
     e = dict(os.environ, **env)

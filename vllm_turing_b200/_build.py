@@ -122,7 +122,7 @@ SIGNATURES = {
     "w8a16_gemv": (_I, [_P] * 5 + [_I] * 4 + [_P]),
     "w8a16_gemv_rows": (_I, [_P] * 5 + [_I] * 4 + [_P, _P]),
     "w8a16_mma": (_I, [_P] * 5 + [_I] * 4 + [_P]),
-    "vt_w8a16_ws_bytes": (_SZ, [_I]),
+    "vt_w8a16_ws_bytes": (_SZ, [_I, _I]),
     "vt_w8a16_mm": (_I, [_P] * 5 + [_I] * 5 + [_P, _SZ, _P]),
     "vt_scaled_int8_quant": (_I, [_P, _P, _P, _I, _I, _I, _P]),
     "vt_rms_norm_quant": (_I, [_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _P]),

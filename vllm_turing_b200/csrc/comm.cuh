@@ -5,7 +5,8 @@
 //
 //   [0, CTRL)            control: seq (u32 @0, the last completed call), done ticket (u32 @64), status (u32 @128),
 //                        group mailbox (u64 [32 rows][16 groups][2] @4096), split-K tickets of the fused
-//                        GEMM (int [4096] @16384: GEMV row-blocks or tcgen05 tiles)
+//                        GEMM (int [4096] @16384: GEMV row-blocks or tcgen05 tiles), tile mailbox of the fused
+//                        decode tail (u64 [2 kinds][64 tiles][32 rows] @32768)
 //   LL                   LL receive slots [parity 2][src rank][ll_slot bytes]: peers push 16-byte LL words here
 //   SCRATCH              int32 split-K partial sums of the fused GEMV [ll rows][N] (local use only)
 //   RS                   two-shot reduce-scatter receive buffers [parity 2][src rank][chunk_cap bytes]
@@ -37,6 +38,8 @@ constexpr size_t COMM_TICKET_OFF = 16384;
 constexpr int COMM_TICKETS = 4096;
 constexpr int COMM_MBOX_ROWS = 32, COMM_MBOX_GROUPS = 16;
 constexpr int PF_MAX_TILES = 4096, PF_MAX_CTAS = 1024;
+constexpr size_t COMM_TMBOX_OFF = 32768;   // tile mailbox: [kind 2][COMM_TMBOX_TILES][COMM_MBOX_ROWS] u64, to 65536
+constexpr int COMM_TMBOX_TILES = 64;
 
 struct CommLayout {
     size_t ll_slot;       // bytes of one LL slot (= 2 x the data bytes it carries)
@@ -74,6 +77,12 @@ struct CommView {
     __device__ __forceinline__ unsigned *status() const { return reinterpret_cast<unsigned *>(local() + 128); }
     __device__ __forceinline__ unsigned long long *mbox() const {
         return reinterpret_cast<unsigned long long *>(local() + COMM_MBOX_OFF);
+    }
+    // fused decode tail: seq-tagged word of 128-feature tile `tile`, token row m (kind 0: sum of squares of the new
+    // residual over the tile's features, kind 1: absmax of the normalised values)
+    __device__ __forceinline__ unsigned long long *tmbox(int kind, int tile, int m) const {
+        return reinterpret_cast<unsigned long long *>(local() + COMM_TMBOX_OFF) +
+               ((size_t)kind * COMM_TMBOX_TILES + tile) * COMM_MBOX_ROWS + m;
     }
     __device__ __forceinline__ int *tickets() const { return reinterpret_cast<int *>(local() + COMM_TICKET_OFF); }
     __device__ __forceinline__ int *scratch() const { return reinterpret_cast<int *>(local() + L.scratch_off); }

@@ -127,6 +127,39 @@ inline Workspace *ws_table() {
     return t;
 }
 
+// Per-device auxiliary buffer for data a kernel rewrites in full on every call before reading it (never assumed to be
+// zero, so it is kept apart from the zeroed workspace). Grows outside stream capture only.
+inline Workspace *aux_table() {
+    static Workspace t[VT_MAX_DEV];
+    return t;
+}
+inline int aux_acquire(size_t need, cudaStream_t s, void **buf) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    std::lock_guard<std::mutex> lk(ws_mutex());
+    Workspace &w = aux_table()[dev];
+    if (w.bytes < need) {
+        if (stream_capturing(s)) return VT_ECAPTURE;
+        const size_t nb = (need + ((size_t)1 << 20) - 1) & ~(((size_t)1 << 20) - 1);
+        if (w.base) {
+            cudaStreamSynchronize(s);
+            cudaDeviceSynchronize();
+            cudaFree(w.base);
+            w.base = nullptr;
+            w.bytes = 0;
+        }
+        void *p = nullptr;
+        if (cudaMalloc(&p, nb) != cudaSuccess) {
+            cudaGetLastError();
+            return VT_ENOMEM;
+        }
+        w.base = p;
+        w.bytes = nb;
+    }
+    *buf = w.base;
+    return 0;
+}
+
 // Returns a zeroed device buffer of at least `need` bytes past the 256-byte status header of the current device (the
 // pointer returned points at the scratch; status = scratch - 256). Grows outside stream capture only.
 inline int ws_acquire(size_t need, cudaStream_t s, void **scratch, unsigned **status) {

@@ -25,6 +25,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "comm.cuh"
 #include "common.cuh"
@@ -380,6 +381,350 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (!publish) comm_end(c, seq);
 }
 
+// ---- tile-owner tail (the default decode tail of the tcgen05 phase) ------------------------------------------------
+// The CTA that finishes a 128-feature tile (its head, or the CTA holding it whole) is that tile's owner for the rest of
+// the call: thread = feature n holds the dequantised partial of all M token rows in registers, so the all-reduce, the
+// residual add and the tile's share of the RMSNorm statistics run right there, spread over the N / 128 owners instead
+// of a few CTAs per token row.
+//  1. finisher (in the GEMM phase): world > 1: push the partial as 16-byte LL words (rows 4i .. 4i + 3 of feature n)
+//     into the same owner's slot on every peer (the stream-K partition is identical on every rank), then poll the
+//     peers' words for the same features, all peers in flight at once, and sum the ranks in order 0 .. world - 1
+//     (own partial from registers). Write `reduced`; add the residual (loaded before the MMAs completed) and write it
+//     back; the tile's sum of squares per token row goes into the tile mailbox (seq-tagged word per tile and row).
+//  2. after the GEMM phase: gather every tile's sums of squares (one poll round), fold them in tile order (identical on
+//     every CTA and rank), normalise the owned features, publish the tile's absmax per row, gather all tiles' maxima,
+//     quantise. The owner of tile 0 writes the scales and publishes the call number.
+// Per call after the weight stream: split-K collection, [the NVLink exchange], two mailbox rounds -- with the work of
+// each round spread over the tile owners.
+template <typename T, int BN>
+struct TcTileTailEpi {
+    // shared floats: [0, 32) token scales, [32, 160) per-warp partials [4][32], [160, 192) per-row 1 / rms,
+    // [192, 224) per-row absmax, [224, 226) ints: owned-tile count, the owned tile
+    static constexpr int kSmemFloats = 256;
+    __device__ __forceinline__ static int *owned_of(float *smp) { return reinterpret_cast<int *>(smp + 224); }
+    struct Prep {
+        float swn;
+        float res[BN];
+    };
+    const FusedArgs<T> *F;
+    unsigned *s_seq;
+    float *sm;
+    unsigned seq;
+    int M, N, world, rank;
+    __device__ __forceinline__ int *owned() const { return owned_of(sm); }
+    __device__ __forceinline__ void on_start(const TcArgs &, float *smp) {
+        sm = smp;
+        const int t = threadIdx.x - TC_EPI_LEAD;
+        if (t < F->M) sm[t] = F->sa[t];
+        if (t == 0) {
+            *s_seq = *reinterpret_cast<volatile unsigned *>(F->c.seq_ptr()) + 1u;
+            owned()[0] = 0;
+        }
+    }
+    __device__ __forceinline__ void post_start() {
+        seq = *s_seq;
+        M = F->M;
+        N = F->N;
+        world = F->c.world;
+        rank = F->c.rank;
+    }
+    __device__ __forceinline__ Prep prep(const TcArgs &, int n) const {
+        Prep r;
+        const bool ok = n < N;
+        r.swn = ok ? F->sw[n] : 0.0f;
+        const T *res = F->residual;
+#pragma unroll
+        for (int m = 0; m < BN; ++m) r.res[m] = (res && ok && m < M) ? t2f<T>(res[(size_t)m * N + n]) : 0.0f;
+        return r;
+    }
+    __device__ __forceinline__ void operator()(const TcArgs &, int n, bool nok, const int (&acc)[BN],
+                                               const Prep &pr) const {
+        const int Mr = M, Nr = N, nw = world, rk = rank, nq = (Mr + 3) >> 2;
+        const unsigned sq = seq, par = sq & 1u;
+        float s[BN];
+#pragma unroll
+        for (int m = 0; m < BN; ++m) s[m] = (m < Mr && nok) ? rnd<T>(dequant1(acc[m], sm[m], pr.swn)) : 0.0f;
+        if (nw > 1) {
+            if (nok) {
+#pragma unroll
+                for (int k = 1; k < COMM_MAX_RANKS; ++k) {
+                    if (k >= nw) break;
+                    int dst = rk + k;
+                    if (dst >= nw) dst -= nw;
+                    char *base = F->c.ll_slot(dst, par, rk) + (size_t)n * 16;
+#pragma unroll
+                    for (int i = 0; i < BN / 4; ++i) {
+                        if (i >= nq) break;
+                        ll_store(base + (size_t)i * Nr * 16, pack2<T>(s[4 * i], s[4 * i + 1]),
+                                 pack2<T>(s[4 * i + 2], s[4 * i + 3]), sq);
+                    }
+                }
+            }
+            const uint64_t deadline = globaltimer() + F->peer_timeout;
+            bool dead = false;
+            // eight token rows (two words per peer) per round, every peer's words in flight together
+#pragma unroll
+            for (int i0 = 0; i0 < BN / 4; i0 += 2) {
+                if (i0 >= nq) break;
+                uint4 v[COMM_MAX_RANKS][2];
+#pragma unroll
+                for (int r = 0; r < COMM_MAX_RANKS; ++r) {
+                    if (r >= nw || r == rk || !nok) continue;
+                    const char *src = F->c.ll_slot(rk, par, r) + (size_t)n * 16;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j)
+                        if (i0 + j < nq) v[r][j] = ld_volatile16(src + (size_t)(i0 + j) * Nr * 16);
+                }
+#pragma unroll
+                for (int r = 0; r < COMM_MAX_RANKS; ++r) {
+                    if (r >= nw || r == rk || !nok) continue;
+                    const char *src = F->c.ll_slot(rk, par, r) + (size_t)n * 16;
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        if (i0 + j >= nq) continue;
+                        uint32_t it = 0;
+                        while (!dead && (v[r][j].y != sq || v[r][j].w != sq)) {
+                            if ((++it & 255u) == 0 && globaltimer() > deadline) {
+                                report(F->c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
+                                dead = true;
+                                break;
+                            }
+                            v[r][j] = ld_volatile16(src + (size_t)(i0 + j) * Nr * 16);
+                        }
+                    }
+                }
+                // rank-ordered float sum, own partial from registers (rank 0's value first, as the oracle)
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int m = 4 * (i0 + j) + e;
+                        if (m >= BN) continue;
+                        float t = 0.0f;
+#pragma unroll
+                        for (int r = 0; r < COMM_MAX_RANKS; ++r) {
+                            if (r >= nw) break;
+                            float x = s[m];
+                            if (r != rk) {
+                                const uint32_t w32 = (e < 2) ? v[r][j].x : v[r][j].z;
+                                const float2 f = unpack2<T>(w32);
+                                x = (e & 1) ? f.y : f.x;
+                            }
+                            t = (r == 0) ? x : t + x;
+                        }
+                        if (i0 + j < nq) s[m] = t;
+                    }
+                }
+            }
+        }
+        T *const red = F->reduced;
+        if (red && nok) {
+#pragma unroll
+            for (int m = 0; m < BN; ++m)
+                if (m < Mr) red[(size_t)m * Nr + n] = f2t<T>(s[m]);
+        }
+        T *const res = F->residual;
+        if (!res) return;
+        const int t = threadIdx.x - TC_EPI_LEAD, q = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
+        float *part = sm + 32;
+#pragma unroll
+        for (int m = 0; m < BN; ++m) {
+            if (m >= Mr) break;   // uniform
+            const float h = rnd<T>(rnd<T>(s[m]) + pr.res[m]);
+            if (nok) res[(size_t)m * Nr + n] = f2t<T>(h);
+            float x = nok ? h * h : 0.0f;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+            if (lane == 0) part[q * 32 + m] = x;
+        }
+        named_sync(TC_EPI_BAR, 128);
+        const int ta = n >> 7;
+        if (t < Mr) {
+            const float x = ((part[t] + part[32 + t]) + part[64 + t]) + part[96 + t];
+            st_volatile8(F->c.tmbox(0, ta, t), ((unsigned long long)sq << 32) | __float_as_uint(x));
+        }
+        if (t == 0) {   // at most one tile per CTA (the launch checks it)
+            int *o = owned();
+            o[0] = 1;
+            o[1] = ta;
+        }
+    }
+};
+
+// Gathers kind `kind` of every tile's mailbox word for the M token rows into buf[m * 64 + tile] (all threads of the
+// CTA; the words of all tiles and rows are in flight together, one poll round).
+__device__ __forceinline__ void tt_gather(const CommView &c, int kind, int T, int M, unsigned seq, float *buf,
+                                          uint64_t deadline) {
+    for (int j = threadIdx.x; j < T * M; j += blockDim.x) {
+        const int m = j / T, tile = j - m * T;
+        const unsigned long long *p = c.tmbox(kind, tile, m);
+        unsigned long long x = ld_volatile8(p);
+        uint32_t it = 0;
+        while ((unsigned)(x >> 32) != seq) {
+            if ((++it & 63u) == 0 && globaltimer() > deadline) {
+                report(c.status(), ST_GROUP_TIMEOUT | 0x700u | (unsigned)kind);
+                break;
+            }
+            x = ld_volatile8(p);
+        }
+        buf[m * COMM_TMBOX_TILES + tile] = __uint_as_float((unsigned)x);
+    }
+}
+
+// Phase 2 of the tile-owner tail: every thread of the CTA calls it after the GEMM phase (residual mode). The launch
+// guarantees that a CTA owns at most one tile (its stream-K range is shorter than a tile's K range, or one unit).
+template <typename T, int BN>
+__device__ __forceinline__ void tile_tail_post(const FusedArgs<T> &P, unsigned seq, float *sm, float *buf) {
+    using Epi = TcTileTailEpi<T, BN>;
+    const int *own = Epi::owned_of(sm);
+    if (own[0] == 0) return;   // uniform: this CTA finished no tile
+    const int ta = own[1];
+    const CommView &c = P.c;
+    const int M = P.M, N = P.N, NT = (N + TC_BM - 1) / TC_BM;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+    const bool epi = tid >= TC_EPI_LEAD;
+    // epilogue thread -> feature of the tile as in the GEMM phase (TMEM lane quarter warp % 4): each thread re-reads
+    // the residual values it wrote there
+    const int q = warp & 3, t = tid - TC_EPI_LEAD;
+    const int n = ta * TC_BM + q * 32 + lane;
+    const bool nok = epi && n < N;
+    T *const res = P.residual;
+    float *part = sm + 32, *rs = sm + 160, *amax = sm + 192;
+    const uint64_t deadline = globaltimer() + P.peer_timeout;
+    // the new residual and the norm weight: loads in flight during the first gather
+    float y[BN];
+#pragma unroll
+    for (int m = 0; m < BN; ++m) y[m] = (nok && m < M) ? t2f<T>(res[(size_t)m * N + n]) : 0.0f;
+    const float wn = nok ? t2f<T>(P.norm_w[n]) : 0.0f;
+    tt_gather(c, 0, NT, M, seq, buf, deadline);
+    __syncthreads();
+    for (int m = warp; m < M; m += nwarps) {   // sum of squares over the tiles, tile order fixed
+        float x = lane < NT ? buf[m * COMM_TMBOX_TILES + lane] : 0.0f;
+        if (lane + 32 < NT) x += buf[m * COMM_TMBOX_TILES + lane + 32];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+        if (lane == 0) rs[m] = __frsqrt_rn(__fdiv_rn(x, (float)N) + P.eps);
+    }
+    __syncthreads();
+    // Every tile was finished, so every CTA of the grid has read this call's number: publish it for the next call.
+    if (tid == 0 && ta == 0) *reinterpret_cast<volatile unsigned *>(c.seq_ptr()) = seq;
+    if (epi) {   // normalise; the tile's absmax per token row
+#pragma unroll
+        for (int m = 0; m < BN; ++m) {
+            if (m >= M) break;
+            y[m] = nok ? rnd<T>(__fmul_rn(__fmul_rn(y[m], rs[m]), wn)) : 0.0f;
+            float a = fabsf(y[m]);
+#pragma unroll
+            for (int k = 16; k > 0; k >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, k));
+            if (lane == 0) part[q * 32 + m] = a;
+        }
+    }
+    __syncthreads();
+    if (epi && t < M) {
+        const float a = fmaxf(fmaxf(part[t], part[32 + t]), fmaxf(part[64 + t], part[96 + t]));
+        st_volatile8(c.tmbox(1, ta, t), ((unsigned long long)seq << 32) | __float_as_uint(a));
+    }
+    tt_gather(c, 1, NT, M, seq, buf + COMM_MBOX_ROWS * COMM_TMBOX_TILES, deadline);
+    __syncthreads();
+    buf += COMM_MBOX_ROWS * COMM_TMBOX_TILES;
+    for (int m = warp; m < M; m += nwarps) {   // max: the same in any order
+        float a = lane < NT ? buf[m * COMM_TMBOX_TILES + lane] : 0.0f;
+        if (lane + 32 < NT) a = fmaxf(a, buf[m * COMM_TMBOX_TILES + lane + 32]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        if (lane == 0) amax[m] = a;
+    }
+    __syncthreads();
+    if (ta == 0 && tid < M) P.scales[tid] = __fdiv_rn(amax[tid], 127.0f);
+    if (!nok) return;
+    int8_t *const qo = P.q;
+#pragma unroll
+    for (int m = 0; m < BN; ++m) {
+        if (m >= M) break;
+        qo[(size_t)m * N + n] = quant1(y[m], quant_inv(amax[m]));
+    }
+}
+
+// The fused kernel with the tile-owner tail. Launched with programmatic dependent launch (see tp_row_linear_tc_kernel).
+template <typename T, int BN, int KBS>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tp_row_linear_tt_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+                            TcArgs G, FusedArgs<T> P) {
+    using Lay = TcLayout<BN, KBS>;
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    __shared__ unsigned s_seq;
+    TcTileTailEpi<T, BN> fin{&P, &s_seq, nullptr, 0u, 0, 0, 0, 0};
+    tc_phase<T, BN, true, KBS>(&tmap_w, &tmap_a, G, smem_raw, fin);   // ends with __syncthreads
+    const unsigned seq = s_seq;
+    unsigned char *ring = tc_align1024(smem_raw);
+    float *sm = reinterpret_cast<float *>(ring + (size_t)G.stages * Lay::STAGE + Lay::BAR_BYTES);
+    if (P.residual)
+        tile_tail_post<T, BN>(P, seq, sm, reinterpret_cast<float *>(ring));   // the stage ring is free now
+    else
+        comm_end(P.c, seq);
+}
+
+// VLLM_TURING_DECODE_TAIL=rows selects the row-CTA epilogue (tp_row_linear_tc_kernel) instead of the tile owners.
+static bool decode_tail_rows() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_DECODE_TAIL");
+        v = (e && strcmp(e, "rows") == 0) ? 1 : 0;
+    }
+    return v != 0;
+}
+
+// The tile-owner tail's limits: N / 128 tiles in the mailbox, each peer's LL words ((M + 3) / 4 x 16 bytes per
+// feature) in one LL slot, and at most one tile owned per CTA: every CTA's stream-K range (ceil(units / grid) K
+// blocks) shorter than a tile's K blocks, or a single unit.
+inline bool tile_tail_fits(const CommView &c, int M, int N, int K) {
+    const int NT = (N + TC_BM - 1) / TC_BM, nkb = (K + TC_BK - 1) / TC_BK;
+    if (NT > COMM_TMBOX_TILES) return false;
+    const int dev = cur_device();
+    if (dev < 0) return false;
+    long long units = (long long)NT * nkb, g = num_sms(dev);
+    if (g > units) g = units;
+    const long long L = (units + g - 1) / g;
+    if (!(L < nkb || L == 1)) return false;
+    return c.world == 1 || (size_t)((M + 3) / 4) * 16 * (size_t)N <= c.L.ll_slot;
+}
+
+template <typename T, int BN, int KBS>
+static int launch_fused_tt(FusedArgs<T> P, cudaStream_t s) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    using Epi = TcTileTailEpi<T, BN>;
+    CUtensorMap mw, ma;
+    if (!tc_make_map(&mw, P.w, P.N, P.K, TC_BM) || !tc_make_map(&ma, P.a, P.M, P.K, BN)) return VT_EARG;
+    TcArgs G{};
+    tc_decode_args(G, P.M, P.N, P.K);
+    G.sa = P.sa;
+    G.sw = P.sw;
+    G.sa_rows = 1;
+    G.sw_rows = 1;
+    char *local = P.c.base[P.c.rank];
+    G.slots = reinterpret_cast<uint4 *>(local + P.c.L.scratch_off);
+    G.status = reinterpret_cast<unsigned *>(local + 128);
+    G.timeout_ns = P.pipe_timeout;
+    const int stages = tc_stages<BN, KBS>(dev, Epi::kSmemFloats, decode_smem_budget());
+    if (stages < 2) return VT_EARG;
+    G.stages = stages;
+    const int smem = tc_smem_bytes<BN, KBS>(stages, Epi::kSmemFloats);
+    static bool attr_set[VT_MAX_DEV] = {false};
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(tp_row_linear_tt_kernel<T, BN, KBS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 smem) != cudaSuccess)
+            return (int)cudaGetLastError();
+        attr_set[dev] = true;
+    }
+    int g = num_sms(dev);
+    if (g > G.units) g = G.units;
+    if (tc_decode_slot_bytes(P.M, g) > P.c.L.scratch_bytes) return VT_EARG;
+    // the post phase's two gather buffers ([32][64] floats each) in the stage ring
+    if ((size_t)2 * COMM_MBOX_ROWS * COMM_TMBOX_TILES * 4 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
+    return launch_k(tp_row_linear_tt_kernel<T, BN, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, mw, ma, G, P);
+}
+
 template <typename T, int BN, int KBS>
 static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
     const int dev = cur_device();
@@ -419,6 +764,13 @@ static int launch_fused_tc(FusedArgs<T> P, cudaStream_t s) {
 
 template <typename T, int BN>
 static int fused_tc_kbs(FusedArgs<T> P, cudaStream_t s) {
+    if (!decode_tail_rows() && tile_tail_fits(P.c, P.M, P.N, P.K)) {
+        switch (decode_kbs()) {
+            case 1: return launch_fused_tt<T, BN, 1>(P, s);
+            case 2: return launch_fused_tt<T, BN, 2>(P, s);
+            default: return launch_fused_tt<T, BN, 4>(P, s);
+        }
+    }
     switch (decode_kbs()) {
         case 1: return launch_fused_tc<T, BN, 1>(P, s);
         case 2: return launch_fused_tc<T, BN, 2>(P, s);
@@ -499,6 +851,12 @@ static void preload_fused() {
     cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 32, 1>);
     cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 32, 2>);
     cudaFuncGetAttributes(&fa, tp_row_linear_tc_kernel<T, 32, 4>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tt_kernel<T, 16, 1>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tt_kernel<T, 16, 2>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tt_kernel<T, 16, 4>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tt_kernel<T, 32, 1>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tt_kernel<T, 32, 2>);
+    cudaFuncGetAttributes(&fa, tp_row_linear_tt_kernel<T, 32, 4>);
 }
 
 }  // namespace vt

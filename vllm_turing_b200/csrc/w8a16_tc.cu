@@ -1,20 +1,28 @@
 // W8A16 GEMM for the LM head on the B200 tensor cores: int8 weight rows with one fp32 scale each, 16-bit float
-// activations (bf16 or fp16), tcgen05.mma kind::f16 with fp32 accumulators in tensor memory (TMEM).
+// activations (bf16 or fp16).
 //
 //   out[m, n] = T((sum_k x[m, k] * W[n, k]) * s[n] + bias[n])      x [M, K], W [N, K] int8 row-major, s [N] fp32
 //
-// This is the arithmetic of the reference's W8A16 kernels (vllm_turing/csrc/w8a16_gemv.cu:27-107 on CUDA-core fp32
-// FMAs, vllm_turing/csrc/w8a16_mma.cu on fp16 mma.sync): every product of an int8 weight and a 16-bit activation is
-// exact in fp32, the sums are fp32, and the row scale and the bias are applied to the finished sum
-// (w8a16_gemv.cu:103). Only the order of the fp32 additions differs from the reference's, so results agree to the
-// rounding of fp32 sums, not bit for bit.
+// The reference's W8A16 kernels (vllm_turing/csrc/w8a16_gemv.cu:27-107 on CUDA-core fp32 FMAs,
+// vllm_turing/csrc/w8a16_mma.cu on fp16 mma.sync) form every product of an int8 weight and a 16-bit activation exactly
+// in fp32, sum in fp32 and apply the row scale and the bias to the finished sum (w8a16_gemv.cu:103). Two kernels here:
 //
-// Work layout (the decode orientation of the W8A8 core, tc_core.cuh): the weights are the MMA's A operand in 128-row
+// 1. Decode, M <= 8 token rows (the default there): the limb GEMM. Each activation row becomes four int8 rows of one
+//    fixed-point integer per element (a power of two per token row, base-256 signed digits: exact for every element
+//    down to 2^-19 of the row's absmax), the weights stay int8, and the contraction runs on the int8 tensor cores of
+//    the W8A8 decode core (tc_core.cuh: tcgen05 kind::i8, weights as the A operand in 128-row tiles fed by TMA,
+//    stream-K over the SMs, exact int32 split-K through LL slot words). The finisher combines the four limb sums of a
+//    token into the exact int64 dot product and rounds it once to fp32 before the reference's epilogue: the results
+//    are the correctly rounded sums, closer to the exact value than any fp32 summation order. No weight byte is
+//    converted, so the kernel streams like the int8 decode GEMM.
+// 2. M <= 64 (and M <= 8 with VLLM_TURING_W8A16_LIMBS=0): tcgen05 kind::f16 with fp32 accumulators in tensor memory
+//    (TMEM); the int8 -> 16-bit conversion runs between shared memory and the tensor core, into TMEM. Only the order
+//    of the fp32 additions differs from the reference's, so results agree to the rounding of fp32 sums.
+//
+// Work layout of kernel 2 (the decode orientation of the W8A8 core): the weights are the MMA's A operand in 128-row
 // tiles of the vocabulary; the M <= 64 token rows are its B operand (BN = 16, 32 or 64 rows, zero-filled past M). The
 // (tile, K block) index space is cut into one contiguous range per CTA (stream-K), so every SM streams the same share
 // of the weights. A split tile is finished by its head CTA from the other CTAs' fp32 partial sums (LL slot words).
-//
-// The int8 -> 16-bit conversion runs between shared memory and the tensor core, into TMEM:
 //   - warp 0 (one thread) TMA-loads each K block of weights (128 rows x 128 bytes, 128-byte swizzle) into a ring of
 //     16 KB shared-memory stages; warp 6 (one thread) loads the K block's activations (two 64-element swizzle atoms
 //     of BN rows) into a separate, smaller ring;
@@ -505,6 +513,129 @@ __global__ void __launch_bounds__(256) w8a16_rows_kernel(const T *__restrict__ x
     }
 }
 
+// ---- exact int8 limbs of the activations (decode: M <= 8 token rows) ------------------------------------------------
+// A 16-bit float row x[m, :] is written as integers X[k] = round(x[k] * 2^-e[m]) with one power of two per row, chosen
+// so that max |X| < 2^30: X is exact for every element of magnitude at least 2^-19 of the row's absmax (a bf16 / fp16
+// value has at most 11 significant bits), smaller ones are rounded to a multiple of 2^e (an error below 2^-30 of the
+// row's absmax). X is
+// split into four signed base-256 digits ("limbs"), X = l3 2^24 + l2 2^16 + l1 2^8 + l0, l_j in [-128, 127]. The
+// LM head then runs on the int8 tensor cores (kind::i8, int32 accumulators) with B = the 4M limb rows:
+//   sum_k x[m, k] W[n, k] = 2^e[m] * sum_j 2^(8 j) * (sum_k l_j[m, k] W[n, k])
+// where every inner sum is an exact int32 (|W l| <= 2^14, K < 2^17) and the combination is an exact int64 (< 2^53).
+// The finisher rounds that exact sum once to fp32 and applies the reference's fp32 epilogue (acc * s + bias): the
+// result is the correctly rounded dot product, not one fp32 summation order of it. No weight byte is converted.
+constexpr int WL_MAX_M = 8;   // 4 limbs x 8 token rows = the 32 B rows of the decode core
+
+// limbs [4M, K] int8 (row 4 m + j = limb j of token m), exps[m]: one CTA per token row. Launched with programmatic
+// dependent launch: the GEMM after it starts its weight stream meanwhile.
+template <typename T>
+__global__ void __launch_bounds__(256) w8a16_limbs_kernel(const T *__restrict__ x, int K, int8_t *__restrict__ limbs,
+                                                           int *__restrict__ exps) {
+    __shared__ float red[8];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const T *xr = x + (size_t)m * K;
+    float mx = 0.0f;
+    for (int i = tid * 8; i < K; i += 256 * 8) {   // K % 16 == 0: whole 8-element vectors
+        const uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = unpack2<T>(w[j]);
+            mx = fmaxf(mx, fmaxf(fabsf(f.x), fabsf(f.y)));
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
+    int e = 0;
+    if (mx > 0.0f) {   // mx = f 2^E2 with f in [0.5, 1): max |x| < 2^E2, so X < 2^30 with e = E2 - 30
+        int E2;
+        frexpf(mx, &E2);
+        e = E2 - 30;
+    }
+    if (tid == 0) exps[m] = e;
+    int8_t *l0 = limbs + (size_t)(4 * m) * K;
+    for (int i = tid * 8; i < K; i += 256 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(xr + i);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t out[4][2] = {};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float2 f = unpack2<T>(w[j >> 1]);
+            int X = __float2int_rn(ldexpf((j & 1) ? f.y : f.x, -e));
+            const int sh = (j & 3) * 8, h = j >> 2;
+#pragma unroll
+            for (int l = 0; l < 3; ++l) {
+                const int d = (int)(int8_t)(X & 0xff);   // the signed digit; X - d is a multiple of 256
+                out[l][h] |= (uint32_t)(d & 0xff) << sh;
+                X = (X - d) >> 8;
+            }
+            out[3][h] |= (uint32_t)(X & 0xff) << sh;   // |X| <= 65 here
+        }
+#pragma unroll
+        for (int l = 0; l < 4; ++l)
+            *reinterpret_cast<uint2 *>(l0 + (size_t)l * K + i) = make_uint2(out[l][0], out[l][1]);
+    }
+}
+
+// Finisher of the limb GEMM (tc_phase, decode orientation, B rows = 4 M limb rows): thread = vocabulary row n,
+// acc[4 m + j] the exact sums of limb j of token m.
+template <typename T, int BN>
+struct WhLimbEpi {
+    static constexpr int kSmemFloats = 64;
+    struct Prep {
+        float sn, bn;
+    };
+    const int *exps;
+    const float *s;
+    const T *bias;
+    T *out;
+    int M, ldo;
+    int *e_sm;
+    __device__ __forceinline__ void on_start(const TcArgs &, float *sm) {
+        e_sm = reinterpret_cast<int *>(sm);
+        const int t = threadIdx.x - TC_EPI_LEAD;
+        if (t < M) e_sm[t] = exps[t];
+    }
+    __device__ __forceinline__ void post_start() {}
+    __device__ __forceinline__ Prep prep(const TcArgs &P, int n) const {
+        Prep r{0.0f, 0.0f};
+        if (n < P.N) {
+            r.sn = s[n];
+            if (bias) r.bn = t2f<T>(bias[n]);
+        }
+        return r;
+    }
+    __device__ __forceinline__ void operator()(const TcArgs &, int n, bool nok, const int (&acc)[BN],
+                                               const Prep &pr) const {
+        if (!nok) return;
+#pragma unroll
+        for (int m = 0; m < BN / 4; ++m) {
+            if (m >= M) break;
+            const long long S = (long long)acc[4 * m] + ((long long)acc[4 * m + 1] << 8) +
+                                ((long long)acc[4 * m + 2] << 16) + ((long long)acc[4 * m + 3] << 24);
+            // 2^e as a double built from its exponent field (e in [-180, 98]): the product is exact
+            const double p2 = __longlong_as_double((long long)(e_sm[m] + 1023) << 52);
+            const float v = __double2float_rn((double)S * p2);
+            out[(size_t)m * ldo + n] = f2t<T>(__fmaf_rn(v, pr.sn, pr.bn));   // (acc * s + b): one fp32 rounding
+        }
+    }
+};
+
+template <typename T, int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    w8a16_limb_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_l,
+                      TcArgs G, WhLimbEpi<T, BN> fin) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    tc_phase<T, BN, true, 4>(&tmap_w, &tmap_l, G, smem_raw, fin);
+}
+
 // ---- host side -------------------------------------------------------------------------------------------------------
 template <int BN> inline int wh_stages(int dev) {   // weight stages
     const int fixed = 1024 + WH_BAR_BYTES + 1024 + WhLayout<BN>::XS * WhLayout<BN>::X_STAGE;
@@ -563,9 +694,72 @@ static bool wh_args_ok(const void *x, const void *w, const void *s, const void *
            ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0;
 }
 
+// Caller-owned workspace of vt_w8a16_mm: [256-byte status][limbs: 4 WL_MAX_M rows x K][exps: 256 bytes][split-K
+// slots, zeroed]. Through the library workspace the slots come from the zeroed workspace and the limbs from the
+// auxiliary buffer (host_util.h), since other kernels rely on the zeroed workspace staying zero.
+static size_t wl_limb_bytes(int K) { return ((size_t)4 * WL_MAX_M * K + 255) & ~(size_t)255; }
+static size_t wh_slots_bytes(int M) {
+    const size_t v2 = wh_slot_bytes(M), limb = tc_decode_slot_bytes(4 * (M < WL_MAX_M ? M : WL_MAX_M),
+                                                                    num_sms(cur_device()));
+    return v2 > limb ? v2 : limb;
+}
+static size_t wh_ws_bytes(int M, int K) { return 256 + wl_limb_bytes(K) + 256 + wh_slots_bytes(M); }
+
+// VLLM_TURING_W8A16_LIMBS=0 keeps M <= 8 on the int8 -> 16-bit converting kernel (default: the limb GEMM).
+inline bool w8a16_limbs() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_W8A16_LIMBS");
+        v = (e && atoi(e) == 0) ? 0 : 1;
+    }
+    return v != 0;
+}
+
+// limbs: wl_limb_bytes(K) + 256 bytes (the limbs, then the exponents), rewritten by every call; slots: zeroed split-K
+// slots (left zeroed); status: the status word.
+template <typename T, int BN>
+static int launch_wl(const void *x, const void *w, const float *s, const void *bias, void *out, int M, int N, int K,
+                     int ldo, unsigned *status, void *limbs_buf, void *slots, cudaStream_t st) {
+    const int dev = cur_device();
+    if (dev < 0 || dev >= VT_MAX_DEV) return VT_EARG;
+    int8_t *limbs = (int8_t *)limbs_buf;
+    int *exps = reinterpret_cast<int *>(limbs + wl_limb_bytes(K));
+    if (int rc = launch_k(w8a16_limbs_kernel<T>, dim3(M), dim3(256), 0, st, true, (const T *)x, K, limbs, exps))
+        return rc;
+    CUtensorMap mw, ml;
+    if (!tc_make_map(&mw, w, N, K, TC_BM) || !tc_make_map(&ml, limbs, 4 * M, K, BN)) return VT_EARG;
+    TcArgs G{};
+    tc_decode_args(G, 4 * M, N, K);
+    G.l2_prefetch_blocks = 0;
+    G.slots = (uint4 *)slots;
+    G.status = status;
+    G.timeout_ns = pipe_timeout_ns();
+    using Fin = WhLimbEpi<T, BN>;
+    const int stages = tc_stages<BN, 4>(dev, Fin::kSmemFloats);
+    if (stages < 2) return VT_EARG;
+    G.stages = stages;
+    const int smem = tc_smem_bytes<BN, 4>(stages, Fin::kSmemFloats);
+    static bool attr[VT_MAX_DEV] = {false};
+    if (!attr[dev]) {
+        if (cudaFuncSetAttribute(w8a16_limb_kernel<T, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return (int)cudaGetLastError();
+        attr[dev] = true;
+    }
+    int g = num_sms(dev);
+    if (g > G.units) g = G.units;
+    Fin fin{exps, s, (const T *)bias, (T *)out, M, ldo, nullptr};
+    return launch_k(w8a16_limb_kernel<T, BN>, dim3(g), dim3(TC_THREADS), smem, st, true, mw, ml, G, fin);
+}
+
+// M <= WL_MAX_M runs the limb GEMM (limbs_buf as above) unless switched off; otherwise the converting kernel.
 template <typename T>
 static int w8a16_tc(const void *x, const void *w, const float *s, const void *bias, void *out, int M, int N, int K,
-                    int ldo, void *scratch, unsigned *status, cudaStream_t st) {
+                    int ldo, unsigned *status, void *limbs_buf, void *slots, cudaStream_t st) {
+    if (M <= WL_MAX_M && w8a16_limbs()) {
+        if (M <= 4) return launch_wl<T, 16>(x, w, s, bias, out, M, N, K, ldo, status, limbs_buf, slots, st);
+        return launch_wl<T, 32>(x, w, s, bias, out, M, N, K, ldo, status, limbs_buf, slots, st);
+    }
     const int BN = M <= 16 ? 16 : (M <= 32 ? 32 : 64);
     CUtensorMap mw, mx;
     if (!tc_make_map(&mw, w, N, K, TC_BM) || !make_map_b16(&mx, x, M, K, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B))
@@ -577,7 +771,7 @@ static int w8a16_tc(const void *x, const void *w, const float *s, const void *bi
     A.t.sw_rows = 1;
     A.t.bias = bias;
     A.t.out = out;
-    A.t.slots = (uint4 *)scratch;
+    A.t.slots = (uint4 *)slots;
     A.t.timeout_ns = pipe_timeout_ns();
     A.t.status = status;
     A.ldo = ldo;
@@ -597,11 +791,13 @@ static int w8a16_rows(const void *x, const void *w, const void *s, const void *b
 
 static int w8a16_dispatch(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N,
                           int K, int ldo, int dtype, cudaStream_t st) {
-    void *scratch;
+    void *scratch, *limbs = nullptr;
     unsigned *status;
-    if (int rc = ws_acquire(wh_slot_bytes(M), st, &scratch, &status)) return rc;
-    if (dtype == 0) return w8a16_tc<__half>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
-    return w8a16_tc<__nv_bfloat16>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
+    if (int rc = ws_acquire(wh_slots_bytes(M), st, &scratch, &status)) return rc;
+    if (M <= WL_MAX_M && w8a16_limbs())
+        if (int rc = aux_acquire(wl_limb_bytes(K) + 256, st, &limbs)) return rc;
+    if (dtype == 0) return w8a16_tc<__half>(x, w, (const float *)s, bias, out, M, N, K, ldo, status, limbs, scratch, st);
+    return w8a16_tc<__nv_bfloat16>(x, w, (const float *)s, bias, out, M, N, K, ldo, status, limbs, scratch, st);
 }
 
 }  // namespace vt
@@ -640,23 +836,24 @@ int w8a16_mma(const void *x, const void *w, const void *s, const void *bias, voi
     return w8a16_dispatch(x, w, s, bias, out, M, N, K, N, 0, (cudaStream_t)stream);
 }
 
-// Zeroed workspace bytes vt_w8a16_mm needs for M token rows (256-byte status header included).
-size_t vt_w8a16_ws_bytes(int M) { return 256 + wh_slot_bytes(M < 1 ? 1 : M); }
+// Zeroed workspace bytes vt_w8a16_mm needs for M token rows and K (256-byte status header included).
+size_t vt_w8a16_ws_bytes(int M, int K) { return wh_ws_bytes(M < 1 ? 1 : M, K < 16 ? 16 : K); }
 
 // W8A16 for M 1..64 in either dtype, with an output row stride ldo (>= N: e.g. this rank's columns of a gathered
-// [M, world * N] logits buffer) and a caller-owned workspace of vt_w8a16_ws_bytes(M) bytes, zeroed once before its
-// first use (the kernel leaves it zeroed); calls sharing a workspace must be stream-ordered. The first 256 bytes hold
-// the status word.
+// [M, world * N] logits buffer) and a caller-owned workspace of vt_w8a16_ws_bytes(M, K) bytes, zeroed once before its
+// first use (the kernels leave its split-K slots zeroed); calls sharing a workspace must be stream-ordered. The first
+// 256 bytes hold the status word.
 int vt_w8a16_mm(const void *x, const void *w, const void *s, const void *bias, void *out, int M, int N, int K, int ldo,
                 int dtype, void *workspace, size_t ws_bytes, void *stream) {
-    if (!wh_args_ok(x, w, s, out, M, N, K, ldo) || !workspace || ws_bytes < vt_w8a16_ws_bytes(M) ||
+    if (!wh_args_ok(x, w, s, out, M, N, K, ldo) || !workspace || ws_bytes < vt_w8a16_ws_bytes(M, K) ||
         ((uintptr_t)workspace & 255))
         return VT_EARG;
     cudaStream_t st = (cudaStream_t)stream;
     unsigned *status = (unsigned *)workspace;
-    void *scratch = (char *)workspace + 256;
-    if (dtype == 0) return w8a16_tc<__half>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
-    return w8a16_tc<__nv_bfloat16>(x, w, (const float *)s, bias, out, M, N, K, ldo, scratch, status, st);
+    char *limbs = (char *)workspace + 256, *slots = limbs + wl_limb_bytes(K) + 256;
+    if (dtype == 0)
+        return w8a16_tc<__half>(x, w, (const float *)s, bias, out, M, N, K, ldo, status, limbs, slots, st);
+    return w8a16_tc<__nv_bfloat16>(x, w, (const float *)s, bias, out, M, N, K, ldo, status, limbs, slots, st);
 }
 
 }  // extern "C"

@@ -36,17 +36,17 @@ def _code(dt):
     raise TypeError(f"vllm_turing_b200: W8A16 needs fp16 / bf16 activations, got {dt}")
 
 
-def workspace(device):
-    """The per-device zeroed workspace of vt_w8a16_mm for up to 64 rows (allocated on first use, which must come
-    before any graph capture; the kernel leaves it zeroed)."""
+def workspace(device, K):
+    """The per-device zeroed workspace of vt_w8a16_mm for up to 64 rows of K (allocated on first use, which must come
+    before any graph capture; the kernels leave its split-K slots zeroed)."""
     d = torch.device(device)
     idx = d.index if d.index is not None else torch.cuda.current_device()
-    ws = _ws.get(idx)
+    ws = _ws.get((idx, K))
     if ws is None:
         if torch.cuda.is_current_stream_capturing():
             raise RuntimeError("vllm_turing_b200: W8A16 workspace must be allocated before graph capture")
-        ws = torch.zeros(int(lib().vt_w8a16_ws_bytes(64)), dtype=torch.uint8, device=torch.device("cuda", idx))
-        _ws[idx] = ws
+        ws = torch.zeros(int(lib().vt_w8a16_ws_bytes(64, K)), dtype=torch.uint8, device=torch.device("cuda", idx))
+        _ws[(idx, K)] = ws
     return ws
 
 
@@ -69,7 +69,7 @@ def mm_into(out, x, w, s, bias=None, ldo=None):
     M, K = x.shape
     N = w.shape[0]
     ldo = N if ldo is None else int(ldo)
-    ws = workspace(x.device)
+    ws = workspace(x.device, K)
     rc = lib().vt_w8a16_mm(x.data_ptr(), w.data_ptr(), s.data_ptr(), bias.data_ptr() if bias is not None else None,
                            out.data_ptr(), M, N, K, ldo, _code(x.dtype), ws.data_ptr(), ws.numel(),
                            torch.cuda.current_stream().cuda_stream)
