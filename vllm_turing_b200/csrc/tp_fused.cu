@@ -8,17 +8,22 @@
 //                                                                     vllm_turing/tailoverlap.py:200; arithmetic of
 //                                                                     tests/test_quantfuse.py:45-48, quantfuse.py:18-24)
 //
-// The reference runs these as three or more kernels (GEMV, LL all-reduce, compiled norm + quant); here:
+// The reference runs these as three or more kernels (GEMV, LL all-reduce, compiled norm + quant); here one kernel:
 //  1. GEMM phase, one of
 //     - tcgen05 (default, tc_core.cuh): weights as the MMA's A operand, stream-K over the SMs; the CTA that completes
-//       a 128-feature tile dequantises it and pushes it as LL words straight into every rank's receive slot,
-//     - dp4a GEMV (VLLM_TURING_FUSED_GEMV=1, M <= 16; gemv_core.cuh): the CTA that finishes a 32-feature row-block
-//       does the same push.
+//       a 128-feature tile finishes it,
+//     - dp4a GEMV (VLLM_TURING_FUSED_GEMV=1, M <= 16; gemv_core.cuh): the CTA that finishes a 32-feature row-block.
+//  2. The tail, one of
+//     - tile owners (default with tcgen05, N <= 8192): the CTA that finished a tile exchanges its partial with the
+//       same CTA on every peer (LL words over NVLink), sums the ranks in order, adds the residual and publishes the
+//       tile's RMSNorm statistics; two mailbox rounds over all tiles then give every owner the row's 1 / rms and absmax
+//       for its features (see "tile-owner tail" below),
+//     - row CTAs (VLLM_TURING_DECODE_TAIL=rows, and the GEMV phase): the finisher pushes its values as LL words into
+//       every rank's receive slot; token row m is owned by E CTAs (CTA index m * E + g), each for a contiguous 1/E of
+//       the row's columns, which poll the LL words of all ranks, sum them in rank order, add the residual, and combine
+//       the sum of squares and then the absmax across the E CTAs through a seq-tagged 8-byte mailbox word per CTA
+//       (combined in CTA order: identical on every rank, no atomics).
 //     Either way: NVLink stores of the finished values, no staging buffer, no flag round trip.
-//  2. Epilogue phase: token row m is owned by E CTAs (CTA index m * E + g), each for a contiguous 1/E of the row's
-//     columns. Each polls the LL words of all ranks for its columns, sums them in rank order, adds the residual and
-//     writes it back; the sum of squares and then the absmax of the normalised row are combined across the E CTAs
-//     through a seq-tagged 8-byte mailbox word per CTA (combined in CTA order: identical on every rank, no atomics).
 // With world = 1 (no tensor parallelism) the same kernel is the TP1 "fused epilogue without collective".
 // All waits are bounded; timeouts land in the communicator's status word.
 #include <cuda_bf16.h>
