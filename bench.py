@@ -1241,7 +1241,8 @@ def main():
            "down": bytes_dn_w + M * K_dn + 4 * M + 4 * HIDDEN + M * HIDDEN * (2 + 2 + 1) + 4 * M + 2 * HIDDEN}
     names = {"gate_up": "tc_gemm_kernel (gate_up, tcgen05 decode)", "silu": "silu_mul_quant_kernel",
              "gate_up_silu": "gate_up_silu_kernel (gate_up + SiLU*up + int8 quant, tcgen05 decode)",
-             "down": "tp_row_linear_tc_kernel (down + all-reduce + RMSNorm + quant)"}
+             "down": ("tp_row_linear_tc_kernel" if os.environ.get("VLLM_TURING_DECODE_TAIL") == "rows" else
+                      "tp_row_linear_tt_kernel") + " (down + all-reduce + RMSNorm + quant)"}
     dom = max(t_k, key=t_k.get)
     hbm, peak_kind = peaks()
     achieved = alg[dom] / t_k[dom] / 1e9

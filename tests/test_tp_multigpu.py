@@ -57,9 +57,12 @@ def _ref_abi_two_ranks(L, rank, dev, check):
         return p.value, qp.value
 
     # har: LL words pushed into the peer's region, the peer's polled in the own one
-    slot_words = 32768
+    slot_words = 65536   # data words per slot: the largest message below is 24 x 5120 values = 61440 words
     local, remote = shared_region(2 * slot_words * 8)
     counters = torch.zeros(L.har_blocks(slot_words), dtype=torch.int32, device=dev)
+    # a message beyond the slot is refused before any launch (host_ar.cu:115-117 returns -1 the same way)
+    check(L.har_all_reduce(None, None, slot_words + 1, 1, remote, local, counters.data_ptr(), slot_words, s) == -1,
+          "har_all_reduce accepted a message larger than its slot")
     for i, n in enumerate((5 * 5120, 24 * 5120, 2 * 777, 5 * 5120)):
         xs = [(torch.randn(n, generator=torch.Generator().manual_seed(60 + 2 * i + r)) * 3).to(torch.bfloat16)
               for r in range(2)]
