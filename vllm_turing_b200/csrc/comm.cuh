@@ -6,7 +6,8 @@
 //   [0, CTRL)            control: seq (u32 @0, the last completed call), done ticket (u32 @64), status (u32 @128),
 //                        group mailbox (u64 [32 rows][16 groups][2] @4096), split-K tickets of the fused
 //                        GEMM (int [4096] @16384: GEMV row-blocks or tcgen05 tiles), tile mailbox of the fused
-//                        decode tail (u64 [2 kinds][64 tiles][32 rows] @32768)
+//                        decode tail (@65536: 16-byte statistics words [64 tiles][32 rows], then 8-byte absmax
+//                        words [64 tiles][32 rows])
 //   LL                   LL receive slots [parity 2][src rank][ll_slot bytes]: peers push 16-byte LL words here
 //   SCRATCH              int32 split-K partial sums of the fused GEMV [ll rows][N] (local use only)
 //   RS                   two-shot reduce-scatter receive buffers [parity 2][src rank][chunk_cap bytes]
@@ -32,13 +33,13 @@ namespace vt {
 
 constexpr int COMM_MAX_RANKS = 8;
 constexpr int COMM_MAX_CTAS = 256;
-constexpr size_t COMM_CTRL = 65536;
+constexpr size_t COMM_CTRL = 131072;
 constexpr size_t COMM_MBOX_OFF = 4096;
 constexpr size_t COMM_TICKET_OFF = 16384;
 constexpr int COMM_TICKETS = 4096;
 constexpr int COMM_MBOX_ROWS = 32, COMM_MBOX_GROUPS = 16;
 constexpr int PF_MAX_TILES = 4096, PF_MAX_CTAS = 1024;
-constexpr size_t COMM_TMBOX_OFF = 32768;   // tile mailbox: [kind 2][COMM_TMBOX_TILES][COMM_MBOX_ROWS] u64, to 65536
+constexpr size_t COMM_TMBOX_OFF = 65536;   // tile mailbox: 32 KB of statistics words, 16 KB of absmax words
 constexpr int COMM_TMBOX_TILES = 64;
 
 struct CommLayout {
@@ -78,11 +79,15 @@ struct CommView {
     __device__ __forceinline__ unsigned long long *mbox() const {
         return reinterpret_cast<unsigned long long *>(local() + COMM_MBOX_OFF);
     }
-    // fused decode tail: seq-tagged word of 128-feature tile `tile`, token row m (kind 0: sum of squares of the new
-    // residual over the tile's features, kind 1: absmax of the normalised values)
-    __device__ __forceinline__ unsigned long long *tmbox(int kind, int tile, int m) const {
-        return reinterpret_cast<unsigned long long *>(local() + COMM_TMBOX_OFF) +
-               ((size_t)kind * COMM_TMBOX_TILES + tile) * COMM_MBOX_ROWS + m;
+    // fused decode tail, 128-feature tile `tile`, token row m: the tile's statistics as one 16-byte LL word (sum of
+    // squares of the new residual; the |residual|, |norm weight| pair of its largest product and a near-tie flag), and
+    // its absmax of the normalised values as a seq-tagged 8-byte word
+    __device__ __forceinline__ uint4 *tm_stat(int tile, int m) const {
+        return reinterpret_cast<uint4 *>(local() + COMM_TMBOX_OFF) + (size_t)tile * COMM_MBOX_ROWS + m;
+    }
+    __device__ __forceinline__ unsigned long long *tm_amax(int tile, int m) const {
+        return reinterpret_cast<unsigned long long *>(local() + COMM_TMBOX_OFF + 32768) +
+               (size_t)tile * COMM_MBOX_ROWS + m;
     }
     __device__ __forceinline__ int *tickets() const { return reinterpret_cast<int *>(local() + COMM_TICKET_OFF); }
     __device__ __forceinline__ int *scratch() const { return reinterpret_cast<int *>(local() + L.scratch_off); }

@@ -54,6 +54,7 @@ struct FusedArgs {
     float *scales;
     T *reduced;
     uint64_t pipe_timeout, peer_timeout;
+    int tt_two_rounds;   // tile-owner tail: always take the absmax through the second mailbox round
 };
 
 template <typename T>
@@ -401,14 +402,29 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 //     quantise. The owner of tile 0 writes the scales and publishes the call number.
 // Per call after the weight stream: split-K collection, [the NVLink exchange], two mailbox rounds -- with the work of
 // each round spread over the tile owners.
+// Products |h w| within this factor of a row's largest are near-ties: a normalised value of such a product may round
+// above the largest one's (two fp32 roundings, 2^-24 each, then the 16-bit rounding); farther ones cannot.
+constexpr float TT_NEAR = 1.0f - 1.0f / 524288.0f;   // 1 - 2^-19, exact in fp32
+
+template <typename T> __device__ __forceinline__ unsigned short t2bits(float x) {
+    const T v = f2t<T>(x);
+    return *reinterpret_cast<const unsigned short *>(&v);
+}
+template <typename T> __device__ __forceinline__ float bits2f(uint32_t b) {
+    const unsigned short u = (unsigned short)b;
+    return t2f<T>(*reinterpret_cast<const T *>(&u));
+}
+
 template <typename T, int BN>
 struct TcTileTailEpi {
-    // shared floats: [0, 32) token scales, [32, 160) per-warp partials [4][32], [160, 192) per-row 1 / rms,
-    // [192, 224) per-row absmax, [224, 226) ints: owned-tile count, the owned tile
-    static constexpr int kSmemFloats = 256;
-    __device__ __forceinline__ static int *owned_of(float *smp) { return reinterpret_cast<int *>(smp + 224); }
+    // shared floats: [0, 32) token scales, [32, 160) per-warp sums of squares [4][32], [160, 416) per-warp largest
+    // products as 64-bit keys [4][32], [416, 544) per-warp near-tie counts [4][32], [544, 576) the |h|, |w| pair of
+    // each row's largest product, [576, 608) per-row 1 / rms, [608, 640) per-row absmax, [640, 672) per-row flags,
+    // [672, 674) ints: owned-tile count, the owned tile
+    static constexpr int kSmemFloats = 704;
+    __device__ __forceinline__ static int *owned_of(float *smp) { return reinterpret_cast<int *>(smp + 672); }
     struct Prep {
-        float swn;
+        float swn, wn;
         float res[BN];
     };
     const FusedArgs<T> *F;
@@ -437,6 +453,7 @@ struct TcTileTailEpi {
         Prep r;
         const bool ok = n < N;
         r.swn = ok ? F->sw[n] : 0.0f;
+        r.wn = (ok && F->residual) ? t2f<T>(F->norm_w[n]) : 0.0f;
         const T *res = F->residual;
 #pragma unroll
         for (int m = 0; m < BN; ++m) r.res[m] = (res && ok && m < M) ? t2f<T>(res[(size_t)m * N + n]) : 0.0f;
@@ -467,35 +484,33 @@ struct TcTileTailEpi {
             }
             const uint64_t deadline = globaltimer() + F->peer_timeout;
             bool dead = false;
-            // eight token rows (two words per peer) per round, every peer's words in flight together
+            // eight token rows (two words per peer) at a time; a poll round re-loads every peer's words and tests all
+            // tags (a tight loop), so the exchange ends one round trip after the last word lands
 #pragma unroll
             for (int i0 = 0; i0 < BN / 4; i0 += 2) {
                 if (i0 >= nq) break;
                 uint4 v[COMM_MAX_RANKS][2];
+                const bool two = i0 + 1 < nq;
+                uint32_t it = 0;
+                while (nok && !dead) {
 #pragma unroll
-                for (int r = 0; r < COMM_MAX_RANKS; ++r) {
-                    if (r >= nw || r == rk || !nok) continue;
-                    const char *src = F->c.ll_slot(rk, par, r) + (size_t)n * 16;
+                    for (int r = 0; r < COMM_MAX_RANKS; ++r) {
+                        if (r >= nw || r == rk) continue;
+                        const char *src = F->c.ll_slot(rk, par, r) + ((size_t)i0 * Nr + n) * 16;
+                        v[r][0] = ld_volatile16(src);
+                        if (two) v[r][1] = ld_volatile16(src + (size_t)Nr * 16);
+                    }
+                    bool ready = true;
 #pragma unroll
-                    for (int j = 0; j < 2; ++j)
-                        if (i0 + j < nq) v[r][j] = ld_volatile16(src + (size_t)(i0 + j) * Nr * 16);
-                }
-#pragma unroll
-                for (int r = 0; r < COMM_MAX_RANKS; ++r) {
-                    if (r >= nw || r == rk || !nok) continue;
-                    const char *src = F->c.ll_slot(rk, par, r) + (size_t)n * 16;
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        if (i0 + j >= nq) continue;
-                        uint32_t it = 0;
-                        while (!dead && (v[r][j].y != sq || v[r][j].w != sq)) {
-                            if ((++it & 255u) == 0 && globaltimer() > deadline) {
-                                report(F->c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)r);
-                                dead = true;
-                                break;
-                            }
-                            v[r][j] = ld_volatile16(src + (size_t)(i0 + j) * Nr * 16);
-                        }
+                    for (int r = 0; r < COMM_MAX_RANKS; ++r) {
+                        if (r >= nw || r == rk) continue;
+                        ready = ready && v[r][0].y == sq && v[r][0].w == sq;
+                        if (two) ready = ready && v[r][1].y == sq && v[r][1].w == sq;
+                    }
+                    if (ready) break;
+                    if ((++it & 255u) == 0 && globaltimer() > deadline) {
+                        report(F->c.status(), ST_PEER_TIMEOUT | 0x500u | (unsigned)(rk == 0 ? 1 : 0));
+                        dead = true;
                     }
                 }
                 // rank-ordered float sum, own partial from registers (rank 0's value first, as the oracle)
@@ -530,23 +545,59 @@ struct TcTileTailEpi {
         }
         T *const res = F->residual;
         if (!res) return;
+        // The tile's statistics per token row, published in one 16-byte LL word: the sum of squares of the new
+        // residual h over the tile's features, and for the absmax of the normalised row y = rnd(rnd(h * rs) * w):
+        // the |h|, |w| pair of the largest product |h w| (exact in fp32; the smallest feature index among equal ones)
+        // and a flag when a second feature's product lies within 2^-19 of it. |y| grows with |h w| except for
+        // products that close, so every owner can derive the row's absmax exactly from these pairs; a flagged
+        // candidate sends the call through a second mailbox round instead.
         const int t = threadIdx.x - TC_EPI_LEAD, q = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
         float *part = sm + 32;
+        unsigned long long *pkey = reinterpret_cast<unsigned long long *>(sm + 160);
+        int *pcnt = reinterpret_cast<int *>(sm + 416);
+        uint32_t *phw = reinterpret_cast<uint32_t *>(sm + 544);
+        const float aw = fabsf(pr.wn);
 #pragma unroll
         for (int m = 0; m < BN; ++m) {
             if (m >= Mr) break;   // uniform
             const float h = rnd<T>(rnd<T>(s[m]) + pr.res[m]);
+            s[m] = h;
             if (nok) res[(size_t)m * Nr + n] = f2t<T>(h);
             float x = nok ? h * h : 0.0f;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-            if (lane == 0) part[q * 32 + m] = x;
+            const float pm = nok ? fabsf(h) * aw : 0.0f;
+            unsigned long long key = ((unsigned long long)__float_as_uint(pm) << 32) | (0xffffffffu - (unsigned)n);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                key = k2 > key ? k2 : key;
+            }
+            if (lane == 0) {
+                part[q * 32 + m] = x;
+                pkey[q * 32 + m] = key;
+            }
+        }
+        named_sync(TC_EPI_BAR, 128);
+#pragma unroll
+        for (int m = 0; m < BN; ++m) {
+            if (m >= Mr) break;
+            unsigned long long k = pkey[m];
+#pragma unroll
+            for (int j = 1; j < 4; ++j) k = pkey[j * 32 + m] > k ? pkey[j * 32 + m] : k;
+            const float pmax = __uint_as_float((unsigned)(k >> 32));
+            const float pm = nok ? fabsf(s[m]) * aw : 0.0f;
+            if (nok && (unsigned)n == 0xffffffffu - (unsigned)k)
+                phw[m] = (uint32_t)t2bits<T>(fabsf(s[m])) | ((uint32_t)t2bits<T>(aw) << 16);
+            const unsigned close = __ballot_sync(0xffffffffu, nok && pm >= pmax * TT_NEAR);
+            if (lane == 0) pcnt[q * 32 + m] = __popc(close);
         }
         named_sync(TC_EPI_BAR, 128);
         const int ta = n >> 7;
         if (t < Mr) {
             const float x = ((part[t] + part[32 + t]) + part[64 + t]) + part[96 + t];
-            st_volatile8(F->c.tmbox(0, ta, t), ((unsigned long long)sq << 32) | __float_as_uint(x));
+            const int cnt = pcnt[t] + pcnt[32 + t] + pcnt[64 + t] + pcnt[96 + t];
+            ll_store(F->c.tm_stat(ta, t), __float_as_uint(x), phw[t] | (cnt >= 2 ? 0x80000000u : 0u), sq);
         }
         if (t == 0) {   // at most one tile per CTA (the launch checks it)
             int *o = owned();
@@ -556,24 +607,76 @@ struct TcTileTailEpi {
     }
 };
 
-// Gathers kind `kind` of every tile's mailbox word for the M token rows into buf[m * 64 + tile] (all threads of the
-// CTA; the words of all tiles and rows are in flight together, one poll round).
-__device__ __forceinline__ void tt_gather(const CommView &c, int kind, int T, int M, unsigned seq, float *buf,
-                                          uint64_t deadline) {
-    for (int j = threadIdx.x; j < T * M; j += blockDim.x) {
-        const int m = j / T, tile = j - m * T;
-        const unsigned long long *p = c.tmbox(kind, tile, m);
-        unsigned long long x = ld_volatile8(p);
-        uint32_t it = 0;
-        while ((unsigned)(x >> 32) != seq) {
-            if ((++it & 63u) == 0 && globaltimer() > deadline) {
-                report(c.status(), ST_GROUP_TIMEOUT | 0x700u | (unsigned)kind);
-                break;
-            }
-            x = ld_volatile8(p);
-        }
-        buf[m * COMM_TMBOX_TILES + tile] = __uint_as_float((unsigned)x);
+// Gathers every tile's statistics word for the M token rows: sums of squares into bss[m * 64 + tile], the pair words
+// into bhw (all threads of the CTA). A poll round re-loads all of a thread's words and tests their tags (a tight loop),
+// so the gather ends one round trip after the last word lands; the words are stored once all have arrived.
+constexpr int TT_GMAX = (COMM_TMBOX_TILES * COMM_MBOX_ROWS + TC_THREADS - 1) / TC_THREADS;
+__device__ __forceinline__ void tt_gather_stats(const CommView &c, int NT, int M, unsigned seq, float *bss,
+                                                uint32_t *bhw, uint64_t deadline) {
+    const int total = NT * M;
+    const uint4 *ptr[TT_GMAX];
+    int dst[TT_GMAX];
+#pragma unroll
+    for (int i = 0; i < TT_GMAX; ++i) {
+        const int j = threadIdx.x + i * TC_THREADS, m = j / NT, tile = j - m * NT;
+        ptr[i] = j < total ? c.tm_stat(tile, m) : nullptr;
+        dst[i] = m * COMM_TMBOX_TILES + tile;
     }
+    uint4 v[TT_GMAX];
+    uint32_t it = 0;
+    while (true) {
+#pragma unroll
+        for (int i = 0; i < TT_GMAX; ++i)
+            if (ptr[i]) v[i] = ld_volatile16(ptr[i]);
+        bool ready = true;
+#pragma unroll
+        for (int i = 0; i < TT_GMAX; ++i)
+            if (ptr[i]) ready = ready && v[i].y == seq && v[i].w == seq;
+        if (ready) break;
+        if ((++it & 63u) == 0 && globaltimer() > deadline) {
+            report(c.status(), ST_GROUP_TIMEOUT | 0x700u);
+            break;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < TT_GMAX; ++i) {
+        if (!ptr[i]) continue;
+        bss[dst[i]] = __uint_as_float(v[i].x);
+        bhw[dst[i]] = v[i].z;
+    }
+}
+
+// The same for the absmax words of the second round (buf[m * 64 + tile]).
+__device__ __forceinline__ void tt_gather_amax(const CommView &c, int NT, int M, unsigned seq, float *buf,
+                                               uint64_t deadline) {
+    const int total = NT * M;
+    const unsigned long long *ptr[TT_GMAX];
+    int dst[TT_GMAX];
+#pragma unroll
+    for (int i = 0; i < TT_GMAX; ++i) {
+        const int j = threadIdx.x + i * TC_THREADS, m = j / NT, tile = j - m * NT;
+        ptr[i] = j < total ? c.tm_amax(tile, m) : nullptr;
+        dst[i] = m * COMM_TMBOX_TILES + tile;
+    }
+    unsigned long long v[TT_GMAX];
+    uint32_t it = 0;
+    while (true) {
+#pragma unroll
+        for (int i = 0; i < TT_GMAX; ++i)
+            if (ptr[i]) v[i] = ld_volatile8(ptr[i]);
+        bool ready = true;
+#pragma unroll
+        for (int i = 0; i < TT_GMAX; ++i)
+            if (ptr[i]) ready = ready && (unsigned)(v[i] >> 32) == seq;
+        if (ready) break;
+        if ((++it & 63u) == 0 && globaltimer() > deadline) {
+            report(c.status(), ST_GROUP_TIMEOUT | 0x701u);
+            break;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < TT_GMAX; ++i)
+        if (ptr[i]) buf[dst[i]] = __uint_as_float((unsigned)v[i]);
 }
 
 // Phase 2 of the tile-owner tail: every thread of the CTA calls it after the GEMM phase (residual mode). The launch
@@ -594,52 +697,98 @@ __device__ __forceinline__ void tile_tail_post(const FusedArgs<T> &P, unsigned s
     const int n = ta * TC_BM + q * 32 + lane;
     const bool nok = epi && n < N;
     T *const res = P.residual;
-    float *part = sm + 32, *rs = sm + 160, *amax = sm + 192;
+    float *part = sm + 32, *rs = sm + 576, *amax = sm + 608;
+    int *fb = reinterpret_cast<int *>(sm + 640);
+    float *bss = buf;
+    uint32_t *bhw = reinterpret_cast<uint32_t *>(buf + COMM_MBOX_ROWS * COMM_TMBOX_TILES);
+    float *bam = buf + 2 * COMM_MBOX_ROWS * COMM_TMBOX_TILES;
     const uint64_t deadline = globaltimer() + P.peer_timeout;
-    // the new residual and the norm weight: loads in flight during the first gather
+    // the new residual and the norm weight: loads in flight during the gather
     float y[BN];
 #pragma unroll
     for (int m = 0; m < BN; ++m) y[m] = (nok && m < M) ? t2f<T>(res[(size_t)m * N + n]) : 0.0f;
     const float wn = nok ? t2f<T>(P.norm_w[n]) : 0.0f;
-    tt_gather(c, 0, NT, M, seq, buf, deadline);
+    tt_gather_stats(c, NT, M, seq, bss, bhw, deadline);
     __syncthreads();
-    for (int m = warp; m < M; m += nwarps) {   // sum of squares over the tiles, tile order fixed
-        float x = lane < NT ? buf[m * COMM_TMBOX_TILES + lane] : 0.0f;
-        if (lane + 32 < NT) x += buf[m * COMM_TMBOX_TILES + lane + 32];
+    // per token row (one warp each): 1 / rms from the sums of squares folded in tile order, and the absmax from the
+    // candidate pairs -- exact unless a candidate is flagged (then fb[m] = 1 and the second round decides)
+    for (int m = warp; m < M; m += nwarps) {
+        const float *ss = bss + m * COMM_TMBOX_TILES;
+        const uint32_t *hw = bhw + m * COMM_TMBOX_TILES;
+        float x = lane < NT ? ss[lane] : 0.0f;
+        if (lane + 32 < NT) x += ss[lane + 32];
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-        if (lane == 0) rs[m] = __frsqrt_rn(__fdiv_rn(x, (float)N) + P.eps);
+        const float r = __frsqrt_rn(__fdiv_rn(x, (float)N) + P.eps);
+        float hh[2], ww[2], pp[2];
+        bool fl[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const int tile = lane + 32 * k;
+            const uint32_t u = tile < NT ? hw[tile] : 0u;
+            hh[k] = bits2f<T>(u & 0xffffu);
+            ww[k] = bits2f<T>((u >> 16) & 0x7fffu);
+            fl[k] = (u >> 31) != 0;
+            pp[k] = tile < NT ? hh[k] * ww[k] : -1.0f;
+        }
+        float pmx = fmaxf(pp[0], pp[1]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) pmx = fmaxf(pmx, __shfl_xor_sync(0xffffffffu, pmx, o));
+        float a = 0.0f;
+        bool flagged = false;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            if (pp[k] >= pmx * TT_NEAR) {
+                a = fmaxf(a, rnd<T>(__fmul_rn(__fmul_rn(hh[k], r), ww[k])));
+                flagged |= fl[k];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+        flagged = __any_sync(0xffffffffu, flagged);
+        if (lane == 0) {
+            rs[m] = r;
+            amax[m] = a;
+            fb[m] = flagged ? 1 : 0;
+        }
     }
     __syncthreads();
     // Every tile was finished, so every CTA of the grid has read this call's number: publish it for the next call.
     if (tid == 0 && ta == 0) *reinterpret_cast<volatile unsigned *>(c.seq_ptr()) = seq;
-    if (epi) {   // normalise; the tile's absmax per token row
+    bool second = P.tt_two_rounds != 0;   // uniform: every CTA decides from the same gathered words
+    for (int m = 0; m < M; ++m) second |= fb[m] != 0;
 #pragma unroll
-        for (int m = 0; m < BN; ++m) {
-            if (m >= M) break;
-            y[m] = nok ? rnd<T>(__fmul_rn(__fmul_rn(y[m], rs[m]), wn)) : 0.0f;
-            float a = fabsf(y[m]);
+    for (int m = 0; m < BN; ++m) {
+        if (m >= M) break;
+        y[m] = nok ? rnd<T>(__fmul_rn(__fmul_rn(y[m], rs[m]), wn)) : 0.0f;
+    }
+    if (second) {   // the tile's absmax per row, one more mailbox round over all tiles
+        if (epi) {
 #pragma unroll
-            for (int k = 16; k > 0; k >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, k));
-            if (lane == 0) part[q * 32 + m] = a;
+            for (int m = 0; m < BN; ++m) {
+                if (m >= M) break;
+                float a = fabsf(y[m]);
+#pragma unroll
+                for (int k = 16; k > 0; k >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, k));
+                if (lane == 0) part[q * 32 + m] = a;
+            }
         }
-    }
-    __syncthreads();
-    if (epi && t < M) {
-        const float a = fmaxf(fmaxf(part[t], part[32 + t]), fmaxf(part[64 + t], part[96 + t]));
-        st_volatile8(c.tmbox(1, ta, t), ((unsigned long long)seq << 32) | __float_as_uint(a));
-    }
-    tt_gather(c, 1, NT, M, seq, buf + COMM_MBOX_ROWS * COMM_TMBOX_TILES, deadline);
-    __syncthreads();
-    buf += COMM_MBOX_ROWS * COMM_TMBOX_TILES;
-    for (int m = warp; m < M; m += nwarps) {   // max: the same in any order
-        float a = lane < NT ? buf[m * COMM_TMBOX_TILES + lane] : 0.0f;
-        if (lane + 32 < NT) a = fmaxf(a, buf[m * COMM_TMBOX_TILES + lane + 32]);
+        __syncthreads();
+        if (epi && t < M) {
+            const float a = fmaxf(fmaxf(part[t], part[32 + t]), fmaxf(part[64 + t], part[96 + t]));
+            st_volatile8(c.tm_amax(ta, t), ((unsigned long long)seq << 32) | __float_as_uint(a));
+        }
+        tt_gather_amax(c, NT, M, seq, bam, deadline);
+        __syncthreads();
+        for (int m = warp; m < M; m += nwarps) {   // max: the same in any order
+            float a = lane < NT ? bam[m * COMM_TMBOX_TILES + lane] : 0.0f;
+            if (lane + 32 < NT) a = fmaxf(a, bam[m * COMM_TMBOX_TILES + lane + 32]);
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-        if (lane == 0) amax[m] = a;
+            for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+            if (lane == 0) amax[m] = a;
+        }
+        __syncthreads();
     }
-    __syncthreads();
     if (ta == 0 && tid < M) P.scales[tid] = __fdiv_rn(amax[tid], 127.0f);
     if (!nok) return;
     int8_t *const qo = P.q;
@@ -667,6 +816,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tile_tail_post<T, BN>(P, seq, sm, reinterpret_cast<float *>(ring));   // the stage ring is free now
     else
         comm_end(P.c, seq);
+}
+
+// VLLM_TURING_TT_ROUNDS=2 makes the tile-owner tail take every row's absmax through the second mailbox round (the
+// path a near-tie takes; tests compare both).
+static int tt_two_rounds() {
+    static int v = -1;
+    if (v < 0) {
+        const char *e = getenv("VLLM_TURING_TT_ROUNDS");
+        v = (e && atoi(e) == 2) ? 1 : 0;
+    }
+    return v;
 }
 
 // VLLM_TURING_DECODE_TAIL=rows selects the row-CTA epilogue (tp_row_linear_tc_kernel) instead of the tile owners.
@@ -725,8 +885,9 @@ static int launch_fused_tt(FusedArgs<T> P, cudaStream_t s) {
     int g = num_sms(dev);
     if (g > G.units) g = G.units;
     if (tc_decode_slot_bytes(P.M, g) > P.c.L.scratch_bytes) return VT_EARG;
-    // the post phase's two gather buffers ([32][64] floats each) in the stage ring
-    if ((size_t)2 * COMM_MBOX_ROWS * COMM_TMBOX_TILES * 4 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
+    P.tt_two_rounds = tt_two_rounds();
+    // the post phase's three gather buffers ([32][64] words each) in the stage ring
+    if ((size_t)3 * COMM_MBOX_ROWS * COMM_TMBOX_TILES * 4 > (size_t)stages * TcLayout<BN, KBS>::STAGE) return VT_EARG;
     return launch_k(tp_row_linear_tt_kernel<T, BN, KBS>, dim3(g), dim3(TC_THREADS), smem, s, true, mw, ma, G, P);
 }
 
