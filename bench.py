@@ -52,7 +52,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--tokens", type=int, default=None, help="tokens per step (decode default 5, prefill 8192)")
-    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce", "lmhead", "p2p", "gemv"],
+    ap.add_argument("--mode", default="decode", choices=["decode", "prefill", "allreduce", "lmhead", "p2p", "gemv",
+                                                         "stack"],
                     help="decode: the 64-layer MLP stack (the headline, config 1/2); prefill: the row-parallel layer "
                          "tail at config 3 (down GEMM -> two-shot all-reduce -> residual add + RMSNorm + int8 quant); "
                          "allreduce: config 4's size sweep, 1 KB .. 256 MB, against NCCL on the same ranks")
@@ -997,6 +998,201 @@ def run_p2p(args, world, rank, local, dev, gloo):
     dist.destroy_process_group()
 
 
+QKV, HEADS_OUT = 14336, 6144   # the attention's input projection (q with its gate, k, v) and o_proj's K (24 x 256)
+
+
+def run_stack(args, world, rank, local, dev, gloo):
+    """a synthetic 64-layer W8A8 stack at N ranks through the public API, then the int8 LM head.
+    Per layer (random-init weights of these shapes, each layer its own, so every step streams them from HBM):
+      1. QKV, column-parallel: vllm_turing::scaled_mm_ 5120 -> 14336 / N, its output all-gathered along the last
+         dimension (dmaag.all_gather_dim, the dmaag all-gather) -- the gathered output config 4 names;
+      2. attention is out of scope: its stand-in output is this rank's first 6144 / N QKV columns, quantised per token
+         (the scaled_int8_quant replacement);
+      3. o_proj, row-parallel: TPComm.row_linear 6144 / N -> 5120 fused with the all-reduce, residual add, RMSNorm and
+         int8 quant (decode: the one-kernel tail; prefill: the GEMM with the reduce-scatter in its epilogue + tail);
+      4. gate_up 5120 -> 34816 / N + silu_mul_quant, down 17408 / N -> 5120 fused like o_proj; its int8 output is the
+         next layer's input.
+    Then the LM head (W8A16 on this rank's 151936 / N rows, the logits all-gathered): on all M rows at decode, on the
+    last token at prefill (the sampled position). The step is captured once as a CUDA graph and replayed; value is the
+    whole-job int8 TOPS of the layers (2 M (14336 + 6144 + 34816 + 17408) 5120 ops per layer)."""
+    import torch
+    import torch.distributed as dist
+
+    from vllm_turing_b200 import _build, dmaag, lmhead, w8a8  # noqa: F401  (w8a8 registers scaled_mm_)
+    from vllm_turing_b200.comm import TPComm
+    from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant, scaled_int8_quant_cuda
+    from vllm_turing_b200.synthetic import make_layer_inputs, quant_per_token
+    from vllm_turing_b200.tailoverlap import silu_mul_quant
+
+    _build.load()
+    M = args.tokens
+    NL = args.layers
+    for full in (QKV, HEADS_OUT, 2 * INTER, INTER, VOCAB):
+        assert full % world == 0, f"{full} does not split over {world} ranks"
+    n_qkv, k_o, n_gu, k_dn, vs = QKV // world, HEADS_OUT // world, 2 * INTER // world, INTER // world, VOCAB // world
+    prefill = M > 32
+    m_head = 1 if prefill else M
+    # a few generated weight sets; every layer gets its own device copy of one of them
+    base = []
+    for i in range(min(NL, 2)):
+        qkv = make_layer_inputs(1, n_qkv, HIDDEN, seed=500 + i, rank=rank, with_norm=False)
+        o = make_layer_inputs(1, HIDDEN, k_o, seed=600 + i, rank=rank)
+        gu = make_layer_inputs(1, n_gu, HIDDEN, seed=700 + i, rank=rank, with_norm=False)
+        dn = make_layer_inputs(1, HIDDEN, k_dn, seed=800 + i, rank=rank)
+        base.append(dict(qkv_w=qkv.w.to(dev), qkv_sw=qkv.sw.to(dev).view(-1, 1), o_w=o.w.to(dev),
+                         o_sw=o.sw.to(dev).view(-1, 1), gu_w=gu.w.to(dev), gu_sw=gu.sw.to(dev).view(-1, 1),
+                         dn_w=dn.w.to(dev), dn_sw=dn.sw.to(dev).view(-1, 1)))
+        if i == 0:
+            norm_w = dn.norm_w.to(dev)
+            g = torch.Generator().manual_seed(9)
+            residual0 = torch.randn(M, HIDDEN, generator=g).to(torch.bfloat16).to(dev)
+        del qkv, o, gu, dn
+    layers = [{k: v.clone() for k, v in base[i % len(base)].items()} for i in range(NL)]
+    del base
+    gh = torch.Generator().manual_seed(10 + rank)
+    head_w = torch.randint(-127, 128, (vs, HIDDEN), generator=gh, dtype=torch.int8).to(dev)
+    head_s = (torch.rand(vs, generator=gh) * 1e-3 + 1e-4).to(dev)
+    x0, xs0 = quant_per_token(torch.randn(M, HIDDEN, generator=torch.Generator().manual_seed(7)).to(torch.bfloat16))
+    x_q, x_s = x0.to(dev), xs0.view(M, 1).to(dev)
+    residual = residual0.clone()
+    qkv_out = torch.empty(M, n_qkv, dtype=torch.bfloat16, device=dev)
+    out_gu = torch.empty(M, n_gu, dtype=torch.bfloat16, device=dev)
+    h_q = torch.empty(M, k_dn, dtype=torch.int8, device=dev)
+    h_s = torch.empty(M, 1, dtype=torch.float32, device=dev)
+    logits = torch.empty(m_head, VOCAB, dtype=torch.bfloat16, device=dev)
+    comm = TPComm(gloo, dev, big_bytes=max(2 * M * HIDDEN, 64 << 20),
+                  ll_bytes=max(512 << 10, m_head * VOCAB * 2 // world))
+    w8a8.workspace(dev, M, max(n_qkv, n_gu))
+    lmhead.workspace(dev, HIDDEN)
+    stream = torch.cuda.current_stream()
+
+    def layer(s):
+        torch.ops.vllm_turing.scaled_mm_(qkv_out, x_q, s["qkv_w"].t(), x_s, s["qkv_sw"], None)
+        if world > 1:
+            dmaag.all_gather_dim(comm, qkv_out, -1)   # column-parallel output, gathered (config 4)
+        a_q, a_s = scaled_int8_quant_cuda(qkv_out[:, :k_o])   # the attention output's stand-in
+        comm.row_linear(a_q, s["o_w"], a_s, s["o_sw"], residual=residual, norm_w=norm_w, eps=1e-6, q=x_q, scales=x_s)
+        torch.ops.vllm_turing.scaled_mm_(out_gu, x_q, s["gu_w"].t(), x_s, s["gu_sw"], None)
+        silu_mul_quant(out_gu, h_q, h_s)
+        comm.row_linear(h_q, s["dn_w"], h_s, s["dn_sw"], residual=residual, norm_w=norm_w, eps=1e-6, q=x_q, scales=x_s)
+
+    def head():
+        lmhead.logits_gathered(residual[M - m_head:], head_w, head_s, comm=comm if world > 1 else None, out=logits)
+
+    def step():
+        for s in layers:
+            layer(s)
+        head()
+
+    def barrier():
+        torch.cuda.synchronize()
+        dist.barrier(group=gloo)
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    def timed(fn, n):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        a.record(stream)
+        for _ in range(n):
+            fn()
+        b.record(stream)
+        barrier()
+        return max_over_ranks(a.elapsed_time(b) / n) / 1e3
+
+    K_steps, W = args.steps, max(args.warmup, 3)
+    step()   # eager warm-up: kernel attributes, workspaces
+    barrier()
+    comm.check()
+    # parity self-check (untimed) on layer 0's o_proj tail: the fused call and the unfused chain from the same inputs
+    from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant  # noqa: F811
+    s0 = layers[0]
+    a_q, a_s = scaled_int8_quant_cuda(qkv_out[:, :k_o].contiguous())
+    partial = torch.empty(M, HIDDEN, dtype=torch.bfloat16, device=dev)
+    torch.ops.vllm_turing.scaled_mm_(partial, a_q, s0["o_w"].t(), a_s, s0["o_sw"], None)
+    fz = dict(residual=residual.clone(), residual0=residual.clone(), norm_w=norm_w, eps=1e-6,
+              reduced=torch.empty(M, HIDDEN, dtype=torch.bfloat16, device=dev),
+              q=torch.empty(M, HIDDEN, dtype=torch.int8, device=dev))
+    comm.row_linear(a_q, s0["o_w"], a_s, s0["o_sw"], residual=fz["residual"], norm_w=norm_w, eps=1e-6, q=fz["q"],
+                    scales=torch.empty(M, 1, dtype=torch.float32, device=dev), reduced=fz["reduced"])
+    chk = dict(reduced=comm.all_reduce(partial.clone()), residual=residual.clone())
+    chk["q"], _ = rms_norm_dynamic_per_token_quant(chk["reduced"], norm_w, 1e-6, chk["residual"])
+    barrier()
+    comm.check()
+    parity = tail_parity(world, gloo, partial, fz, chk)
+    del a_q, a_s, partial, fz, chk
+
+    g_step = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_step):
+        step()
+    g_head = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_head):
+        head()
+    for _ in range(W):
+        g_step.replay()
+    barrier()
+    comm.check()
+    with ClockSampler(local) as clk:
+        t_step = timed(g_step.replay, K_steps)
+        t_head = timed(g_head.replay, max(K_steps, 10))
+    comm.check()
+    # the logits agree on every rank (each holds the gathered [m_head, 151936])
+    lb = logits.view(torch.int16).to(torch.int32)
+    l0 = lb.clone()
+    if world > 1:
+        dist.broadcast(l0, src=0)
+    parity["logits_ranks_identical"] = bool(torch.equal(l0, lb))
+
+    e2e = None
+    if not args.no_e2e:
+        h_x, h_xs = x0.pin_memory(), xs0.view(M, 1).pin_memory()
+        h_l = torch.empty(m_head, VOCAB, dtype=torch.bfloat16).pin_memory()
+
+        def e2e_step():
+            x_q.copy_(h_x, non_blocking=True)
+            x_s.copy_(h_xs, non_blocking=True)
+            g_step.replay()
+            h_l.copy_(logits, non_blocking=True)
+
+        for _ in range(2):
+            e2e_step()
+        t_e2e = timed(e2e_step, K_steps)
+        e2e = {"value": NL * 2.0 * M * HIDDEN * (QKV + HEADS_OUT + 2 * INTER + INTER) / (t_e2e - t_head) / 1e12
+               if t_e2e > t_head else None, "unit": "TOPS (layers only)", "step_ms": t_e2e * 1e3,
+               "h2d_bytes_per_step": int(h_x.numel() + h_xs.numel() * 4),
+               "d2h_bytes_per_step": int(h_l.numel() * 2),
+               "api": "the captured step (scaled_mm_, all_gather_dim, scaled_int8_quant, TPComm.row_linear, "
+                      "silu_mul_quant, lmhead.logits_gathered); pinned host input copied in, logits read back"}
+    ops_layer = 2.0 * M * HIDDEN * (QKV + HEADS_OUT + 2 * INTER + INTER)
+    t_layers = t_step - t_head
+    line = {
+        "metric": "config-4 64-layer W8A8 TP stack: whole-job int8 TOPS of the layers, us per layer, LM head us",
+        "value": NL * ops_layer / t_layers / 1e12, "unit": "TOPS", "n_gpus": world, "steps": K_steps, "warmup": W,
+        "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic", "mode": "stack",
+        "us_per_layer": t_layers / NL * 1e6, "lmhead_us": t_head * 1e6,
+        "tokens_per_s": M / t_step,
+        "config": {"workload": f"BASELINE config 4: {NL} layers of QKV 5120->14336 (column-parallel, all-gathered), "
+                               f"o_proj 6144->5120 and down 17408->5120 (row-parallel, fused all-reduce + residual + "
+                               f"RMSNorm + int8 quant), gate_up 5120->34816 + SiLU*up + quant; int8 LM head "
+                               f"5120->151936 on {m_head} row(s), logits all-gathered; M={M}",
+                   "tokens": M, "layers": NL, "tp": world, "head_rows": m_head,
+                   "l2": f"inputs larger than L2: {NL} layers with their own weights",
+                   "launch": "CUDA graph of the step, replayed K times", "parallelism": f"tp{world}"},
+        "clocks": clk.summary(), "e2e": e2e, "cpu_baseline": None, "parity": parity,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    del g_step, g_head
+    comm.close()
+    dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -1020,6 +1216,8 @@ def main():
         return run_p2p(args, world, rank, local, dev, gloo)
     if args.mode == "gemv":
         return run_gemv(args, world, rank, local, dev, gloo)
+    if args.mode == "stack":
+        return run_stack(args, world, rank, local, dev, gloo)
     _build.load()
     M = args.tokens
     NL = args.layers
