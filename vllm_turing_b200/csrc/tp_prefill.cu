@@ -16,10 +16,11 @@
 //     a peer, HBM for itself) and then releases a per-tile flag there. The reduce-scatter's traffic thus leaves tile by
 //     tile while the tensor cores work on the next tiles; no partial is ever written to this rank's own memory first.
 //  2. tp_prefill_tail_kernel: phase A -- for each owned row, once every source's tiles of its 128-row block are flagged,
-//     sum the sources' partials in rank order (identical bits on every rank), publish the reduced row in this rank's AG
-//     buffer and run the residual add + RMSNorm + quant on it while it is in registers. Phase B -- pull the peers'
-//     reduced rows over NVLink (each CTA waits for the one peer flag of the CTA that produced them) and run the same
-//     row epilogue on them. Each row is handled by one group of N / 8 / VPT threads with the register-resident
+//     sum the sources' partials in rank order (identical bits on every rank), push the reduced row into every peer's
+//     receive buffer (NVLink stores, in flight while the CTA goes on) and run the residual add + RMSNorm + quant on it
+//     while it is in registers. Phase B -- once the peers' same CTA flagged its pushed rows, read them locally and run
+//     the same row epilogue on them. (Pulling the peers' rows in phase B instead put a load latency over NVLink on
+//     the critical path of every row.) Each row is handled by one group of N / 8 / VPT threads with the register-resident
 //     arithmetic of vt_rms_norm_quant (same VPT, same summation order), so the outputs equal the unfused chain's bits.
 //
 // NVLink bytes per rank: (world - 1) / world x 2 M N out in (1) and in (2), the two-shot's bus traffic, of which (1)'s
@@ -330,10 +331,10 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1) tp_prefill_tail_kernel(con
         for (int k = 0; k < VPT; ++k)
             ov[k] = make_uint4(pack2<T>(x[8 * k], x[8 * k + 1]), pack2<T>(x[8 * k + 2], x[8 * k + 3]),
                                pack2<T>(x[8 * k + 4], x[8 * k + 5]), pack2<T>(x[8 * k + 6], x[8 * k + 7]));
-        if (W > 1) {
-            uint4 *ag = reinterpret_cast<uint4 *>(c.ag_buf(me, p) + (size_t)lr * rowb);
+        for (int k2 = 1; k2 < W; ++k2) {   // push the reduced row into every peer's receive buffer (NVLink stores)
+            uint4 *agr = reinterpret_cast<uint4 *>(c.agr_buf((me + k2) % W, p, me) + (size_t)lr * rowb);
 #pragma unroll
-            for (int k = 0; k < VPT; ++k) ag[t + k * tpr] = ov[k];
+            for (int k = 0; k < VPT; ++k) agr[t + k * tpr] = ov[k];
         }
         if (A.reduced) {
 #pragma unroll
@@ -348,19 +349,20 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1) tp_prefill_tail_kernel(con
         }
     }
 
-    // ---- phase B: the peers' rows, pulled from their AG buffers ----
+    // ---- phase B: the peers' rows, pushed into this rank's receive buffer by their owners ----
     if (W > 1) {
-        __threadfence_system();
+        __threadfence_system();   // the pushes of this CTA's rows are performed before their flags
         __syncthreads();
-        if (threadIdx.x == 0) st_release_sys(c.pf_ag_flag(me, p, blockIdx.x), seq);
+        if ((int)threadIdx.x < W && (int)threadIdx.x != me)
+            st_release_sys(c.pf_ag_flag(threadIdx.x, p, me, blockIdx.x), seq);
         for (int k = 1; k < W; ++k) {
             const int src = (me + k) % W;
-            if (threadIdx.x == 0 && !dead && !flag_wait(c.pf_ag_flag(src, p, blockIdx.x), seq, deadline)) {
+            if (threadIdx.x == 0 && !dead && !flag_wait(c.pf_ag_flag(me, p, src, blockIdx.x), seq, deadline)) {
                 report(c.status(), ST_PEER_TIMEOUT | 0xc00u | (unsigned)src);
                 dead = true;
             }
             __syncthreads();
-            const uint4 *agp = reinterpret_cast<const uint4 *>(c.ag_buf(src, p));
+            const uint4 *agp = reinterpret_cast<const uint4 *>(c.agr_buf(me, p, src));
             for (int lr = lr0; lr < lr1; ++lr) {
                 const size_t gr = (size_t)src * R + lr;
                 uint4 rv[VPT], v[VPT];
@@ -504,10 +506,10 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1)
         for (int j = 0; j < VPT; ++j)
             ov[j] = make_uint4(pack2<T>(x[8 * j], x[8 * j + 1]), pack2<T>(x[8 * j + 2], x[8 * j + 3]),
                                pack2<T>(x[8 * j + 4], x[8 * j + 5]), pack2<T>(x[8 * j + 6], x[8 * j + 7]));
-        if (W > 1) {
-            uint4 *ag = reinterpret_cast<uint4 *>(c.ag_buf(me, p) + (size_t)lr * rowb);
+        for (int k2 = 1; k2 < W; ++k2) {   // push the reduced row into every peer's receive buffer (NVLink stores)
+            uint4 *agr = reinterpret_cast<uint4 *>(c.agr_buf((me + k2) % W, p, me) + (size_t)lr * rowb);
 #pragma unroll
-            for (int j = 0; j < VPT; ++j) ag[t + j * tpr] = ov[j];
+            for (int j = 0; j < VPT; ++j) agr[t + j * tpr] = ov[j];
         }
         if (A.reduced) {
 #pragma unroll
@@ -529,11 +531,12 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1)
         }
     }
 
-    // ---- phase B ----
+    // ---- phase B: the peers' rows, pushed into this rank's receive buffer by their owners (local reads) ----
     if (W > 1) {
-        __threadfence_system();
+        __threadfence_system();   // the pushes of this CTA's rows are performed before their flags
         __syncthreads();
-        if (threadIdx.x == 0) st_release_sys(c.pf_ag_flag(me, p, blockIdx.x), seq);
+        if ((int)threadIdx.x < W && (int)threadIdx.x != me)
+            st_release_sys(c.pf_ag_flag(threadIdx.x, p, me, blockIdx.x), seq);
         const int per_row_b = A.residual ? 2 : 1;
         const int rows = lr1 - lr0;
         const int items_b = (W - 1) * rows * per_row_b;
@@ -542,16 +545,16 @@ __global__ void __launch_bounds__(PF_TAIL_THREADS, 1)
         auto src_b = [&](int i) -> const void * {
             const int k = 1 + i / (rows * per_row_b), r = (i / per_row_b) % rows, e = i % per_row_b;
             const int srk = (me + k) % W;
-            if (e == 0) return c.ag_buf(srk, p) + (size_t)(lr0 + r) * rowb;
+            if (e == 0) return c.agr_buf(me, p, srk) + (size_t)(lr0 + r) * rowb;
             return A.residual + ((size_t)srk * R + lr0 + r) * N;
         };
         int ib = 0;   // items of phase B issued (by the group's first thread); the ring continues from phase A
         auto issue_b = [&]() {
-            // a peer's first item: its CTA blockIdx.x must have published its reduced rows
+            // a peer's first item: its CTA blockIdx.x must have pushed its reduced rows here
             const int k = 1 + ib / (rows * per_row_b);
             if (ib % (rows * per_row_b) == 0) {
                 const int srk = (me + k) % W;
-                if (!dead && !flag_wait(c.pf_ag_flag(srk, p, blockIdx.x), seq, deadline)) {
+                if (!dead && !flag_wait(c.pf_ag_flag(me, p, srk, blockIdx.x), seq, deadline)) {
                     report(c.status(), ST_PEER_TIMEOUT | 0xc00u | (unsigned)srk);
                     dead = true;
                 }
