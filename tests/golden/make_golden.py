@@ -18,6 +18,9 @@ exact formulas the reference's tests compute where the reference is CUDA:
              the reference's large-M path (lmhead.py:104-110: dequantise to the activation dtype, matmul), run on CPU
   convert    the reference's scripts/w8a8_convert.py itself (run on the CPU) on a tiny seeded bf16 checkpoint, W8A8,
              --w8a16 64 and --mixed: every stored tensor and the quantization_config
+  smooth     the same script with --smooth (SmoothQuant folding) on a tiny seeded checkpoint of one attention layer,
+             one GDN layer and the MTP layer, with seeded calibration maxima in the two-rank files its calibration run
+             writes, at alpha 0.5 and 0.8 (tests/golden/golden_smooth.npz; --smooth-only writes just that file)
   config 0   the whole chain at BASELINE config 0 (M=16, K_local=8704, N=5120, 2 ranks, seed 0): digests of the
              exact parts plus the int8 / scales arrays
 Inputs come from seeded torch CPU generators (vllm_turing_b200.synthetic for config 0) and are stored (small cases)
@@ -73,6 +76,79 @@ CKPT_SHARDS = {
 }
 CKPT_MODES = {"w8a8": [], "w8a16": ["--w8a16", "64"], "mixed": ["--mixed"]}
 
+# a tiny checkpoint for SmoothQuant folding: an attention layer (q with its gate, GQA), a GDN layer and the MTP layer,
+# with the norms and producers the folding touches; dims of the config's text_config
+SMOOTH_CFG = {"hidden_size": 64, "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 16,
+              "linear_num_value_heads": 4, "linear_value_head_dim": 16}
+
+
+def _smooth_tensors():
+    H, I = 64, 96
+    t = {}
+    for pre in ("model.language_model.layers.0.", "mtp.layers.0."):
+        t.update({pre + "input_layernorm.weight": (H,), pre + "post_attention_layernorm.weight": (H,),
+                  pre + "self_attn.q_proj.weight": (128, H), pre + "self_attn.k_proj.weight": (32, H),
+                  pre + "self_attn.v_proj.weight": (32, H), pre + "self_attn.o_proj.weight": (H, 64),
+                  pre + "mlp.gate_proj.weight": (I, H), pre + "mlp.up_proj.weight": (I, H),
+                  pre + "mlp.down_proj.weight": (H, I)})
+    pre = "model.language_model.layers.1."
+    t.update({pre + "input_layernorm.weight": (H,), pre + "post_attention_layernorm.weight": (H,),
+              pre + "linear_attn.in_proj_qkv.weight": (160, H), pre + "linear_attn.in_proj_z.weight": (64, H),
+              pre + "linear_attn.in_proj_a.weight": (4, H), pre + "linear_attn.in_proj_b.weight": (4, H),
+              pre + "linear_attn.out_proj.weight": (H, 64), pre + "linear_attn.norm.weight": (16,),
+              pre + "mlp.gate_proj.weight": (I, H), pre + "mlp.up_proj.weight": (I, H),
+              pre + "mlp.down_proj.weight": (H, I), "lm_head.weight": (50, H)})
+    names = sorted(t)
+    half = len(names) // 2
+    return {"model-00001-of-00002.safetensors": {n: t[n] for n in names[:half]},
+            "model-00002-of-00002.safetensors": {n: t[n] for n in names[half:]}}
+
+
+SMOOTH_SHARDS = _smooth_tensors()
+SMOOTH_ALPHAS = (0.5, 0.8)
+
+
+def smooth_checkpoint(path, calib):
+    """Writes the seeded bf16 checkpoint for the SmoothQuant case into `path` and the calibration maxima into `calib`
+    (rank{0,1}.pt for the text layers, rank{0,1}_m1.pt for the MTP layer, keyed by vLLM's fused module names;
+    row-parallel inputs as each rank's K-shard)."""
+    import json as _json
+    from safetensors.torch import save_file
+    os.makedirs(path, exist_ok=True)
+    os.makedirs(calib, exist_ok=True)
+    g = torch.Generator().manual_seed(78)
+    wmap = {}
+    for shard, tensors in SMOOTH_SHARDS.items():
+        out = {}
+        for name, shape in tensors.items():
+            if len(shape) == 1:   # norm weights: zero-centred (Qwen's 1 + w) or plain
+                t = (torch.randn(*shape, generator=g) * 0.1).to(torch.bfloat16)
+            else:
+                t = (torch.randn(*shape, generator=g) * 0.05).to(torch.bfloat16)
+                t[:, 3] *= 8                     # an input channel with large weights
+            out[name] = t
+            wmap[name] = shard
+        save_file(out, os.path.join(path, shard), metadata={"format": "pt"})
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        _json.dump({"metadata": {"total_size": 0}, "weight_map": wmap}, f)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        _json.dump({"architectures": ["Qwen3_5ForConditionalGeneration"], "text_config": dict(SMOOTH_CFG)}, f)
+    keys = {"language_model.model.layers.0.self_attn.qkv_proj": 64, "language_model.model.layers.0.self_attn.o_proj": 32,
+            "language_model.model.layers.0.mlp.gate_up_proj": 64, "language_model.model.layers.0.mlp.down_proj": 48,
+            "language_model.model.layers.1.linear_attn.in_proj_qkvz": 64,
+            "language_model.model.layers.1.linear_attn.out_proj": 32,
+            "language_model.model.layers.1.mlp.gate_up_proj": 64, "language_model.model.layers.1.mlp.down_proj": 48}
+    keys_m1 = {"model.layers.0.self_attn.qkv_proj": 64, "model.layers.0.self_attn.o_proj": 32,
+               "model.layers.0.mlp.gate_up_proj": 64, "model.layers.0.mlp.down_proj": 48}
+    for tag, ks in (("", keys), ("_m1", keys_m1)):
+        for r in (0, 1):
+            d = {}
+            for k, n in ks.items():
+                x = torch.randn(n, generator=g).abs() * 2 + 1e-6
+                x[min(7, n - 1)] *= 40            # an activation outlier channel
+                d[k] = x
+            torch.save(d, os.path.join(calib, f"rank{r}{tag}.pt"))
+
 
 def tiny_checkpoint(path):
     """Writes the synthetic bf16 checkpoint (seeded) into `path`."""
@@ -103,7 +179,10 @@ def main():
     ap.add_argument("--ref", default=os.environ.get("VLLM_TURING_REFERENCE")
                     or os.path.join(os.path.dirname(REPO), "reference"))
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
+    ap.add_argument("--smooth-only", action="store_true", help="write only golden_smooth.npz")
     args = ap.parse_args()
+    if args.smooth_only:
+        return smooth_golden(args.ref, os.path.join(HERE, "golden_smooth.npz"))
     sys.path.insert(0, args.ref)
     from vllm_turing.quantfuse import quant_torch  # the reference's own quantiser
     sys.path.insert(0, REPO)
@@ -234,6 +313,29 @@ def main():
 
     np.savez_compressed(args.out, **out)
     print(f"wrote {args.out}: {len(out)} arrays, {os.path.getsize(args.out) / 1024:.0f} KiB")
+    smooth_golden(args.ref, os.path.join(HERE, "golden_smooth.npz"))
+
+
+def smooth_golden(ref, path):
+    """The reference's scripts/w8a8_convert.py --smooth on the SmoothQuant checkpoint (CPU): every stored tensor."""
+    import subprocess
+    import tempfile
+    from safetensors import safe_open
+    out = {}
+    with tempfile.TemporaryDirectory() as tmp:
+        src, calib = os.path.join(tmp, "src"), os.path.join(tmp, "calib")
+        smooth_checkpoint(src, calib)
+        for alpha in SMOOTH_ALPHAS:
+            dst = os.path.join(tmp, f"a{alpha}")
+            subprocess.run([sys.executable, os.path.join(ref, "scripts", "w8a8_convert.py"), src, dst, "cpu",
+                            "--smooth", calib, "--alpha", str(alpha)], check=True, capture_output=True)
+            for shard in SMOOTH_SHARDS:
+                with safe_open(os.path.join(dst, shard), framework="pt") as f:
+                    for name in f.keys():
+                        t = f.get_tensor(name)
+                        out[f"sm{alpha}_{name}"] = bits(t) if t.dtype == torch.bfloat16 else t.numpy()
+    np.savez_compressed(path, **out)
+    print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1024:.0f} KiB")
 
 
 if __name__ == "__main__":
