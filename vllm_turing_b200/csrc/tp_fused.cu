@@ -839,6 +839,17 @@ static bool decode_tail_rows() {
     return v != 0;
 }
 
+// Grid of the tile-owner kernel: one CTA per SM; with few K blocks per tile (a tensor-parallel rank's share of
+// K, nkb <= 34), two CTAs per tile instead: every tile then has one contributor, whose split-K hand-off is cheaper
+// than collecting three or four, while the weight stream per CTA stays short. Measured with a per-CTA timer, M = 5:
+// K = 2176 12.5 -> 11.8 us, K = 4352 14.7 -> 13.9 us; at K = 17408 one CTA per SM stays faster (24.6 vs 25.1 us: a
+// CTA streams at most ~60 GB/s with its ring in flight, so 80 CTAs cannot carry 89 MB as fast as 148).
+inline long long tt_grid(int dev, int NT, int nkb) {
+    const long long units = (long long)NT * nkb, sms = num_sms(dev);
+    if (nkb <= 34 && nkb >= 2 && 2LL * NT <= sms) return 2LL * NT;
+    return sms < units ? sms : units;
+}
+
 // The tile-owner tail's limits: N / 128 tiles in the mailbox, each peer's LL words ((M + 3) / 4 x 16 bytes per
 // feature) in one LL slot, and at most one tile owned per CTA: every CTA's stream-K range (ceil(units / grid) K
 // blocks) shorter than a tile's K blocks, or a single unit.
@@ -847,8 +858,7 @@ inline bool tile_tail_fits(const CommView &c, int M, int N, int K) {
     if (NT > COMM_TMBOX_TILES) return false;
     const int dev = cur_device();
     if (dev < 0) return false;
-    long long units = (long long)NT * nkb, g = num_sms(dev);
-    if (g > units) g = units;
+    const long long units = (long long)NT * nkb, g = tt_grid(dev, NT, nkb);
     const long long L = (units + g - 1) / g;
     if (!(L < nkb || L == 1)) return false;
     return c.world == 1 || (size_t)((M + 3) / 4) * 16 * (size_t)N <= c.L.ll_slot;
@@ -882,8 +892,7 @@ static int launch_fused_tt(FusedArgs<T> P, cudaStream_t s) {
             return (int)cudaGetLastError();
         attr_set[dev] = true;
     }
-    int g = num_sms(dev);
-    if (g > G.units) g = G.units;
+    const int g = (int)tt_grid(dev, G.n_tiles_a, G.nkb);
     if (tc_decode_slot_bytes(P.M, g) > P.c.L.scratch_bytes) return VT_EARG;
     P.tt_two_rounds = tt_two_rounds();
     // the post phase's three gather buffers ([32][64] words each) in the stage ring
