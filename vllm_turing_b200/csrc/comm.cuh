@@ -11,9 +11,9 @@
 //   LL                   LL receive slots [parity 2][src rank][ll_slot bytes]: peers push 16-byte LL words here
 //   SCRATCH              int32 split-K partial sums of the fused GEMV [ll rows][N] (local use only)
 //   RS                   two-shot reduce-scatter receive buffers [parity 2][src rank][chunk_cap bytes]
-//   AG                   two-shot reduced own chunk [parity 2][chunk_cap bytes] (pulled by peers)
-//   AGR                  fused prefill: peers' reduced rows, pushed by their owners [parity 2][src rank][chunk_cap]
-//   FLAGS                u32 flags [parity 2][kind 2][src rank][256 CTAs] (kind 0: RS data landed, 1: AG chunk ready)
+//   AGR                  all-gather receive buffers of the two-shot and the fused prefill tail: the peers' reduced
+//                        chunks / rows, pushed by their owners [parity 2][src rank][chunk_cap] (world > 1)
+//   FLAGS                u32 flags [parity 2][kind 2][src rank][256 CTAs] (kind 0: RS data landed, 1: reduced chunk pushed)
 //   PF                   fused prefill row-linear: tile flags [parity 2][src rank][PF_MAX_TILES] (a source's GEMM
 //                        tile of this rank's rows landed in RS) and reduced-rows flags [parity 2][src rank][PF_MAX_CTAS]
 //                        (CTA j of rank src pushed its reduced rows into this rank's AGR buffer)
@@ -45,7 +45,7 @@ constexpr int COMM_TMBOX_TILES = 64;
 
 struct CommLayout {
     size_t ll_slot;       // bytes of one LL slot (= 2 x the data bytes it carries)
-    size_t ll_off, scratch_off, scratch_bytes, rs_off, ag_off, agr_off, flags_off, pf_off, total;
+    size_t ll_off, scratch_off, scratch_bytes, rs_off, agr_off, flags_off, pf_off, total;
     size_t chunk_cap;     // two-shot: bytes of one rank's chunk per call
 };
 
@@ -61,8 +61,7 @@ __host__ __device__ inline CommLayout comm_layout(int world, size_t ll_data, siz
     L.scratch_bytes = comm_align(scratch_ints * 4);
     L.chunk_cap = comm_align((big_data + world - 1) / world);
     L.rs_off = L.scratch_off + L.scratch_bytes;
-    L.ag_off = L.rs_off + 2 * (size_t)world * L.chunk_cap;
-    L.agr_off = L.ag_off + 2 * L.chunk_cap;
+    L.agr_off = L.rs_off + 2 * (size_t)world * L.chunk_cap;
     L.flags_off = L.agr_off + (world > 1 ? 2 * (size_t)world * L.chunk_cap : 0);
     L.pf_off = L.flags_off + comm_align(2 * 2 * (size_t)COMM_MAX_RANKS * COMM_MAX_CTAS * 4);
     L.total = L.pf_off + comm_align(2 * (size_t)COMM_MAX_RANKS * PF_MAX_TILES * 4 +
@@ -101,9 +100,6 @@ struct CommView {
     __device__ __forceinline__ char *rs_buf(int dst, unsigned p, int src) const {
         return base[dst] + L.rs_off + ((size_t)p * world + src) * L.chunk_cap;
     }
-    __device__ __forceinline__ char *ag_buf(int owner, unsigned p) const {
-        return base[owner] + L.ag_off + (size_t)p * L.chunk_cap;
-    }
     __device__ __forceinline__ unsigned *flag(int dst, unsigned p, int kind, int src, int cta) const {
         return reinterpret_cast<unsigned *>(base[dst] + L.flags_off) +
                (((size_t)p * 2 + kind) * COMM_MAX_RANKS + src) * COMM_MAX_CTAS + cta;
@@ -113,7 +109,7 @@ struct CommView {
         return reinterpret_cast<unsigned *>(base[dst] + L.pf_off) + ((size_t)p * COMM_MAX_RANKS + src) * PF_MAX_TILES +
                tile;
     }
-    // fused prefill: rank `src`'s reduced rows in rank `dst`'s receive buffer (pushed by src)
+    // two-shot and fused prefill: rank `src`'s reduced chunk / rows in rank `dst`'s receive buffer (pushed by src)
     __device__ __forceinline__ char *agr_buf(int dst, unsigned p, int src) const {
         return base[dst] + L.agr_off + ((size_t)p * world + src) * L.chunk_cap;
     }

@@ -6,9 +6,11 @@
 //     rounding). The reference's two-rank LL kernel (vllm_turing/csrc/host_ar.cu:31-82) generalised to N ranks with
 //     16-byte stores and bounded waits.
 //   two-shot (prefill messages): reduce-scatter by chunk ownership (rank c owns chunk c; peers push their slice of it
-//     into c's receive buffers, then a release flag), the owner sums in rank order and publishes the reduced chunk,
-//     every rank pulls the other chunks (all-gather). The N-rank SM version of the reference's copy-engine all-reduce
-//     (vllm_turing/csrc/ce_ar.cu:103-146: push half, flag, wait, add, push, flag, wait).
+//     into c's receive buffers, then a release flag), the owner sums in rank order and pushes the reduced chunk into
+//     every peer's all-gather receive buffer as it goes (NVLink stores in flight with the reduction), then a flag;
+//     every rank copies the peers' reduced chunks out locally. The N-rank SM version of the reference's copy-engine
+//     all-reduce (vllm_turing/csrc/ce_ar.cu:103-146: push half, flag, wait, add, push, flag, wait). (Pulling the
+//     reduced chunks after the reduction instead put an NVLink load latency on every unit of the all-gather.)
 //   all-gather: each rank's slot of `gathered` is pre-written by the caller and the kernel fills the peers' slots
 //     (the ABI idea of vllm_turing/csrc/dma_ag.cu:41-47, over P2P for N ranks instead of host staging for two).
 //
@@ -128,7 +130,6 @@ __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, cons
     __syncthreads();
     (void)ok;
     slice_of(U, W, R, G, j, cs, b, e);
-    uint4 *ag = reinterpret_cast<uint4 *>(c.ag_buf(R, p));
     const int nt = blockDim.x;
     for (long long u0 = b + tid; u0 < e; u0 += 2LL * nt) {   // two units per step: 2 x world loads in flight
         uint4 v[2][COMM_MAX_RANKS];
@@ -151,20 +152,25 @@ __global__ void __launch_bounds__(AR_THREADS) ar_twoshot_kernel(CommView c, cons
             const uint4 o = make_uint4(pack2<T>(s[0], s[1]), pack2<T>(s[2], s[3]), pack2<T>(s[4], s[5]),
                                        pack2<T>(s[6], s[7]));
             out[u] = o;
-            ag[u - cs] = o;
+#pragma unroll
+            for (int k2 = 1; k2 < COMM_MAX_RANKS; ++k2) {   // push the reduced slice into every peer (NVLink stores)
+                if (k2 >= W) break;
+                int dst = R + k2;
+                if (dst >= W) dst -= W;
+                reinterpret_cast<uint4 *>(c.agr_buf(dst, p, R))[u - cs] = o;
+            }
         }
     }
     __syncthreads();
     if (tid < W && tid != R) st_release_sys(c.flag(tid, p, 1, R, j), seq);
-    // 3. pull every peer's reduced slice j
+    // 3. every peer pushed its reduced slice j into this rank's receive buffer: copy it out (local reads)
     if (tid < W && tid != R && !flag_wait(c.flag(R, p, 1, tid, j), seq, deadline))
         report(c.status(), ST_PEER_TIMEOUT | 0x200u | (unsigned)tid);
     __syncthreads();
     for (int k = 1; k < W; ++k) {
         const int src = (R + k) % W;
         slice_of(U, W, src, G, j, cs, b, e);
-        // out[cs + i] = the peer's reduced slice, read over NVLink
-        copy_units(out + cs, 0, reinterpret_cast<const uint4 *>(c.ag_buf(src, p)), b - cs, e - cs);
+        copy_units(out + cs, 0, reinterpret_cast<const uint4 *>(c.agr_buf(R, p, src)), b - cs, e - cs);
     }
     comm_end(c, seq);
 }
@@ -236,7 +242,7 @@ __global__ void __launch_bounds__(AR_THREADS) ag_bulk_kernel(CommView c, char *_
     comm_end(c, seq);
 }
 
-// NVLink bandwidth probe: this rank's AG buffer -> a peer's RS buffer (the slot of this rank), 16-byte stores with
+// NVLink bandwidth probe: one of this rank's RS buffers -> a peer's RS buffer (the slot of this rank), 16-byte stores with
 // TS_UNROLL loads in flight per thread over a grid-stride loop. Touches no flags and no call number.
 __global__ void __launch_bounds__(AR_THREADS) peer_push_kernel(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
                                                                long long U) {
@@ -453,8 +459,8 @@ int vt_all_gather(void *comm, void *gathered, long long m, void *stream) {
     return 0;
 }
 
-// NVLink bandwidth probe (bench.py --mode p2p): copies `bytes` (% 16 == 0, <= the two-shot chunk capacity) from this
-// rank's AG buffer into rank `peer`'s RS buffer, with SM stores (engine 0: grid of `ctas` CTAs, 0 = 4 per SM) or the
+// NVLink bandwidth probe (bench.py --mode p2p): copies `bytes` (% 16 == 0, <= the two-shot chunk capacity) from one
+// of this rank's RS buffers (parity 1) into one of rank `peer`'s (parity 0), with SM stores (engine 0: grid of `ctas` CTAs, 0 = 4 per SM) or the
 // copy engines (engine 1: cudaMemcpyAsync to the IPC-mapped peer address). Not a collective: the caller brackets it
 // with barriers and runs no other call on the communicator meanwhile. The copied bytes are meaningless.
 int vt_comm_peer_copy(void *comm, int peer, long long bytes, int engine, int ctas, void *stream) {
@@ -462,7 +468,7 @@ int vt_comm_peer_copy(void *comm, int peer, long long bytes, int engine, int cta
     if (!c || peer < 0 || peer >= c->v.world || bytes <= 0 || (bytes & 15) ||
         bytes > (long long)c->v.L.chunk_cap)
         return VT_EARG;
-    const char *src = c->v.base[c->v.rank] + c->v.L.ag_off;
+    const char *src = c->v.base[c->v.rank] + c->v.L.rs_off + ((size_t)c->v.world + c->v.rank) * c->v.L.chunk_cap;
     char *dst = c->v.base[peer] + c->v.L.rs_off + (size_t)c->v.rank * c->v.L.chunk_cap;
     cudaStream_t s = (cudaStream_t)stream;
     if (engine == 1) return (int)cudaMemcpyAsync(dst, src, (size_t)bytes, cudaMemcpyDeviceToDevice, s);
