@@ -1446,14 +1446,18 @@ def main():
     achieved = alg[dom] / t_k[dom] / 1e9
     traffic = read_traffic().get(f"{dom}_tp{world}_m{M}")
 
+    # bus GB/s of the layer's all-reduce (nccl-tests convention, 2 (n - 1) / n x message bytes / time): the one-shot
+    # all-reduce of the down projection's [M, 5120] bf16 message, timed alone in a captured graph of NL calls; the
+    # same bytes over the whole layer's time beside it
     S = 2 * M * HIDDEN
-    bus = (2.0 * (world - 1) / world * S / t_layer / 1e9) if world > 1 else 0.0
+    bus = (2.0 * (world - 1) / world * S / t_ll / 1e9) if t_ll else 0.0
+    bus_layer = (2.0 * (world - 1) / world * S / t_layer / 1e9) if world > 1 else 0.0
     clocks = clk.summary()
     line = {
         "metric": METRIC, "value": layer_ops(M, world) / t_layer / 1e12, "unit": "TOPS", "n_gpus": world,
         "steps": K, "warmup": W, "ms_per_step": t_step * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "us_per_layer": t_layer * 1e6, "bus_gbs": bus,
+        "us_per_layer": t_layer * 1e6, "bus_gbs": bus, "bus_gbs_over_layer": bus_layer,
         "config": {"workload": f"decode W8A8 MLP stack of {NL} layers, M={M}: gate_up 5120->34816 column-parallel "
                                f"with SiLU*up + int8 quant ({'one kernel' if args.mlp == 'fused' else 'two ops'}), "
                                f"down 17408->5120 row-parallel fused with TP all-reduce + RMSNorm + int8 quant "
