@@ -457,7 +457,7 @@ def run_prefill(args, world, rank, local, dev, gloo):
 
     def fused(st):   # one call: GEMM with the reduce-scatter in its epilogue, then reduce + all-gather + row epilogue
         comm.row_linear(st["a"], st["w"], st["sa"], st["sw"], residual=st["res"], norm_w=st["nw"], eps=1e-6,
-                        q=st["q"], scales=st["s"])
+                        q=st["q"], scales=st["s"], route="fused")
 
     STEP = (fused,) if args.tail == "fused" else (gemm, allreduce, norm)
 

@@ -8,6 +8,7 @@ torch.multiprocessing.spawn, a gloo group for set-up, tests/test_hostar.py:13-20
     on every rank, within the W8A16 tolerance of the oracle;
   - the fused GEMV + all-reduce + residual + RMSNorm + quant at BASELINE config 0 (M=16, K_local=8704, N=5120) and
     config 2 (M in {1, 5}, K = 17408 / world): reduced sum bit-exact, residual bit-exact, int8 within 1 LSB;
+  - the prefill row-linear on both routes (the fused tail, and the GEMM -> two-shot -> norm chain), the same bar;
   - 64 back-to-back calls without host syncs, and a captured CUDA graph of mixed calls replayed with fresh inputs
     (tests/test_hostar.py:33-54).
 Skipped with fewer than 2 GPUs."""
@@ -232,32 +233,37 @@ def _worker(rank, world, port, q):
 
         # ---- fused prefill row-linear (M > 32): the GEMM epilogue scatters tiles to their owner ranks, the owners
         # reduce in rank order and every rank pulls the reduced rows and runs the residual + RMSNorm + quant ----
+        # both routes of the prefill row-linear: the fused tail and the three-kernel chain (the default route at
+        # comm.PREFILL_CHAIN_WORLD ranks or more), against one oracle result per shape
         for (M, N, K) in ((256 * world, 5120, 512), (128 * world, 2048, 1040)):
             lis = [make_layer_inputs(M, N, K, seed=40 + M + N, rank=r) for r in range(world)]
             me = lis[rank]
-            res = me.residual.to(dev)
-            red = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
             a_d, w_d, sa_d, sw_d, nw_d = me.a.to(dev), me.w.to(dev), me.sa.to(dev), me.sw.to(dev), me.norm_w.to(dev)
-            qd, sd = comm.row_linear(a_d, w_d, sa_d, sw_d, residual=res, norm_w=nw_d, eps=1e-6, reduced=red)
-            # ten more calls back to back on fresh residual copies: identical results, no host sync between them
-            more = []
-            for _ in range(10):
-                r2 = me.residual.to(dev)
-                more.append((r2,) + tuple(comm.row_linear(a_d, w_d, sa_d, sw_d, residual=r2, norm_w=nw_d, eps=1e-6)))
-            torch.cuda.synchronize()
             ro, qo, so, redo = O.row_linear_tp_big([li.a.numpy() for li in lis], [li.w.numpy() for li in lis],
                                                    [li.sa.numpy() for li in lis], [li.sw.numpy() for li in lis],
                                                    O.to_bits(me.residual), O.to_bits(me.norm_w), 1e-6, 1)
-            check(np.array_equal(O.to_bits(red.cpu()), redo), f"prefill fused reduced M={M} N={N}")
-            check(np.array_equal(O.to_bits(res.cpu()), ro), f"prefill fused residual M={M} N={N}")
-            d = np.abs(qd.cpu().numpy().astype(np.int32) - qo.astype(np.int32))
-            check(d.max() <= 1, f"prefill fused q M={M} off by {d.max()}")
-            for i, (r2, q2, s2) in enumerate(more):
-                check(torch.equal(r2, res) and torch.equal(q2, qd) and torch.equal(s2, sd),
-                      f"prefill fused call {i + 1} differs from call 0 (M={M})")
-            q0 = qd.clone().cpu()
-            dist.broadcast(q0, src=0)
-            check(torch.equal(q0, qd.cpu()), f"prefill fused q differs from rank 0 (M={M})")
+            for route in ("fused", "chain"):
+                res = me.residual.to(dev)
+                red = torch.empty(M, N, dtype=torch.bfloat16, device=dev)
+                qd, sd = comm.row_linear(a_d, w_d, sa_d, sw_d, residual=res, norm_w=nw_d, eps=1e-6, reduced=red,
+                                         route=route)
+                # ten more calls back to back on fresh residual copies: identical results, no host sync between them
+                more = []
+                for _ in range(10):
+                    r2 = me.residual.to(dev)
+                    more.append((r2,) + tuple(comm.row_linear(a_d, w_d, sa_d, sw_d, residual=r2, norm_w=nw_d,
+                                                              eps=1e-6, route=route)))
+                torch.cuda.synchronize()
+                check(np.array_equal(O.to_bits(red.cpu()), redo), f"prefill {route} reduced M={M} N={N}")
+                check(np.array_equal(O.to_bits(res.cpu()), ro), f"prefill {route} residual M={M} N={N}")
+                d = np.abs(qd.cpu().numpy().astype(np.int32) - qo.astype(np.int32))
+                check(d.max() <= 1, f"prefill {route} q M={M} off by {d.max()}")
+                for i, (r2, q2, s2) in enumerate(more):
+                    check(torch.equal(r2, res) and torch.equal(q2, qd) and torch.equal(s2, sd),
+                          f"prefill {route} call {i + 1} differs from call 0 (M={M})")
+                q0 = qd.clone().cpu()
+                dist.broadcast(q0, src=0)
+                check(torch.equal(q0, qd.cpu()), f"prefill {route} q differs from rank 0 (M={M})")
 
         # ---- fused row-linear captured in a CUDA graph (three chained calls), replayed with fresh inputs ----
         M, N, K = 5, 5120, 17408 // world

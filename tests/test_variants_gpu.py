@@ -10,7 +10,9 @@ process against the oracle (int32 accumulators and the fused layer's reduced sum
     launch wait (VLLM_TURING_L2_PREFETCH_KB, off by default);
   - the prefill GEMM on 128 x 256 tiles instead of 256 x 256 (VLLM_TURING_PREFILL_WIDE=0), its last round as whole
     256 x 256 tiles instead of 128-row halves (VLLM_TURING_PREFILL_SPLIT=0), and the fused prefill
-    tail's reduce-scatter stores staged through shared memory at one rank too (VLLM_TURING_PF_STAGE=2)."""
+    tail's reduce-scatter stores staged through shared memory at one rank too (VLLM_TURING_PF_STAGE=2);
+  - the prefill row-linear's three-kernel chain (GEMM, all-reduce, norm + quant), the default route from four ranks
+    up, taken at one rank (VLLM_TURING_PREFILL_CHAIN_WORLD=1)."""
 import os
 import subprocess
 import sys
@@ -104,10 +106,11 @@ def child():
                                  {"VLLM_TURING_PDL": "0"}, {"VLLM_TURING_L2_PREFETCH_KB": "256"},
                                  {"VLLM_TURING_PREFILL_WIDE": "0"}, {"VLLM_TURING_PF_STAGE": "2"},
                                  {"VLLM_TURING_PF_STAGE": "2", "VLLM_TURING_PREFILL_WIDE": "0"},
-                                 {"VLLM_TURING_PREFILL_SPLIT": "0"}],
+                                 {"VLLM_TURING_PREFILL_SPLIT": "0"}, {"VLLM_TURING_PREFILL_CHAIN_WORLD": "1"}],
                          ids=["fused_gemv", "kbs1", "kbs2", "rows_tail", "rows_tail_ctas4", "gemv_row_ctas3", "no_pdl",
                               "l2_prefetch",
-                              "prefill_128x256", "pf_staged", "pf_staged_128x256", "prefill_no_split"])
+                              "prefill_128x256", "pf_staged", "pf_staged_128x256", "prefill_no_split",
+                              "prefill_chain"])
 def test_variant_in_child(env):
     e = dict(os.environ, **env)
     r = subprocess.run([sys.executable, "-c", "import tests.test_variants_gpu as t; t.child()"], cwd=ROOT, env=e,

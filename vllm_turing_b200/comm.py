@@ -19,6 +19,11 @@ from . import _build
 
 LL_BYTES = int(os.environ.get("VLLM_TURING_LL_KB", "512")) << 10
 BIG_BYTES = int(float(os.environ.get("VLLM_TURING_CE_AR_MB", "64")) * (1 << 20))
+# Prefill row-linear (M > 32) at this many ranks or more runs as the three-kernel chain (this rank's GEMM, the two-shot
+# all-reduce in place, the residual + RMSNorm + quant kernel) instead of the fused prefill tail. Measured on B200 at
+# M = 8192, N = 5120, K = 17408 / TP: at 2 ranks the fused tail takes 447 us against ~537 us for the chain; at 4 ranks
+# the chain's kernels take 479 us (184 + 240 + 55) against the fused tail's 518 us.
+PREFILL_CHAIN_WORLD = int(os.environ.get("VLLM_TURING_PREFILL_CHAIN_WORLD", "4"))
 
 
 class CommError(RuntimeError):
@@ -202,9 +207,13 @@ class TPComm:
             raise CommError(f"vt_all_gather_rows failed: {rc}")
         return gathered
 
-    def row_linear(self, a, w, sa, sw, residual=None, norm_w=None, eps=1e-6, q=None, scales=None, reduced=None):
+    def row_linear(self, a, w, sa, sw, residual=None, norm_w=None, eps=1e-6, q=None, scales=None, reduced=None,
+                   route="auto"):
         """The fused row-parallel tail. With residual: residual += all_reduce(a.w^T * sa * sw) in place and returns
-        (q, scales) of RMSNorm(residual) * norm_w; without: returns the all-reduced [M, N] (reduced)."""
+        (q, scales) of RMSNorm(residual) * norm_w; without: returns the all-reduced [M, N] (reduced).
+        route, for prefill (M > 32): "auto" takes the three-kernel chain at PREFILL_CHAIN_WORLD ranks or more and the
+        fused prefill tail below; "fused" / "chain" force one (the chain needs the prefill GEMM's shapes, else the
+        fused tail runs)."""
         M, K = a.shape
         N = w.shape[0]
         dt = residual.dtype if residual is not None else (reduced.dtype if reduced is not None else torch.bfloat16)
@@ -213,6 +222,13 @@ class TPComm:
             scales = scales if scales is not None else torch.empty(M, 1, dtype=torch.float32, device=a.device)
         elif reduced is None:
             reduced = torch.empty(M, N, dtype=dt, device=a.device)
+        if route not in ("auto", "fused", "chain"):
+            raise ValueError(f"row_linear: unknown route {route!r}")
+        if M > 32 and (route == "chain" or (route == "auto" and self.world >= PREFILL_CHAIN_WORLD)):
+            from . import w8a8
+            part = reduced if reduced is not None else torch.empty(M, N, dtype=dt, device=a.device)
+            if w8a8.big_ok(part, a, w.t(), sa, sw, None):
+                return self._row_linear_chain(part, a, w, sa, sw, residual, norm_w, eps, q, scales)
         rc = self.L.vt_tp_row_linear(self.handle, a.data_ptr(), w.data_ptr(), sa.data_ptr(), sw.data_ptr(),
                                      residual.data_ptr() if residual is not None else None,
                                      norm_w.data_ptr() if norm_w is not None else None, float(eps),
@@ -223,6 +239,19 @@ class TPComm:
         if rc != 0:
             raise CommError(f"vt_tp_row_linear failed: {rc}")
         return (q, scales) if residual is not None else reduced
+
+    def _row_linear_chain(self, part, a, w, sa, sw, residual, norm_w, eps, q, scales):
+        """The prefill row-linear as three launches: the int8 GEMM into part (bf16 / fp16 partial of this rank's K
+        slice), the all-reduce of part in place (float32 sum in rank order, one rounding: the fused tail's reduced
+        values), then residual += part and the RMSNorm + per-token int8 quant."""
+        from . import w8a8
+        from .quantfuse import rms_norm_dynamic_per_token_quant
+        w8a8.big(part, a, w.t(), sa, sw)
+        self.all_reduce(part, out=part)
+        if residual is None:
+            return part
+        rms_norm_dynamic_per_token_quant(part, norm_w, eps, residual, q=q, s=scales)
+        return q, scales
 
 
 class _nullctx:

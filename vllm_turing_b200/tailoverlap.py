@@ -10,7 +10,8 @@ How it runs here (a plan per layer, resolved at the first call, when the checkpo
     quant(attn) -> TPComm.row_linear(o_proj, residual, norm)    one fused row-linear: GEMM + all-reduce + residual add
                                                                  + RMSNorm + int8 quant (decode: one kernel, prefill:
                                                                  GEMM with the reduce-scatter in its epilogue + reduce
-                                                                 / all-gather / norm kernel)
+                                                                 / all-gather / norm kernel; from four ranks up the
+                                                                 GEMM -> two-shot -> norm chain, measured faster there)
     -> scaled_mm(gate_up) -> silu_mul_quant -> TPComm.row_linear(down_proj)   GEMM + all-reduce, no norm
   The overlap of communication with the GEMMs happens inside those kernels, tile by tile, so no chunking is needed.
 * staged (anything else, or a token count the fused kernels do not take): the model's own modules, with each
