@@ -1109,7 +1109,8 @@ def run_stack(args, world, rank, local, dev, gloo):
     step()   # eager warm-up: kernel attributes, workspaces
     barrier()
     comm.check()
-    # parity self-check (untimed) on layer 0's o_proj tail: the fused call and the unfused chain from the same inputs
+    # parity self-check (untimed) on layer 0's o_proj tail: the public call (TPComm.row_linear, whichever route it
+    # takes) and the unfused chain from the same inputs, both against a torch float32 restatement
     from vllm_turing_b200.quantfuse import rms_norm_dynamic_per_token_quant  # noqa: F811
     s0 = layers[0]
     a_q, a_s = scaled_int8_quant_cuda(qkv_out[:, :k_o].contiguous())
